@@ -1,0 +1,481 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a int8 weight-only linear (one JSON line on rank 0).
+
+Metric: int8 linear HBM GB/s (M<=64) & TFLOP/s (prefill) vs roofline;
+decode tok/s.
+
+Workload (`config.workload`): config 2, the decode sweep: M in {1, 4, 16, 64} x the four
+Llama-3-8B projection shapes (K, N) = (4096, 6144) QKV, (4096, 4096) O, (4096, 28672)
+gate_up, (14336, 4096) down.  One step = the int8 projections of one Llama-3-8B decode
+iteration (32 layers x 4 projections, each layer with its own weights: 6.98 GB of int8, far
+larger than L2) for each of the four M: 512 launches, captured once in a CUDA graph (the
+reference engine replays decode iterations as CUDA graphs, decode_graph.py:87-140) and
+replayed.  `value` = algorithmic bytes (N*K + 4N + 2MK + 2MN per launch) / device time.
+
+Extra keys: `prefill` (config 3 sweep, TFLOP/s against the bf16 dense peak), `points`
+(per-shape breakdown), `roofline` for the dominant kernel, `cpu_baseline` (the reference's
+CPU path on the host cores), `e2e` (pinned host inputs copied in, graph replay, outputs
+copied back, every step), `clocks` (nvidia-smi sampled during the timed region).
+
+`--impl reference` times the reference's own CPU implementation of the path (the CPU
+nn.Linear of `_forward_hf`, float32, on the dequantized weights; the reference has no int8
+kernel) on a bounded sample of the same workload with all host threads.
+
+Multi-GPU (`torchrun --nproc-per-node N bench.py --gpus N`): every rank holds its own
+column stripe of an N-times-wider layer stack (the same per-rank shapes), no collective in
+the data path; value = bytes all ranks processed / max over ranks of the device time
+(weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from llm_serving_engine_b200.inputs import DECODE_M, LLAMA3_8B_SHAPES, PREFILL_M, linear_bytes, linear_flops  # noqa: E402
+
+METRIC = "int8 linear HBM GB/s (M<=64) & TFLOP/s (prefill) vs roofline; decode tok/s"
+UNIT = "GB/s"
+N_LAYERS = 32
+SHAPE_ORDER = ("qkv", "o", "gate_up", "down")
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU sample length")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# --------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# --------------------------------------------------------------------------------------
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(val: float, world: int) -> float:
+    if world == 1:
+        return val
+    import torch.distributed as dist
+
+    t = torch.tensor([val], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def make_weights(layers: int, device, seed: int):
+    """Per layer, per shape: int8 W uniform on [-127, 127] and fp32 s uniform [1e-4, 5e-4],
+    drawn on the device from a seeded generator (7 GB would take minutes on the host)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(layers):
+        d = {}
+        for name in SHAPE_ORDER:
+            K, N = LLAMA3_8B_SHAPES[name]
+            w = torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int8)
+            s = torch.empty(N, device=device).uniform_(1e-4, 5e-4, generator=g)
+            d[name] = (w, s)
+        out.append(d)
+    return out
+
+
+def decode_step_fn(weights, xs, ys, int8_linear):
+    def step():
+        for M in DECODE_M:
+            for layer in weights:
+                for name in SHAPE_ORDER:
+                    w, s = layer[name]
+                    int8_linear(xs[(M, name)], w, s, out=ys[(M, name)])
+    return step
+
+
+def capture(fn, warm_stream):
+    warm_stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(warm_stream):
+        fn()
+    torch.cuda.current_stream().wait_stream(warm_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=warm_stream):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, reps: int) -> float:
+    """Average ms per replay, CUDA events on the replay stream, synchronized both sides."""
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+# --------------------------------------------------------------------------------------
+def cpu_reference_sample(seconds: float):
+    """The reference's CPU path (float32 nn.Linear on the dequantized weight, all host
+    threads) over one layer of the decode sweep, repeated for ~`seconds`."""
+    from llm_serving_engine_b200.inputs import make_inputs
+    from oracle.cpu_path import ReferenceCpuLinear, cpu_model, host_threads
+
+    threads = host_threads()
+    mods, xs, nbytes = {}, {}, 0
+    for name in SHAPE_ORDER:
+        K, N = LLAMA3_8B_SHAPES[name]
+        x, w, s = make_inputs(max(DECODE_M), K, N, seed=0)
+        mods[name] = ReferenceCpuLinear(w, s)
+        for M in DECODE_M:
+            xs[(M, name)] = x[:M].float().contiguous()
+            nbytes += linear_bytes(M, K, N)
+    for M in DECODE_M:  # warm-up pass
+        for name in SHAPE_ORDER:
+            mods[name](xs[(M, name)])
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        for M in DECODE_M:
+            for name in SHAPE_ORDER:
+                mods[name](xs[(M, name)])
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or passes >= 1000:
+            break
+    gbs = nbytes * passes / el / 1e9
+    return {
+        "value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
+        "sample": f"{passes} passes of the 16 decode-sweep points (1 layer of weights), float32 torch "
+                  f"F.linear on dequantized weights, {el:.1f} s, CPU {cpu_model()}",
+    }, el / passes
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from llm_serving_engine_b200.inputs import make_inputs
+    from oracle.cpu_path import ReferenceCpuLinear, cpu_model, host_threads
+
+    threads = host_threads()
+    mods, xs, nbytes = {}, {}, 0
+    for name in SHAPE_ORDER:
+        K, N = LLAMA3_8B_SHAPES[name]
+        x, w, s = make_inputs(max(DECODE_M), K, N, seed=0)
+        mods[name] = ReferenceCpuLinear(w, s)
+        for M in DECODE_M:
+            xs[(M, name)] = x[:M].float().contiguous()
+            nbytes += linear_bytes(M, K, N)
+
+    def step():
+        for M in DECODE_M:
+            for name in SHAPE_ORDER:
+                mods[name](xs[(M, name)])
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = nbytes * args.steps / el / 1e9
+    sample = (f"each step: the 16 decode-sweep points over 1 layer of weights (the GPU arm's step runs "
+              f"32 layers), float32 torch F.linear on dequantized weights (the reference's CPU nn.Linear "
+              f"path; it has no int8 kernel), CPU {cpu_model()}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 decode sweep (M in 1,4,16,64 x Llama-3-8B qkv/o/gate_up/down), 1-layer sample on CPU"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    world, rank, local = setup_dist(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    from llm_serving_engine_b200 import ops
+
+    hbm_peak, bf16_peak, bf16_sustained, peak_src = peaks()
+    layers = args.layers
+    weights = make_weights(layers, dev, seed=1000 + rank)
+    gx = torch.Generator(device=dev).manual_seed(7 + rank)
+    xs, ys = {}, {}
+    for M in DECODE_M:
+        for name in SHAPE_ORDER:
+            K, N = LLAMA3_8B_SHAPES[name]
+            xs[(M, name)] = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
+            ys[(M, name)] = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    step_bytes = sum(linear_bytes(M, *LLAMA3_8B_SHAPES[n]) for M in DECODE_M for n in SHAPE_ORDER) * layers
+    launches_per_step = len(DECODE_M) * len(SHAPE_ORDER) * layers
+
+    warm = torch.cuda.Stream(device=dev)
+    step = decode_step_fn(weights, xs, ys, ops.int8_linear)
+    graph = capture(step, warm)
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    value = step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+    ms_per_step = ms_max / args.steps
+
+    # ---- per-point breakdown: one graph per (M, shape) over all layers -----------------
+    points = []
+    tc_bytes = tc_ms = 0.0
+    gemv_bytes = gemv_ms = 0.0
+    for M in DECODE_M:
+        for name in SHAPE_ORDER:
+            K, N = LLAMA3_8B_SHAPES[name]
+
+            def one(M=M, name=name):
+                for layer in weights:
+                    w, s = layer[name]
+                    ops.int8_linear(xs[(M, name)], w, s, out=ys[(M, name)])
+            g1 = capture(one, warm)
+            time_graph(g1, 2)
+            per_launch_ms = time_graph(g1, 10) / layers
+            b = linear_bytes(M, K, N)
+            algo = "gemv" if M <= 2 else "tcgen05"
+            if algo == "tcgen05":
+                tc_bytes += b
+                tc_ms += per_launch_ms
+            else:
+                gemv_bytes += b
+                gemv_ms += per_launch_ms
+            points.append({"M": M, "shape": name, "K": K, "N": N, "us": round(per_launch_ms * 1e3, 3),
+                           "GBps": round(b / per_launch_ms / 1e6, 1), "kernel": algo})
+            del g1
+    dominant_is_tc = tc_ms >= gemv_ms
+    dom_bytes, dom_ms = (tc_bytes, tc_ms) if dominant_is_tc else (gemv_bytes, gemv_ms)
+    achieved = dom_bytes / dom_ms / 1e6
+    traffic_info = committed_traffic().get("decode_tcgen05" if dominant_is_tc else "decode_gemv")
+    roofline = {
+        "kernel": "tc_gemm_i8_kernel (tcgen05, decode M=4..64)" if dominant_is_tc else "gemv_i8_kernel (M<=2)",
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+        "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback",
+        "traffic": traffic_info.get("dram_bytes_per_launch") if traffic_info else None,
+        "algorithmic_bytes_per_launch": round(dom_bytes / (12 if dominant_is_tc else 4)),
+        "frac_of_8TBps": round(achieved / 8000.0, 4),
+    }
+
+    # ---- prefill (config 3) ------------------------------------------------------------
+    prefill = None
+    if not args.no_prefill:
+        pre_pts, fl_tot, ms_tot = [], 0.0, 0.0
+        layer0 = weights[0]
+        for M in PREFILL_M:
+            for name in SHAPE_ORDER:
+                K, N = LLAMA3_8B_SHAPES[name]
+                xp = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
+                yp = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                w, s = layer0[name]
+
+                def one(xp=xp, yp=yp, w=w, s=s):
+                    ops.int8_linear(xp, w, s, out=yp)
+                g1 = capture(one, warm)
+                time_graph(g1, 2)
+                t = time_graph(g1, 10)
+                fl = linear_flops(M, K, N)
+                fl_tot += fl
+                ms_tot += t
+                pre_pts.append({"M": M, "shape": name, "us": round(t * 1e3, 2), "TFLOPs": round(fl / t / 1e9, 1)})
+                del g1, xp, yp
+        tf = fl_tot / ms_tot / 1e9
+        prefill = {"value": round(tf, 1), "unit": "TFLOP/s", "workload": "config3: M in 512,2048,8192 x 4 shapes",
+                   "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                                "frac": round(tf / bf16_peak, 4), "frac_of_2250": round(tf / 2250.0, 4),
+                                "peak_source": peak_src + " bf16_tflops (burst)"},
+                   "points": pre_pts}
+
+    # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
+    host_x = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    host_y = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host_x.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_y.values())
+    e2e_steps = max(1, min(args.steps, 50))
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for k, v in host_x.items():
+            xs[k].copy_(v, non_blocking=True)
+        graph.replay()
+        for k, v in ys.items():
+            host_y[k].copy_(v, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s, world)
+    e2e_val = step_bytes * e2e_steps * world / e2e_s / 1e9
+
+    cpu_base = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu_base, _ = cpu_reference_sample(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 x int8 (fp32 accumulate)",
+            "data": "synthetic (seeded: x~N(0,1) bf16, W uniform int8 [-127,127], s uniform [1e-4,5e-4])",
+            "config": {
+                "workload": "config2 decode sweep: M in 1,4,16,64 x Llama-3-8B (K,N) qkv 4096x6144, o 4096x4096, "
+                            "gate_up 4096x28672, down 14336x4096",
+                "layers": layers, "launches_per_step": launches_per_step,
+                "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (6.98 GB of distinct int8 weights per M pass)",
+                "graph": "one CUDA graph per step (decode-graph replay)",
+                "parallelism": f"column stripes x{world}, no collective" if world > 1 else "single GPU",
+            },
+            "roofline": roofline,
+            "gpu_launches": launches_per_step * args.steps,
+            "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "how": "pinned host x -> device, graph replay, y -> pinned host, sync; wall clock"},
+            "clocks": clk.summary(),
+            "points": points,
+        }
+        if prefill:
+            line["prefill"] = prefill
+        if cpu_base:
+            line["cpu_baseline"] = cpu_base
+        print(json.dumps(line), flush=True)
+
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,126 @@
+/*
+ * lse_int8.h -- C ABI of the B200 (sm_100a) int8 weight-only linear for
+ * vladimirfilip/llm-serving-engine.
+ *
+ * The reference engine calls each projection as a torch.nn.Linear module
+ * (src/llm_serving_engine/model/model_runner.py:322-324 q/k/v, :369 and :418 o_proj,
+ * :223 the MLP; src/llm_serving_engine/model/piecewise_graph.py:163-166) with
+ * y = x W^T, W [out_features, in_features], no bias, and raises NotImplementedError for
+ * ModelConfig.quantize == "int8" (model_runner.py:45-46; config.py:32,46).  This library
+ * is what that `quantize="int8"` switch binds to: each entry point below replaces one
+ * piece of the nn.Linear call the engine makes.
+ *
+ * Conventions (all entry points):
+ *   - Plain pointers to device memory, sizes in elements, row strides in elements.
+ *   - `stream` is a cudaStream_t passed as void*; every launch goes to that stream, no
+ *     entry point synchronizes, allocates device memory, or changes device settings, so
+ *     each one can be captured in a CUDA graph (after lse_init on that device).
+ *   - Return value is an lse_status; nonzero means nothing was launched (argument errors)
+ *     or the launch failed (LSE_ERR_CUDA).  The library never aborts or traps.
+ *   - The caller owns every buffer.
+ */
+#ifndef LSE_INT8_H
+#define LSE_INT8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum lse_status {
+    LSE_OK = 0,
+    LSE_ERR_INVALID_ARG = 1,   /* null pointer, negative size, ld < K, ... */
+    LSE_ERR_ALIGNMENT = 2,     /* K % 16, ldx % 8, ldy % 8 or a pointer not 16-byte aligned */
+    LSE_ERR_UNSUPPORTED = 3,   /* shape/algo combination this build does not run */
+    LSE_ERR_WORKSPACE = 4,     /* workspace missing or smaller than lse_int8_linear_workspace() */
+    LSE_ERR_CUDA = 5,          /* a CUDA runtime/driver call failed (see lse_last_cuda_error) */
+    LSE_ERR_DEVICE_TIMEOUT = 6 /* a device-side wait ran out (reported by lse_device_status) */
+} lse_status;
+
+/* Kernel selection for lse_int8_linear_ex. */
+typedef enum lse_algo {
+    LSE_ALGO_AUTO = 0,     /* pick by M: CUDA-core GEMV for tiny M, tcgen05 GEMM otherwise */
+    LSE_ALGO_GEMV = 1,     /* CUDA-core GEMV, 128-bit int8 streams, warp-shuffle reduction */
+    LSE_ALGO_TCGEN05 = 2   /* tcgen05/TMEM tensor-core GEMM fed by TMA (stream-K over tiles) */
+} lse_algo;
+
+/* Weight dtypes accepted by lse_int8_quantize. */
+typedef enum lse_dtype { LSE_BF16 = 0, LSE_F16 = 1, LSE_F32 = 2 } lse_dtype;
+
+/*
+ * One-time per-device set-up (SM count, kernel attributes, driver entry points).  Optional:
+ * the first call of any entry point on a device does it; call it explicitly before a CUDA
+ * graph capture so that capture records only kernel launches.
+ */
+int lse_init(int device);
+
+/*
+ * y[m, n] = bf16( s[n] * sum_k x[m, k] * w[n, k] )       m < M, n < N
+ *
+ * Replaces nn.Linear.forward at the call sites above (model_runner.py:322-324,369,418,223).
+ *   x      bf16 [M, K], row stride ldx (>= K, multiple of 8), 16-byte aligned
+ *   w      int8 [N, K] row-major (nn.Linear [out, in] layout), K % 16 == 0, 16-byte aligned
+ *   scale  fp32 [N] per-output-channel scale
+ *   y      bf16 [M, N], row stride ldy (>= N, multiple of 8 unless M == 1), 16-byte aligned
+ *   workspace  device scratch of at least lse_int8_linear_workspace(M, K, N) bytes,
+ *              16-byte aligned; its first LSE_WS_COUNTER_BYTES bytes must be zero before the
+ *              first call, and every successful call leaves them zero again.
+ * M == 0 or N == 0 is a no-op returning LSE_OK.  K == 0 writes zeros.
+ * Calls that share one workspace must be ordered on the GPU (same stream, or events).
+ */
+int lse_int8_linear(const void *x, int64_t M, int64_t K, int64_t ldx,
+                    const int8_t *w, const float *scale, int64_t N,
+                    void *y, int64_t ldy,
+                    void *workspace, size_t workspace_bytes,
+                    void *stream);
+
+/* Same as lse_int8_linear with an explicit kernel choice (lse_algo). */
+int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx,
+                       const int8_t *w, const float *scale, int64_t N,
+                       void *y, int64_t ldy,
+                       void *workspace, size_t workspace_bytes,
+                       int algo, void *stream);
+
+/* Bytes of the counter region at the start of every workspace (must start zeroed). */
+#define LSE_WS_COUNTER_BYTES 65536
+
+/* Workspace bytes lse_int8_linear needs for this shape (auto algo); always >= the
+ * counter region. */
+size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N);
+
+/*
+ * Symmetric per-output-channel quantization at load time (the build's replacement for the
+ * reference's raise at model_runner.py:45-46):
+ *   s[n] = max_k |w[n,k]| / 127   (1.0 for an all-zero row)
+ *   q[n,k] = clamp(rint(w[n,k] / s[n]), -127, 127)      (fp32 arithmetic, half-to-even)
+ *   w      [N, K] in `dtype` (lse_dtype), row stride ldw elements, any alignment
+ *   q_out  int8 [N, K] row-major;  s_out fp32 [N]
+ */
+int lse_int8_quantize(const void *w, int dtype, int64_t N, int64_t K, int64_t ldw,
+                      int8_t *q_out, float *s_out, void *stream);
+
+/* Human-readable name of a status code (static string). */
+const char *lse_status_string(int status);
+
+/* Text of the last CUDA error this thread saw inside the library ("" if none). */
+const char *lse_last_cuda_error(void);
+
+/*
+ * Device-side status of `device`: LSE_OK, or LSE_ERR_DEVICE_TIMEOUT when a bounded
+ * wait inside a kernel gave up since the last reset.  Synchronizes the device.  When
+ * `reset` is nonzero the flag is cleared.  After a timeout the workspace counter region
+ * must be zeroed again before the next call.
+ */
+int lse_device_status(int device, int reset);
+
+/* Library ABI version (LSE_ABI_VERSION). */
+#define LSE_ABI_VERSION 1
+int lse_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSE_INT8_H */

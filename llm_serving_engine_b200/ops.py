@@ -1,0 +1,159 @@
+"""Torch-facing int8 linear ops over the C ABI (liblse_int8.so).
+
+`int8_linear(x, weight, scale)` is the call every int8 projection makes: the replacement
+for `torch.nn.Linear.__call__` at the reference's call sites
+(`src/llm_serving_engine/model/model_runner.py:322-324`, `:369`, `:418`, `:223`;
+`src/llm_serving_engine/model/piecewise_graph.py:163-166`).  Shapes, dtypes and devices are
+validated on the host and raise `ValueError` / `RuntimeError` before anything launches, the
+way the reference surfaces load-time refusals (`model_runner.py:77-94`).
+
+Graph capture: the op launches on `torch.cuda.current_stream()`, never synchronizes and
+never allocates outside the torch caching allocator (the output), so the reference's decode
+and piecewise CUDA-graph captures (`decode_graph.py:87-116`, `piecewise_graph.py:71-109`)
+record it like any other kernel.  The one piece of state is a per-(device, stream) workspace,
+created zeroed on first use; creating it inside a capture is refused, and the engine's
+warm-up iterations on the capture stream create it before the capture starts.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "int8_linear",
+    "quantize_per_channel",
+    "workspace_for",
+    "device_status",
+    "ALGO_AUTO",
+    "ALGO_GEMV",
+    "ALGO_TCGEN05",
+]
+
+ALGO_AUTO = _lib.ALGO_AUTO
+ALGO_GEMV = _lib.ALGO_GEMV
+ALGO_TCGEN05 = _lib.ALGO_TCGEN05
+
+_DTYPE_CODES = {torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16, torch.float32: _lib.DT_F32}
+
+# One workspace per (device, stream): calls on one stream are ordered, calls on different
+# streams never share scratch.  Sized for the largest token tile, so it never grows.
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_ws_lock = threading.Lock()
+_inited: set[int] = set()
+
+
+def _ensure_device(device: torch.device) -> None:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _inited:
+        _lib.check(_lib.load().lse_init(idx), f"lse_init(cuda:{idx})")
+        _inited.add(idx)
+
+
+def workspace_for(device: torch.device, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """The zero-initialised scratch buffer calls on (device, stream) share."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    stream = stream if stream is not None else torch.cuda.current_stream(idx)
+    key = (idx, stream.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        with _ws_lock:
+            ws = _workspaces.get(key)
+            if ws is None:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError(
+                        "int8_linear: first call on this stream happened inside a CUDA graph capture; "
+                        "run one eager call on the capture stream first (the engine's warm-up does)")
+                nbytes = int(_lib.load().lse_int8_linear_workspace(1 << 20, 1, 1))
+                ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+                _workspaces[key] = ws
+    return ws
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                out: torch.Tensor | None = None, algo: int = ALGO_AUTO) -> torch.Tensor:
+    """y = bf16(x @ (weight * scale[:, None]).T): x bf16 [..., K] on CUDA, weight int8 [N, K]
+    contiguous, scale fp32 [N].  Returns bf16 [..., N] (or writes `out`, a [..., N] bf16
+    tensor whose last dim is contiguous)."""
+    if not (x.is_cuda and weight.is_cuda and scale.is_cuda):
+        raise RuntimeError("int8_linear runs on CUDA only (no CPU fallback)")
+    if x.device != weight.device or x.device != scale.device:
+        raise ValueError(f"int8_linear: tensors on different devices ({x.device}, {weight.device}, {scale.device})")
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"int8_linear: x must be bfloat16, got {x.dtype}")
+    if weight.dtype != torch.int8 or weight.dim() != 2:
+        raise ValueError(f"int8_linear: weight must be int8 [N, K], got {weight.dtype} {tuple(weight.shape)}")
+    if scale.dtype != torch.float32 or scale.shape != (weight.shape[0],):
+        raise ValueError(f"int8_linear: scale must be float32 [{weight.shape[0]}], got {scale.dtype} {tuple(scale.shape)}")
+    N, K = weight.shape
+    if x.shape[-1] != K:
+        raise ValueError(f"int8_linear: x last dim {x.shape[-1]} != in_features {K}")
+    if not weight.is_contiguous():
+        raise ValueError("int8_linear: weight must be contiguous [N, K]")
+    if K % 16 != 0:
+        raise ValueError(f"int8_linear: in_features must be a multiple of 16, got {K}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        y2 = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        y = y2.view(*lead, N)
+    else:
+        if out.dtype != torch.bfloat16 or out.shape != (*lead, N) or out.stride(-1) != 1:
+            raise ValueError("int8_linear: out must be bf16 [..., N] with a contiguous last dim")
+        y = out
+        y2 = out.view(-1, N) if M > 0 else out.reshape(0, N)
+    if M == 0:
+        return y
+    _ensure_device(x.device)
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace_for(x.device, stream)
+    rc = _lib.load().lse_int8_linear_ex(
+        x2.data_ptr(), M, K, x2.stride(0), weight.data_ptr(), scale.data_ptr(), N,
+        y2.data_ptr(), y2.stride(0), ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
+    _lib.check(rc, "lse_int8_linear")
+    return y
+
+
+def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-channel int8 quantization of a CUDA weight [N, K] (bf16, fp16 or
+    fp32): s = max|w[n,:]|/127 (1.0 for an all-zero row), q = clamp(rint(w/s), -127, 127)."""
+    if not w.is_cuda:
+        raise RuntimeError("quantize_per_channel runs on CUDA only (no CPU fallback)")
+    if w.dim() != 2 or w.dtype not in _DTYPE_CODES:
+        raise ValueError(f"quantize_per_channel: need a 2-D bf16/fp16/fp32 weight, got {w.dtype} {tuple(w.shape)}")
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    s = torch.empty((N,), dtype=torch.float32, device=w.device)
+    if N == 0:
+        return q, s
+    _ensure_device(w.device)
+    stream = torch.cuda.current_stream(w.device)
+    rc = _lib.load().lse_int8_quantize(w.data_ptr(), _DTYPE_CODES[w.dtype], N, K, w.stride(0),
+                                       q.data_ptr(), s.data_ptr(), stream.cuda_stream)
+    _lib.check(rc, "lse_int8_quantize")
+    return q, s
+
+
+def device_status(device: int | torch.device | None = None, reset: bool = True) -> int:
+    """Synchronize and read the device-side status (LSE_OK or LSE_ERR_DEVICE_TIMEOUT).  After a
+    timeout the workspaces of that device are re-zeroed."""
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, torch.device):
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    else:
+        idx = int(device)
+    st = int(_lib.load().lse_device_status(idx, 1 if reset else 0))
+    if st == _lib.LSE_ERR_DEVICE_TIMEOUT:
+        for (d, _), ws in _workspaces.items():
+            if d == idx:
+                ws.zero_()
+    return st

@@ -1,0 +1,60 @@
+"""Shared helpers for the GPU tests: drive the C ABI directly (ctypes) on torch-allocated
+device buffers and compare with the CPU oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from llm_serving_engine_b200 import _lib
+from oracle.ref_linear import parity_errors, ref_int8_linear
+
+
+class Workspace:
+    """A zeroed scratch buffer for lse_int8_linear plus a guard band to catch overruns."""
+
+    GUARD = 4096
+
+    def __init__(self, device="cuda"):
+        self.nbytes = int(_lib.load().lse_int8_linear_workspace(1 << 20, 1, 1))
+        self.buf = torch.zeros(self.nbytes + self.GUARD, dtype=torch.uint8, device=device)
+        self.buf[self.nbytes:] = 0xA5
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def counters_clear(self) -> bool:
+        return bool((self.buf[:_lib.WS_COUNTER_BYTES] == 0).all().item())
+
+    def guard_intact(self) -> bool:
+        return bool((self.buf[self.nbytes:] == 0xA5).all().item())
+
+
+def abi_linear(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, ws: Workspace, algo: int = 0,
+               ldx: int | None = None, y: torch.Tensor | None = None, ldy: int | None = None) -> torch.Tensor:
+    """Call lse_int8_linear_ex through ctypes. x: bf16 [M, >=K] (row stride ldx)."""
+    lib = _lib.load()
+    M = x.shape[0]
+    N, K = w.shape
+    ldx = x.stride(0) if ldx is None else ldx
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    ldy = y.stride(0) if ldy is None else ldy
+    rc = lib.lse_int8_linear_ex(x.data_ptr(), M, K, ldx, w.data_ptr(), s.data_ptr(), N, y.data_ptr(), ldy,
+                                ws.ptr, ws.nbytes, algo, torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "lse_int8_linear_ex")
+    return y
+
+
+def oracle_rows(x_cpu: torch.Tensor, w_cpu: torch.Tensor, s_cpu: torch.Tensor, rows) -> np.ndarray:
+    return ref_int8_linear(x_cpu[rows].float().numpy(), w_cpu.numpy(), s_cpu.numpy())
+
+
+def check_parity(y_gpu: torch.Tensor, ref: np.ndarray, what: str = "") -> float:
+    y = y_gpu.float().cpu().numpy()
+    nw, ok, ratio = parity_errors(y, ref)
+    assert np.all(np.isfinite(y)), f"{what}: non-finite output"
+    assert nw <= 1e-2, f"{what}: normwise error {nw:.3e} > 1e-2"
+    assert ok, f"{what}: elementwise criterion violated (worst ratio {ratio:.3f})"
+    return nw

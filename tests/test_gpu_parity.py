@@ -1,0 +1,171 @@
+"""Parity of the sm_100a kernels with the CPU oracle, called through the C ABI.
+
+Tolerance (from the north_star): normwise max|y - ref| / max|ref| <= 1e-2 against the fp64
+dequant-matmul oracle, and elementwise |y - ref| <= 1e-2*|ref| + 1e-3*max|ref|; bf16 output
+rounding alone is ~2e-3 relative.  Full-size shapes are checked on a sample of rows of the
+output (the oracle cost), plus size-independent properties (determinism, linearity in x,
+zero inputs, workspace counters re-armed).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from llm_serving_engine_b200 import _lib, ops
+from llm_serving_engine_b200.inputs import LLAMA3_8B_SHAPES, make_inputs
+from oracle.ref_linear import ref_int8_linear, ref_quantize
+from tests.gpu_helpers import Workspace, abi_linear, check_parity, oracle_rows
+
+pytestmark = pytest.mark.gpu
+
+ALGOS = {"gemv": _lib.ALGO_GEMV, "tcgen05": _lib.ALGO_TCGEN05, "auto": _lib.ALGO_AUTO}
+
+
+@pytest.fixture(scope="module")
+def ws():
+    return Workspace()
+
+
+def _run_case(M, K, N, algo, ws, seed=0, sample=None):
+    x, w, s = make_inputs(M, K, N, seed=seed)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    y = abi_linear(xd, wd, sd, ws, algo=algo)
+    torch.cuda.synchronize()
+    rows = np.arange(M) if sample is None or M <= sample else np.unique(
+        np.concatenate([[0, M - 1], np.random.default_rng(seed).choice(M, sample, replace=False)]))
+    ref = oracle_rows(x, w, s, rows)
+    return check_parity(y[torch.as_tensor(rows, device="cuda")], ref, f"M={M} K={K} N={N} algo={algo}")
+
+
+def test_config1_all_algos(ws):
+    for name, algo in ALGOS.items():
+        _run_case(8, 2048, 2048, algo, ws)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+@pytest.mark.parametrize("shape", list(LLAMA3_8B_SHAPES))
+@pytest.mark.parametrize("M", [1, 4, 16, 64])
+def test_decode_sweep_tcgen05(ws, shape, M):
+    K, N = LLAMA3_8B_SHAPES[shape]
+    _run_case(M, K, N, _lib.ALGO_TCGEN05, ws)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+@pytest.mark.parametrize("shape", list(LLAMA3_8B_SHAPES))
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_decode_sweep_gemv(ws, shape, M):
+    K, N = LLAMA3_8B_SHAPES[shape]
+    _run_case(M, K, N, _lib.ALGO_GEMV, ws)
+
+
+@pytest.mark.parametrize("shape", list(LLAMA3_8B_SHAPES))
+@pytest.mark.parametrize("M", [512, 2048])
+def test_prefill_tcgen05(ws, shape, M):
+    K, N = LLAMA3_8B_SHAPES[shape]
+    _run_case(M, K, N, _lib.ALGO_TCGEN05, ws, sample=24)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (1, 16, 8), (3, 48, 17), (17, 144, 136), (65, 4112, 200), (129, 272, 40), (7, 32, 64),
+    (200, 64, 32), (16, 128, 128), (33, 256, 300), (1, 14336, 1000),
+])
+@pytest.mark.parametrize("algo", ["gemv", "tcgen05"])
+def test_ragged_shapes(ws, M, K, N, algo):
+    """Tails in every dimension: N and M not multiples of the tiles, K not a multiple of
+    the 128-wide stage (TMA zero fill), tiny K, M past one token tile."""
+    _run_case(M, K, N, ALGOS[algo], ws, seed=M + K + N)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+@pytest.mark.parametrize("algo", ["gemv", "tcgen05"])
+def test_strided_x_and_y(ws, algo):
+    M, K, N = 20, 256, 192
+    x, w, s = make_inputs(M, K, N, seed=3)
+    big = torch.zeros(M, K + 64, dtype=torch.bfloat16, device="cuda")
+    big[:, :K] = x.cuda()
+    ybig = torch.full((M, N + 24), 7.0, dtype=torch.bfloat16, device="cuda")
+    abi_linear(big, w.cuda(), s.cuda(), ws, algo=ALGOS[algo], ldx=K + 64, y=ybig)
+    torch.cuda.synchronize()
+    check_parity(ybig[:, :N], oracle_rows(x, w, s, np.arange(M)), "strided")
+    assert torch.all(ybig[:, N:] == 7.0), "wrote outside [M, N]"
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 512])
+def test_deterministic(ws, M):
+    K, N = 4096, 4096
+    x, w, s = make_inputs(M, K, N, seed=5)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    a = abi_linear(xd, wd, sd, ws, algo=_lib.ALGO_TCGEN05)
+    b = abi_linear(xd, wd, sd, ws, algo=_lib.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_linearity_full_size(ws):
+    """y(2x) == 2 y(x) exactly (power-of-two scaling commutes with every rounding), at a
+    full 8B gate_up shape where the oracle would be slow."""
+    K, N = LLAMA3_8B_SHAPES["gate_up"]
+    x, w, s = make_inputs(64, K, N, seed=9)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    for algo in (_lib.ALGO_TCGEN05, _lib.ALGO_GEMV):
+        y1 = abi_linear(xd[:4] if algo == _lib.ALGO_GEMV else xd, wd, sd, ws, algo=algo)
+        y2 = abi_linear((xd[:4] if algo == _lib.ALGO_GEMV else xd) * 2, wd, sd, ws, algo=algo)
+        torch.cuda.synchronize()
+        assert torch.equal(y2, y1 * 2)
+
+
+def test_zero_inputs(ws):
+    K, N = 512, 256
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+    s = torch.rand(N, device="cuda") + 0.1
+    for algo in (_lib.ALGO_GEMV, _lib.ALGO_TCGEN05):
+        y = abi_linear(torch.zeros(9, K, dtype=torch.bfloat16, device="cuda"), w, s, ws, algo=algo)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(y) == 0
+
+
+def test_extreme_weights(ws):
+    """All +-127 weights with the largest scale: no int overflow / saturation anywhere."""
+    K, N = 14336, 256
+    w = torch.full((N, K), 127, dtype=torch.int8)
+    w[1::2] = -127
+    s = torch.full((N,), 5e-4)
+    x = torch.ones(16, K, dtype=torch.bfloat16)
+    for algo in (_lib.ALGO_GEMV, _lib.ALGO_TCGEN05):
+        y = abi_linear(x.cuda(), w.cuda(), s.cuda(), ws, algo=algo)
+        torch.cuda.synchronize()
+        check_parity(y, ref_int8_linear(x.float().numpy(), w.numpy(), s.numpy()), "extremes")
+
+
+def test_quantize_kernel_bit_exact():
+    g = torch.Generator().manual_seed(11)
+    for dtype in (torch.float32, torch.bfloat16, torch.float16):
+        w = (torch.randn(300, 1000, generator=g) * torch.rand(300, 1, generator=g) * 3).to(dtype)
+        w[5] = 0
+        q, s = ops.quantize_per_channel(w.cuda())
+        qr, sr = ref_quantize(w.float().numpy())
+        assert np.array_equal(q.cpu().numpy(), qr), dtype
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32)), dtype
+
+
+def test_ops_wrapper_leading_dims_and_errors():
+    x, w, s = make_inputs(6, 256, 96, seed=2)
+    xd = x.cuda().view(2, 3, 256)
+    y = ops.int8_linear(xd, w.cuda(), s.cuda())
+    assert y.shape == (2, 3, 96) and y.dtype == torch.bfloat16
+    check_parity(y.view(6, 96), ref_int8_linear(x.float().numpy(), w.numpy(), s.numpy()), "ops")
+    with pytest.raises(ValueError):
+        ops.int8_linear(xd.float(), w.cuda(), s.cuda())
+    with pytest.raises(ValueError):
+        ops.int8_linear(xd, w.cuda()[:, :128], s.cuda())
+    with pytest.raises(ValueError):
+        ops.int8_linear(torch.zeros(2, 24, dtype=torch.bfloat16, device="cuda"),
+                        torch.zeros(8, 24, dtype=torch.int8, device="cuda"), torch.ones(8, device="cuda"))
+    assert ops.int8_linear(torch.zeros(0, 256, dtype=torch.bfloat16, device="cuda"), w.cuda(), s.cuda()).shape == (0, 96)
+
+
+def test_device_status_clean():
+    assert ops.device_status() == _lib.LSE_OK
