@@ -172,9 +172,10 @@ def barrier(world: int):
         dist.barrier()
 
 
-def make_weights(layers: int, device, seed: int):
+def make_weights(layers: int, device, seed: int, ops):
     """Per layer, per shape: int8 W uniform on [-127, 127] and fp32 s uniform [1e-4, 5e-4],
-    drawn on the device from a seeded generator (7 GB would take minutes on the host)."""
+    drawn on the device from a seeded generator (7 GB would take minutes on the host), then
+    repacked once into the tile-contiguous layout the module stores (Int8Linear)."""
     g = torch.Generator(device=device).manual_seed(seed)
     out = []
     for _ in range(layers):
@@ -183,18 +184,24 @@ def make_weights(layers: int, device, seed: int):
             K, N = LLAMA3_8B_SHAPES[name]
             w = torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int8)
             s = torch.empty(N, device=device).uniform_(1e-4, 5e-4, generator=g)
-            d[name] = (w, s)
+            d[name] = (ops.pack_weight(w), s)
+            del w
         out.append(d)
     return out
 
 
-def decode_step_fn(weights, xs, ys, int8_linear):
+def linear_call(ops, x, wp, s, y, name):
+    K, N = LLAMA3_8B_SHAPES[name]
+    ops.int8_linear_packed(x, wp, s, N, K, out=y)
+
+
+def decode_step_fn(weights, xs, ys, ops):
     def step():
         for M in DECODE_M:
             for layer in weights:
                 for name in SHAPE_ORDER:
-                    w, s = layer[name]
-                    int8_linear(xs[(M, name)], w, s, out=ys[(M, name)])
+                    wp, s = layer[name]
+                    linear_call(ops, xs[(M, name)], wp, s, ys[(M, name)], name)
     return step
 
 
@@ -317,7 +324,7 @@ def main():
 
     hbm_peak, bf16_peak, bf16_sustained, peak_src = peaks()
     layers = args.layers
-    weights = make_weights(layers, dev, seed=1000 + rank)
+    weights = make_weights(layers, dev, seed=1000 + rank, ops=ops)
     gx = torch.Generator(device=dev).manual_seed(7 + rank)
     xs, ys = {}, {}
     for M in DECODE_M:
@@ -329,7 +336,7 @@ def main():
     launches_per_step = len(DECODE_M) * len(SHAPE_ORDER) * layers
 
     warm = torch.cuda.Stream(device=dev)
-    step = decode_step_fn(weights, xs, ys, ops.int8_linear)
+    step = decode_step_fn(weights, xs, ys, ops)
     graph = capture(step, warm)
 
     for _ in range(args.warmup):
@@ -360,8 +367,8 @@ def main():
 
             def one(M=M, name=name):
                 for layer in weights:
-                    w, s = layer[name]
-                    ops.int8_linear(xs[(M, name)], w, s, out=ys[(M, name)])
+                    wp, s = layer[name]
+                    linear_call(ops, xs[(M, name)], wp, s, ys[(M, name)], name)
             g1 = capture(one, warm)
             time_graph(g1, 2)
             per_launch_ms = time_graph(g1, 10) / layers
@@ -399,10 +406,10 @@ def main():
                 K, N = LLAMA3_8B_SHAPES[name]
                 xp = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
                 yp = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-                w, s = layer0[name]
+                wp, s = layer0[name]
 
-                def one(xp=xp, yp=yp, w=w, s=s):
-                    ops.int8_linear(xp, w, s, out=yp)
+                def one(xp=xp, yp=yp, wp=wp, s=s, name=name):
+                    linear_call(ops, xp, wp, s, yp, name)
                 g1 = capture(one, warm)
                 time_graph(g1, 2)
                 t = time_graph(g1, 10)

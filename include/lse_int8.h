@@ -41,9 +41,12 @@ typedef enum lse_status {
 
 /* Kernel selection for lse_int8_linear_ex. */
 typedef enum lse_algo {
-    LSE_ALGO_AUTO = 0,     /* pick by M: CUDA-core GEMV for tiny M, tcgen05 GEMM otherwise */
-    LSE_ALGO_GEMV = 1,     /* CUDA-core GEMV, 128-bit int8 streams, warp-shuffle reduction */
-    LSE_ALGO_TCGEN05 = 2   /* tcgen05/TMEM tensor-core GEMM fed by TMA (stream-K over tiles) */
+    LSE_ALGO_AUTO = 0,     /* pick by M and weight layout (see lse_int8_linear_packed) */
+    LSE_ALGO_GEMV = 1,     /* row-major W only: CUDA-core GEMV, 128-bit int8 streams, warp-shuffle reduction */
+    LSE_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM tensor-core GEMM fed by TMA (stream-K over tiles) */
+    LSE_ALGO_SKINNY = 3    /* packed W only, M <= 16: warp-MMA skinny GEMM for decode (fp16 MMA on
+                              exactly widened weights and bf16->fp16 activations), bulk-copied
+                              weight streams, K split reduced across warps with the scale folded in */
 } lse_algo;
 
 /* Weight dtypes accepted by lse_int8_quantize. */
@@ -63,7 +66,7 @@ int lse_init(int device);
  *   x      bf16 [M, K], row stride ldx (>= K, multiple of 8), 16-byte aligned
  *   w      int8 [N, K] row-major (nn.Linear [out, in] layout), K % 16 == 0, 16-byte aligned
  *   scale  fp32 [N] per-output-channel scale
- *   y      bf16 [M, N], row stride ldy (>= N, multiple of 8 unless M == 1), 16-byte aligned
+ *   y      bf16 [M, N], row stride ldy (>= N), 2-byte aligned
  *   workspace  device scratch of at least lse_int8_linear_workspace(M, K, N) bytes,
  *              16-byte aligned; its first LSE_WS_COUNTER_BYTES bytes must be zero before the
  *              first call, and every successful call leaves them zero again.
@@ -82,6 +85,30 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx,
                        void *y, int64_t ldy,
                        void *workspace, size_t workspace_bytes,
                        int algo, void *stream);
+
+/*
+ * Packed weights.  The kernels stream weights fastest from a fragment-major layout: W is
+ * zero padded to Np = 128*ceil(N/128) rows and Kp = 128*ceil(K/128) columns; each block of
+ * 16 rows is one contiguous run of 16*Kp bytes made of 512-byte chunks (one per 32 columns)
+ * in which lane t = 4*r0 + q of a warp owns 16 bytes:
+ *   W[rb*16 + rr*8 + r0][kc*32 + h*16 + 4*q + e]  at  (rb*(Kp/32) + kc)*512 + t*16 + h*8 + rr*4 + e
+ * (rb row block, kc column chunk, h, rr in {0,1}, r0 < 8, q < 4, e < 4), each byte stored
+ * biased (v ^ 0x80, i.e. v + 128).  One 128-bit load per
+ * lane then yields warp-MMA operand fragments for the decode kernel, and tensor-memory rows
+ * for the prefill kernel, without any shuffling.
+ * The repack happens once, at load (the build's counterpart of the reference loading
+ * nn.Linear weights at model_runner.py:50-53); lse_int8_linear_packed then has the same
+ * contract as lse_int8_linear_ex with `w_packed` in place of the row-major W.  Its auto
+ * choice is LSE_ALGO_SKINNY for M <= 16 (decode) and LSE_ALGO_TCGEN05 above.
+ */
+size_t lse_int8_packed_weight_bytes(int64_t N, int64_t K);
+int lse_int8_pack_weight(const int8_t *w, int64_t N, int64_t K, int64_t ldw, int8_t *w_packed, void *stream);
+int lse_int8_unpack_weight(const int8_t *w_packed, int64_t N, int64_t K, int8_t *w, void *stream);
+int lse_int8_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx,
+                           const int8_t *w_packed, const float *scale, int64_t N,
+                           void *y, int64_t ldy,
+                           void *workspace, size_t workspace_bytes,
+                           int algo, void *stream);
 
 /* Bytes of the counter region at the start of every workspace (must start zeroed). */
 #define LSE_WS_COUNTER_BYTES 65536

@@ -28,6 +28,7 @@ LSE_ERR_DEVICE_TIMEOUT = 6
 ALGO_AUTO = 0
 ALGO_GEMV = 1
 ALGO_TCGEN05 = 2
+ALGO_SKINNY = 3
 
 # lse_dtype
 DT_BF16 = 0
@@ -44,6 +45,10 @@ SIGNATURES = {
     "lse_int8_linear": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _P], _I32),
     "lse_int8_linear_ex": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
     "lse_int8_linear_workspace": ([_I64, _I64, _I64], _SZ),
+    "lse_int8_linear_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
+    "lse_int8_packed_weight_bytes": ([_I64, _I64], _SZ),
+    "lse_int8_pack_weight": ([_P, _I64, _I64, _I64, _P, _P], _I32),
+    "lse_int8_unpack_weight": ([_P, _I64, _I64, _P, _P], _I32),
     "lse_int8_quantize": ([_P, _I32, _I64, _I64, _I64, _P, _P, _P], _I32),
     "lse_status_string": ([_I32], ctypes.c_char_p),
     "lse_last_cuda_error": ([], ctypes.c_char_p),

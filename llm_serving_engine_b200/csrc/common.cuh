@@ -71,6 +71,38 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t v, uint32_t &p01, uint32
     p23 = i8pair_to_bf16x2(__byte_perm(v, 0u, 0x4342));
 }
 
+// Biased weights (u = v ^ 0x80, the packed layout's storage) -> bf16x2.  Same construction as
+// above; only the sign term flips: c = 0x4300 | (~u & 0x80).
+__device__ __forceinline__ uint32_t u8pair_to_bf16x2(uint32_t spread) {
+    uint32_t t, c, r;
+    asm("lop3.b32 %0, %1, 0x007F007F, 0x43004300, 0xEA;" : "=r"(t) : "r"(spread));  // (a&b)|c
+    asm("lop3.b32 %0, %1, 0x00800080, 0x43004300, 0xAE;" : "=r"(c) : "r"(spread));  // (~a&b)|c
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(c));
+    return r;
+}
+__device__ __forceinline__ void u8x4_to_bf16x4(uint32_t v, uint32_t &p01, uint32_t &p23) {
+    p01 = u8pair_to_bf16x2(__byte_perm(v, 0u, 0x4140));
+    p23 = u8pair_to_bf16x2(__byte_perm(v, 0u, 0x4342));
+}
+
+// Biased weights -> f16x2 in two instructions per pair: the byte permute builds
+// 0x64uu = 1024 + u (exact: fp16 has 10 mantissa bits) and 1024 + u - 1152 = v is exact.
+__device__ __forceinline__ void u8x4_to_f16x4(uint32_t v, uint32_t &p01, uint32_t &p23) {
+    const uint32_t k1152 = 0x64806480u;  // (1152, 1152) in f16
+    const uint32_t a = __byte_perm(v, 0x64646464u, 0x5140);
+    const uint32_t b = __byte_perm(v, 0x64646464u, 0x5342);
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(p01) : "r"(a), "r"(k1152));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(p23) : "r"(b), "r"(k1152));
+}
+
+// bf16x2 -> f16x2, round to nearest, saturating to +-65504 (exact for |x| in [2^-14, 65504]).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
+    const float lo = __uint_as_float(v << 16), hi = __uint_as_float(v & 0xFFFF0000u);
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 __device__ __forceinline__ long long clock64_now() {
     long long c;
     asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));

@@ -1,4 +1,4 @@
-// CUDA-core int8 weight-only GEMV for tiny M (decode with 1-4 tokens).
+// CUDA-core int8 weight-only GEMV for tiny M (decode with 1-4 tokens) on row-major W.
 //
 // y[m, n] = s[n] * sum_k x[m, k] * w[n, k]
 //
@@ -36,14 +36,26 @@ gemv_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 #pragma unroll
         for (int t = 0; t < MT; ++t) acc[r][t] = make_float2(0.f, 0.f);
 
-    for (int c = threadIdx.x; c < chunks; c += kGemvThreads) {
-        int4 wv[ROWS];
+    // Weights never depend on the previous kernel: issue the first chunk's weight loads,
+    // then wait for the previous kernel's output (programmatic dependent launch) before
+    // reading activations or writing y.
+    int4 wv[ROWS];
+    auto load_w = [&](int c) {
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
             const int n = n0 + r;
-            wv[r] = (n < N) ? ld_stream_v4(w + (int64_t)n * K + (int64_t)c * 16)
-                            : make_int4(0, 0, 0, 0);
+            wv[r] = (n < N && c < chunks) ? ld_stream_v4(w + static_cast<int64_t>(n) * K + static_cast<int64_t>(c) * 16)
+                                          : make_int4(0, 0, 0, 0);
         }
+    };
+    load_w(threadIdx.x);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    for (int c = threadIdx.x; c < chunks; c += kGemvThreads) {
+        int4 cur[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) cur[r] = wv[r];
+        load_w(c + kGemvThreads);  // next chunk in flight while this one is consumed
         // Activations for this chunk: 16 bf16 per token = two 128-bit loads.
         float2 xf[MT][8];
 #pragma unroll
@@ -66,8 +78,8 @@ gemv_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
         }
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
-            const uint32_t words[4] = {(uint32_t)wv[r].x, (uint32_t)wv[r].y, (uint32_t)wv[r].z,
-                                       (uint32_t)wv[r].w};
+            const uint32_t words[4] = {(uint32_t)cur[r].x, (uint32_t)cur[r].y, (uint32_t)cur[r].z,
+                                       (uint32_t)cur[r].w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 float2 lo, hi;
@@ -80,6 +92,9 @@ gemv_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
             }
         }
     }
+
+    // Multi-wave grid: admit the next kernel's CTAs only as this one winds down.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // Reduce: pair -> warp (shuffle) -> CTA (shared memory, 8 warps).
     __shared__ float red[kGemvThreads / 32][ROWS * MT];

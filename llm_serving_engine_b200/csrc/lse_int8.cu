@@ -9,12 +9,15 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/lse_int8.h"
 #include "gemv_i8.cuh"
+#include "pack_w.cuh"
 #include "quantize.cuh"
+#include "skinny_mma.cuh"
 #include "tc_gemm_i8.cuh"
 
 namespace lse {
@@ -53,6 +56,19 @@ cudaError_t set_tc_attrs() {
                                 tc::Cfg<NT>::SMEM_BYTES);
 }
 
+template <int MT, int KW>
+cudaError_t set_skinny_attr() {
+    return cudaFuncSetAttribute(skinny_i8_kernel<MT, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                SkinnyCfg<KW>::SMEM);
+}
+cudaError_t set_skinny_attrs() {
+    cudaError_t e = set_skinny_attr<1, 4>();
+    if (e == cudaSuccess) e = set_skinny_attr<2, 4>();
+    if (e == cudaSuccess) e = set_skinny_attr<1, 16>();
+    if (e == cudaSuccess) e = set_skinny_attr<2, 16>();
+    return e;
+}
+
 int init_device(int device) {
     if (device < 0 || device >= kMaxDevices) return LSE_ERR_INVALID_ARG;
     DeviceState &d = g_dev[device];
@@ -67,6 +83,7 @@ int init_device(int device) {
         if (e == cudaSuccess) e = set_tc_attrs<32>();
         if (e == cudaSuccess) e = set_tc_attrs<64>();
         if (e == cudaSuccess) e = set_tc_attrs<128>();
+        if (e == cudaSuccess) e = set_skinny_attrs();
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
         std::call_once(g_encode_once, [] {
             void *fn = nullptr;
@@ -92,6 +109,39 @@ int current_device(int *dev) {
     cudaError_t e = cudaGetDevice(dev);
     if (e != cudaSuccess) { set_cuda_error(e, "cudaGetDevice"); return LSE_ERR_CUDA; }
     return init_device(*dev);
+}
+
+// Programmatic dependent launch: both kernels start their weight streams before waiting on
+// the previous kernel in the stream (griddepcontrol.wait), which hides launch latency and
+// pipeline fill between back-to-back projections.  LSE_DISABLE_PDL=1 turns it off.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("LSE_DISABLE_PDL");
+        return !(v && v[0] == '1');
+    }();
+    return on;
+}
+
+// How many 16 KB weight tiles the kernel's prefetch warp keeps in flight to L2 ahead of the
+// data that has landed in shared memory (LSE_PF_STAGES overrides; 0 disables).
+int prefetch_stages() {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_PF_STAGES");
+        return e ? std::atoi(e) : 12;
+    }();
+    return v;
+}
+
+void launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&attr)[1], dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t st) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -131,13 +181,14 @@ size_t tc_workspace_bytes(int nt, int grid) {
 }
 
 int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         std::snprintf(t_last_error, sizeof(t_last_error), "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -148,9 +199,15 @@ int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
 
 template <int NT>
 int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
-              const float *scale, int64_t N, void *y, int64_t ldy, void *ws, cudaStream_t st) {
+              const float *scale, int64_t N, void *y, int64_t ldy, void *ws, bool packed, cudaStream_t st) {
     CUtensorMap tw, tx;
-    int rc = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, tc::BK, tc::BN);
+    // Packed W: [Np/16 row blocks][16*Kp bytes] as 8-byte elements, box = one 128 x 128 tile
+    // (8 row blocks x 2 KB), no swizzle.  Row-major W: [N][K] bytes, 128 x 128 box, 128B swizzle.
+    const int64_t Kp = packed_cols(K);
+    int rc = packed ? encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, static_cast<uint64_t>(2 * Kp),
+                                static_cast<uint64_t>(packed_rows(N) / 16), static_cast<uint64_t>(16 * Kp), 256, 8,
+                                CU_TENSOR_MAP_SWIZZLE_NONE)
+                    : encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, tc::BK, tc::BN);
     if (rc) return rc;
     rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, ldx * 2, 64, NT);
     if (rc) return rc;
@@ -169,38 +226,88 @@ int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx
     p.dp_tiles = pl.dp_tiles;
     p.grid = pl.grid;
     p.sk_units = pl.sk_units;
-    tc::tc_gemm_i8_kernel<NT><<<pl.grid, tc::NUM_THREADS, tc::Cfg<NT>::SMEM_BYTES, st>>>(tw, tx, p);
-    cudaError_t e = cudaGetLastError();
+    p.w_packed = packed ? 1 : 0;
+    p.w = w;
+    p.pf_stages = prefetch_stages();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(pl.grid), dim3(tc::NUM_THREADS), tc::Cfg<NT>::SMEM_BYTES, st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_i8_kernel<NT>, tw, tx, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "tc_gemm_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }
 
 template <int MT, int ROWS>
-void launch_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale,
+cudaError_t launch_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale,
                  int64_t N, void *y, int64_t ldy, cudaStream_t st) {
     dim3 grid(static_cast<unsigned>((N + ROWS - 1) / ROWS), static_cast<unsigned>((M + MT - 1) / MT));
-    gemv_i8_kernel<MT, ROWS><<<grid, kGemvThreads, 0, st>>>(static_cast<const __nv_bfloat16 *>(x), ldx,
-                                                           static_cast<int>(M), static_cast<int>(K), w, scale,
-                                                           static_cast<int>(N),
-                                                           static_cast<__nv_bfloat16 *>(y), ldy);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, grid, dim3(kGemvThreads), 0, st);
+    return cudaLaunchKernelEx(&cfg, gemv_i8_kernel<MT, ROWS>, static_cast<const __nv_bfloat16 *>(x), ldx,
+                              static_cast<int>(M), static_cast<int>(K), w, scale, static_cast<int>(N),
+                              static_cast<__nv_bfloat16 *>(y), ldy);
 }
 
 int run_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale, int64_t N,
              void *y, int64_t ldy, cudaStream_t st) {
+    cudaError_t e;
     switch (M) {
-        case 1: launch_gemv<1, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
-        case 2: launch_gemv<2, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
-        case 3: launch_gemv<3, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
-        default: launch_gemv<4, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
+        case 1: e = launch_gemv<1, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
+        case 2: e = launch_gemv<2, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
+        case 3: e = launch_gemv<3, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
+        default: e = launch_gemv<4, 4>(x, M, K, ldx, w, scale, N, y, ldy, st); break;
     }
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "gemv_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }
 
-// Auto policy: the CUDA-core GEMV while its FMA work stays under the HBM stream
-// (M <= 2), the tensor-core kernel from there on.
-int auto_algo(int64_t M) { return M <= 2 ? LSE_ALGO_GEMV : LSE_ALGO_TCGEN05; }
+template <int MT, int KW>
+cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
+                          int64_t N, void *y, int64_t ldy, cudaStream_t st) {
+    dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, grid, dim3(KW * 32), SkinnyCfg<KW>::SMEM, st);
+    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW>, static_cast<const __nv_bfloat16 *>(x), ldx,
+                              static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
+                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)));
+}
+
+int num_sms_of_current() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || g_dev[dev].num_sms <= 0) return 148;
+    return g_dev[dev].num_sms;
+}
+
+constexpr int64_t kSkinnyMaxM = 16;  // the decode kernel's token range (two 8-token tiles)
+
+int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale, int64_t N,
+               void *y, int64_t ldy, cudaStream_t st) {
+    if (M > kSkinnyMaxM) return LSE_ERR_UNSUPPORTED;
+    // Few row blocks (N / 16 below ~2 per SM): split K over 16 warps so every SM still holds
+    // enough warps (and bytes in flight); otherwise 4 warps per CTA and more CTAs per SM.
+    const bool wide = (N + 15) / 16 < 2 * num_sms_of_current();
+    cudaError_t e;
+    if (M <= 8) e = wide ? launch_skinny<1, 16>(x, M, K, ldx, wp, scale, N, y, ldy, st)
+                         : launch_skinny<1, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+    else e = wide ? launch_skinny<2, 16>(x, M, K, ldx, wp, scale, N, y, ldy, st)
+                  : launch_skinny<2, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+// Auto policy.  Row-major W: the CUDA-core GEMV while its FMA work stays under the HBM
+// stream (M <= 2), the tensor-core kernel from there on.  Packed W: the warp-MMA skinny
+// kernel while the weight stream, not MMA issue, is the bound (M <= 16), the tcgen05
+// kernel from there on.
+int auto_algo(int64_t M, bool packed) {
+    if (packed) return M <= 16 ? LSE_ALGO_SKINNY : LSE_ALGO_TCGEN05;
+    return M <= 2 ? LSE_ALGO_GEMV : LSE_ALGO_TCGEN05;
+}
 
 }  // namespace
 }  // namespace lse
@@ -235,9 +342,12 @@ size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N) {
     return tc_workspace_bytes(token_tile(M), kMaxGridForWorkspace);
 }
 
-int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale,
-                       int64_t N, void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo,
-                       void *stream) {
+}  // extern "C"
+
+namespace lse {
+namespace {
+int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale, int64_t N,
+                void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo, bool packed, void *stream) {
     if (M < 0 || N < 0 || K < 0) return LSE_ERR_INVALID_ARG;
     if (M == 0 || N == 0) return LSE_OK;
     if (!x || !w || !scale || !y) return LSE_ERR_INVALID_ARG;
@@ -245,7 +355,8 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx, const i
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
     if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w)) return LSE_ERR_ALIGNMENT;
     if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
-    if (algo < LSE_ALGO_AUTO || algo > LSE_ALGO_TCGEN05) return LSE_ERR_INVALID_ARG;
+    if (algo < LSE_ALGO_AUTO || algo > LSE_ALGO_SKINNY) return LSE_ERR_INVALID_ARG;
+    if ((algo == LSE_ALGO_GEMV && packed) || (algo == LSE_ALGO_SKINNY && !packed)) return LSE_ERR_UNSUPPORTED;
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
@@ -256,24 +367,77 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx, const i
         if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
         return LSE_OK;
     }
-    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M);
+    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed);
     if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);
+    if (algo == LSE_ALGO_SKINNY) return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, st);
 
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
         return LSE_ERR_WORKSPACE;
     switch (pl.nt) {
-        case 16: return launch_tc<16>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, st);
-        case 32: return launch_tc<32>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, st);
-        case 64: return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, st);
-        default: return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, st);
+        case 16: return launch_tc<16>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
+        case 32: return launch_tc<32>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
+        case 64: return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
+        default: return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
     }
+}
+}  // namespace
+}  // namespace lse
+
+extern "C" {
+
+int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale,
+                       int64_t N, void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo,
+                       void *stream) {
+    return linear_impl(x, M, K, ldx, w, scale, N, y, ldy, workspace, workspace_bytes, algo, false, stream);
 }
 
 int lse_int8_linear(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale,
                     int64_t N, void *y, int64_t ldy, void *workspace, size_t workspace_bytes, void *stream) {
-    return lse_int8_linear_ex(x, M, K, ldx, w, scale, N, y, ldy, workspace, workspace_bytes, LSE_ALGO_AUTO,
-                              stream);
+    return linear_impl(x, M, K, ldx, w, scale, N, y, ldy, workspace, workspace_bytes, LSE_ALGO_AUTO, false,
+                       stream);
+}
+
+int lse_int8_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                           const float *scale, int64_t N, void *y, int64_t ldy, void *workspace,
+                           size_t workspace_bytes, int algo, void *stream) {
+    return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, workspace, workspace_bytes, algo, true, stream);
+}
+
+size_t lse_int8_packed_weight_bytes(int64_t N, int64_t K) {
+    if (N <= 0 || K <= 0) return 0;
+    return static_cast<size_t>(packed_weight_bytes(N, K));
+}
+
+int lse_int8_pack_weight(const int8_t *w, int64_t N, int64_t K, int64_t ldw, int8_t *w_packed, void *stream) {
+    if (N < 0 || K < 0 || ldw < K) return LSE_ERR_INVALID_ARG;
+    if (N == 0 || K == 0) return LSE_OK;
+    if (!w || !w_packed) return LSE_ERR_INVALID_ARG;
+    if (!aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const int64_t quads = packed_weight_bytes(N, K) / 4;
+    pack_weight_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        w, N, K, ldw, w_packed, packed_cols(K), quads);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "pack launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+int lse_int8_unpack_weight(const int8_t *w_packed, int64_t N, int64_t K, int8_t *w, void *stream) {
+    if (N < 0 || K < 0) return LSE_ERR_INVALID_ARG;
+    if (N == 0 || K == 0) return LSE_OK;
+    if (!w || !w_packed) return LSE_ERR_INVALID_ARG;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const int64_t total = N * K;
+    unpack_weight_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        w_packed, N, K, w, packed_cols(K));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "unpack launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
 }
 
 int lse_int8_quantize(const void *w, int dtype, int64_t N, int64_t K, int64_t ldw, int8_t *q_out, float *s_out,

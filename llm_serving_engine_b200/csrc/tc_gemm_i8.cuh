@@ -17,8 +17,8 @@
 //     warps read it with tcgen05.ld, apply s[n] and store bf16 y.
 //
 // Warp roles (512 threads): warp 0 TMA producer, warp 1 TMEM allocator + single-thread MMA
-// issuer, warps 4-7 epilogue (TMEM lane quarter = warp % 4), warps 8-15 converters (two
-// warps per lane quarter, each widening half of a stage's K).
+// issuer, warp 2 L2 prefetcher for the weight stream, warps 4-7 epilogue (TMEM lane quarter = warp % 4), warps 8-15 converters (two
+// groups of four, one warp per lane quarter; the groups take alternate stages).
 //
 // Work distribution: tiles are (128 weight rows) x (NT tokens), tile = n_tile * m_tiles +
 // m_tile.  Full waves of tiles are dealt round-robin to a persistent grid of G CTAs
@@ -47,7 +47,9 @@ constexpr int W_STAGE_BYTES = BN * BK;    // int8 weight tile per stage
 constexpr int A_SLOT_COLS = BK / 2;       // TMEM columns per A slot (2 bf16 per column)
 constexpr int ASLOTS = 4;                 // A slots in TMEM
 constexpr int NUM_THREADS = 512;
-constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 4, WARP_CONV0 = 8;
+constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_PREFETCH = 2, WARP_EPI0 = 4, WARP_CONV0 = 8;
+// A throttle wait of the L2 prefetcher that exceeds this gives up prefetching (~20 us).
+constexpr long long kPrefetchWaitCycles = 40000;
 constexpr int NUM_EPI_WARPS = 4, NUM_CONV_WARPS = 8;
 constexpr int EPI_BAR = 1;                // named barrier id used by the epilogue warps
 constexpr int TMEM_COLS = 512;
@@ -59,9 +61,14 @@ struct Cfg {
     static constexpr int X_STAGE_BYTES = 2 * X_BOX_BYTES;
     static constexpr int STAGE_BYTES = W_STAGE_BYTES + X_STAGE_BYTES;
     static constexpr int ACC_BUFS = 2;
+    // Independent accumulators per buffer: consecutive K16 MMAs of a stage go to different
+    // accumulators, so small-N MMAs do not wait on each other's read-modify-write of one
+    // TMEM tile; the epilogue sums them.
+    static constexpr int NACC = NT <= 32 ? 4 : (NT <= 64 ? 2 : 1);
+    static constexpr int ACC_COLS = NACC * NT;   // TMEM columns of one accumulator buffer
     static constexpr int STAGES = NT <= 32 ? 8 : (NT <= 64 ? 6 : 4);
     static constexpr int D_COL0 = 0;
-    static constexpr int A_COL0 = ACC_BUFS * NT;
+    static constexpr int A_COL0 = ACC_BUFS * ACC_COLS;
     static_assert(A_COL0 + ASLOTS * A_SLOT_COLS <= TMEM_COLS, "TMEM budget");
     // barrier block after the stages: full, empty (STAGES each), a_full, a_empty (ASLOTS),
     // d_full, d_empty (ACC_BUFS), drain; then tmem address, abort flag, reduce flag.
@@ -80,7 +87,37 @@ struct Params {
     int *counters;     // [stream-K tiles] arrival counters, zero between launches
     int m_tiles, tiles, kb, dp_tiles, grid;
     long long sk_units;
+    int w_packed;      // 1: weights in the tile-contiguous packed layout (see pack_w.cuh)
+    const int8_t *w;   // packed weights (read with 1-D bulk copies, no tensor map)
+    int pf_stages;     // L2 prefetch distance in stages beyond the shared-memory ring
 };
+
+// Weight tile (n0 / BN, kb) -> shared memory, one TMA copy either way.
+//   Packed W (pack_w.cuh): the tile is 8 row-block runs of 2 KB, stride 16*Kp bytes; the
+//   tensor map views the buffer as [Np/16 rows][2*Kp 8-byte elements] and the box is
+//   256 x 8, landing as [row block j][2 KB] in shared memory.
+//   Row-major W [N, K]: a box of 128 rows x 128 bytes at (kb * BK, n0), 128-byte swizzled.
+__device__ __forceinline__ void load_w_tile(const Params &p, const CUtensorMap *tmap_w, uint32_t dst, int n0,
+                                            int kb, uint32_t bar, uint64_t pol) {
+    if (p.w_packed) ptx::tma_load_2d(dst, tmap_w, bar, kb * (BK * 16 / 8), n0 / 16, pol);
+    else ptx::tma_load_2d(dst, tmap_w, bar, kb * BK, n0, pol);
+}
+// One warp pulls weight tile (n0 / BN, kb) into L2 ahead of its TMA copy: 128 lines of
+// 128 bytes, 4 per lane.
+__device__ __forceinline__ void prefetch_w_tile_l2(const Params &p, int n0, int kb, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int line = i * 32 + lane;
+        if (p.w_packed) {
+            const int j = line >> 4;  // row block within the tile
+            const int64_t run = (static_cast<int64_t>(n0 / 16 + j) * (p.kb * 4) + kb * 4) * 512;
+            ptx::prefetch_line_l2(p.w + run + (line & 15) * 128);
+        } else {
+            const int r = n0 + line;
+            if (r < p.N) ptx::prefetch_line_l2(p.w + static_cast<int64_t>(r) * p.K + kb * BK);
+        }
+    }
+}
 
 // ---- schedule (identical in every role) -------------------------------------------------
 __device__ __forceinline__ long long sk_begin(const Params &p, int c) {
@@ -132,6 +169,30 @@ __device__ __forceinline__ int partial_slot(const Params &p, int c, int tile) {
     return 2 * c + (tile == first_tile ? 0 : 1);
 }
 
+// Walks this CTA's (tile, k-block) stages in the order the pipeline consumes them; used
+// by the producer to issue L2 prefetches a fixed distance ahead of the TMA loads.
+struct StageCursor {
+    SegIter it;
+    Seg s;
+    int kb = 0, k1 = 0;
+    __device__ __forceinline__ void init(const Params &p, int c) { it.init(p, c); }
+    __device__ __forceinline__ bool next(const Params &p, int &n0, int &kbo) {
+        while (kb >= k1) {
+            if (!it.next(p, s)) return false;
+            kb = s.k0;
+            k1 = s.k1;
+        }
+        n0 = (s.tile / p.m_tiles) * BN;
+        kbo = kb++;
+        return true;
+    }
+    __device__ __forceinline__ void skip(const Params &p) {
+        int a, b;
+        next(p, a, b);
+    }
+
+};
+
 // Weights are read exactly once when there is a single token tile (decode): stream them
 // with evict-first so x and the partial tiles keep L2.  With several token tiles each weight
 // tile is re-read once per token tile, so leave it at normal priority.
@@ -168,10 +229,10 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::STAGES; ++i) {
             ptx::mbar_init(ptx::smem_u32(&full[i]), 1);
-            ptx::mbar_init(ptx::smem_u32(&empty[i]), 1 + NUM_CONV_WARPS);
+            ptx::mbar_init(ptx::smem_u32(&empty[i]), 1 + NUM_CONV_WARPS / 2);
         }
         for (int i = 0; i < ASLOTS; ++i) {
-            ptx::mbar_init(ptx::smem_u32(&a_full[i]), NUM_CONV_WARPS);
+            ptx::mbar_init(ptx::smem_u32(&a_full[i]), NUM_CONV_WARPS / 2);
             ptx::mbar_init(ptx::smem_u32(&a_empty[i]), 1);
         }
         for (int i = 0; i < C::ACC_BUFS; ++i) {
@@ -190,7 +251,7 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
-    __syncthreads();
+    ptx::cta_sync_all();
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -198,11 +259,31 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     it.init(p, blockIdx.x);
     Seg s;
 
+    if (threadIdx.x == 0) ptx::grid_dep_launch();
+
     if (warp == WARP_TMA) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             const uint64_t pol_w = policy_w_for(p);
             const uint64_t pol_x = ptx::policy_evict_last();
+            // Weights never depend on the previous kernel: start the first stages' weight
+            // copies before waiting for it (programmatic dependent launch), then add the
+            // activations once the previous kernel's output is visible.
+            long long pre = 0;
+            {
+                SegIter ip = it;
+                Seg sp;
+                while (pre < C::STAGES && ip.next(p, sp)) {
+                    const int n0 = (sp.tile / p.m_tiles) * BN;
+                    for (int kb = sp.k0; kb < sp.k1 && pre < C::STAGES; ++kb, ++pre) {
+                        const uint32_t fb = ptx::smem_u32(&full[pre]);
+                        ptx::mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                        load_w_tile(p, &tmap_w, ptx::smem_u32(w_smem + pre * W_STAGE_BYTES), n0, kb, fb, pol_w);
+                    }
+                }
+            }
+
+            ptx::grid_dep_wait();
             long long pos = 0;  // stages issued so far
             bool ok = true;
             while (ok && it.next(p, s)) {
@@ -211,20 +292,35 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 for (int kb = s.k0; kb < s.k1; ++kb, ++pos) {
                     const int st = static_cast<int>(pos % C::STAGES);
                     const uint32_t ph = static_cast<uint32_t>((pos / C::STAGES) & 1);
-                    if (!ptx::mbar_wait(ptx::smem_u32(&empty[st]), ph ^ 1, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
                     const uint32_t fb = ptx::smem_u32(&full[st]);
-                    ptx::mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
-                    ptx::tma_load_2d(ptx::smem_u32(w_smem + st * W_STAGE_BYTES), &tmap_w, fb, kb * BK, n0,
-                                     pol_w);
+                    if (pos >= pre) {
+                        if (!ptx::mbar_wait(ptx::smem_u32(&empty[st]), ph ^ 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+
+                        ptx::mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                        load_w_tile(p, &tmap_w, ptx::smem_u32(w_smem + st * W_STAGE_BYTES), n0, kb, fb, pol_w);
+                    }
                     uint8_t *xs = x_smem + st * C::X_STAGE_BYTES;
                     ptx::tma_load_2d(ptx::smem_u32(xs), &tmap_x, fb, kb * BK, m0, pol_x);
                     ptx::tma_load_2d(ptx::smem_u32(xs + C::X_BOX_BYTES), &tmap_x, fb, kb * BK + 64, m0, pol_x);
                 }
             }
-            // Drain: every copy this CTA issued must land before shared memory is released.
+            // Drain: every copy this CTA issued must land before shared memory is released
+            // (stages prefetched but never reached still complete their weight bytes only if
+            // their activations were issued too, so drain exactly the issued set).
+            if (pos < pre) {
+                // aborted before the loop reached every prefetched stage: issue their
+                // activation copies so each prefetched barrier can complete, then drain
+                for (long long q = pos; q < pre; ++q) {
+                    uint8_t *xs = x_smem + q * C::X_STAGE_BYTES;
+                    const uint32_t fb = ptx::smem_u32(&full[q]);
+                    ptx::tma_load_2d(ptx::smem_u32(xs), &tmap_x, fb, 0, 0, pol_x);
+                    ptx::tma_load_2d(ptx::smem_u32(xs + C::X_BOX_BYTES), &tmap_x, fb, 64, 0, pol_x);
+                }
+                pos = pre;
+            }
             const long long first = pos > C::STAGES ? pos - C::STAGES : 0;
             for (long long q = first; q < pos; ++q)
                 ptx::mbar_drain(ptx::smem_u32(&full[q % C::STAGES]), static_cast<uint32_t>((q / C::STAGES) & 1));
@@ -239,7 +335,7 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 const uint32_t dph = static_cast<uint32_t>((dpos / C::ACC_BUFS) & 1);
                 if (!ptx::mbar_wait(ptx::smem_u32(&d_empty[buf]), dph ^ 1, abort_flag)) break;
                 ptx::tc_fence_after();
-                const uint32_t d_tmem = tmem_base + C::D_COL0 + buf * NT;
+                const uint32_t d_tmem = tmem_base + C::D_COL0 + buf * C::ACC_COLS;
                 for (int kb = s.k0; kb < s.k1; ++kb, ++pos, ++apos) {
                     const int st = static_cast<int>(pos % C::STAGES);
                     const uint32_t ph = static_cast<uint32_t>((pos / C::STAGES) & 1);
@@ -251,13 +347,16 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         break;
                     }
                     ptx::tc_fence_after();
-                    const uint32_t xs = ptx::smem_u32(x_smem + st * C::X_STAGE_BYTES);
+                    // Descriptors advance by constants inside a stage: B (x) by 32 bytes per
+                    // K16 step within a 64-wide box, A (TMEM) by 8 columns.
+                    const uint64_t b0 = ptx::smem_desc_sw128(ptx::smem_u32(x_smem + st * C::X_STAGE_BYTES));
+                    const uint32_t a0 = tmem_base + C::A_COL0 + as * A_SLOT_COLS;
 #pragma unroll
                     for (int j = 0; j < KSTEPS; ++j) {
-                        const uint32_t a_tmem = tmem_base + C::A_COL0 + as * A_SLOT_COLS + j * (UK / 2);
-                        const uint64_t b_desc =
-                            ptx::smem_desc_sw128(xs + (j >> 2) * C::X_BOX_BYTES + (j & 3) * (UK * 2));
-                        ptx::mma_bf16_ts(d_tmem, a_tmem, b_desc, C::IDESC, (kb > s.k0 || j > 0) ? 1u : 0u);
+                        const uint64_t b_desc = b0 + static_cast<uint64_t>(((j >> 2) * C::X_BOX_BYTES + (j & 3) * (UK * 2)) >> 4);
+                        const int acc = j % C::NACC;
+                        ptx::mma_bf16_ts(d_tmem + acc * NT, a0 + j * (UK / 2), b_desc, C::IDESC,
+                                         (kb > s.k0 || j >= C::NACC) ? 1u : 0u);
                     }
                     ptx::mma_commit(ptx::smem_u32(&empty[st]));
                     ptx::mma_commit(ptx::smem_u32(&a_empty[as]));
@@ -272,17 +371,23 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
         }
     } else if (warp >= WARP_CONV0) {
         // ---------------- converters: int8 smem -> bf16 TMEM (A operand) ----------------
-        const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int half = (warp - WARP_CONV0) >> 2;  // which 64-K half of the stage
-        const int row = q * 32 + lane;          // weight row within the tile
-        long long pos = 0, apos = 0;
+        // Two groups of four warps (one warp per TMEM lane quarter each) take alternate
+        // stages, so each group has two stage-times per stage; inside a stage the two 64-K
+        // halves are converted back to back, the first half's tcgen05.st draining while the
+        // second half is converted.
+        const int q = warp & 3;                       // TMEM lane quarter this warp may access
+        const int grp = (warp - WARP_CONV0) >> 2;     // stages with (pos & 1) == grp
+        const int row = q * 32 + lane;                // weight row within the tile
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0;
+        long long pos = 0;
         bool ok = true;
         while (ok && it.next(p, s)) {
-            for (int kb = s.k0; kb < s.k1; ++kb, ++pos, ++apos) {
+            for (int kb = s.k0; kb < s.k1; ++kb, ++pos) {
+                if ((pos & 1) != grp) continue;
                 const int st = static_cast<int>(pos % C::STAGES);
                 const uint32_t ph = static_cast<uint32_t>((pos / C::STAGES) & 1);
-                const int as = static_cast<int>(apos % ASLOTS);
-                const uint32_t aph = static_cast<uint32_t>((apos / ASLOTS) & 1);
+                const int as = static_cast<int>(pos % ASLOTS);
+                const uint32_t aph = static_cast<uint32_t>((pos / ASLOTS) & 1);
                 bool w_ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), ph, abort_flag) &&
                             ptx::mbar_wait(ptx::smem_u32(&a_empty[as]), aph ^ 1, abort_flag);
                 if (!__all_sync(0xffffffffu, w_ok)) {
@@ -290,20 +395,47 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     break;
                 }
                 ptx::tc_fence_after();
-                const uint8_t *wrow = w_smem + st * W_STAGE_BYTES + row * BK;
-                uint32_t out[32];
+                const uint8_t *wst = w_smem + st * W_STAGE_BYTES;
+                if (p.w_packed) {
+                    // rows 32q..32q+31 = row blocks 2q, 2q+1; lane owns rows lane/4 (+8) of each
+                    // and the K quad 4(lane%4) of every 16-column step (pack_w.cuh)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int c = half * 4 + j;  // 16-byte chunk (K16 step) within the row
-                    const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ (row & 7)) << 4));
-                    i8x4_to_bf16x4(v.x, out[8 * j + 0], out[8 * j + 1]);
-                    i8x4_to_bf16x4(v.y, out[8 * j + 2], out[8 * j + 3]);
-                    i8x4_to_bf16x4(v.z, out[8 * j + 4], out[8 * j + 5]);
-                    i8x4_to_bf16x4(v.w, out[8 * j + 6], out[8 * j + 7]);
+                    for (int jb = 0; jb < 2; ++jb) {
+                        const uint8_t *src = wst + (2 * q + jb) * 2048 + lane * 16;
+                        uint4 v[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const uint4 *>(src + i * 512);
+                        uint32_t out[32];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            u8x4_to_bf16x4(v[i].x, out[8 * i + 0], out[8 * i + 1]);  // step 2i, row r0
+                            u8x4_to_bf16x4(v[i].y, out[8 * i + 2], out[8 * i + 3]);  // step 2i, row r0+8
+                            u8x4_to_bf16x4(v[i].z, out[8 * i + 4], out[8 * i + 5]);  // step 2i+1, row r0
+                            u8x4_to_bf16x4(v[i].w, out[8 * i + 6], out[8 * i + 7]);  // step 2i+1, row r0+8
+                        }
+                        ptx::tmem_st_16x256b_x8(lane_base + (static_cast<uint32_t>(16 * jb) << 16) + as * A_SLOT_COLS,
+                                                out);
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint4 v[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int c = h * 4 + j;  // 16-byte chunk (K16 step) within the row
+                            v[j] = *reinterpret_cast<const uint4 *>(wst + row * BK + ((c ^ (row & 7)) << 4));
+                        }
+                        uint32_t out[32];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            i8x4_to_bf16x4(v[j].x, out[8 * j + 0], out[8 * j + 1]);
+                            i8x4_to_bf16x4(v[j].y, out[8 * j + 2], out[8 * j + 3]);
+                            i8x4_to_bf16x4(v[j].z, out[8 * j + 4], out[8 * j + 5]);
+                            i8x4_to_bf16x4(v[j].w, out[8 * j + 6], out[8 * j + 7]);
+                        }
+                        ptx::tmem_st_32x32b_x32(lane_base + as * A_SLOT_COLS + h * (A_SLOT_COLS / 2), out);
+                    }
                 }
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + C::A_COL0 +
-                                       as * A_SLOT_COLS + half * (A_SLOT_COLS / 2);
-                ptx::tmem_st_32x32b_x32(taddr, out);
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
                 __syncwarp();
@@ -313,8 +445,36 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 }
             }
         }
+    } else if (warp == WARP_PREFETCH) {
+        // ---------------- L2 prefetcher ----------------
+        // Keeps p.pf_stages weight tiles of this CTA in flight to L2 ahead of the bulk-copy
+        // engine, through the load/store path: the engine's own request slots then only
+        // cover L2 latency, not DRAM latency.  Throttled by the `full` barriers (it never
+        // runs more than pf_stages stages past the data that has landed), and only a hint:
+        // if a throttle wait runs long it stops prefetching, it never aborts the CTA.
+        if (p.pf_stages > 0) {
+            StageCursor cur;
+            cur.init(p, blockIdx.x);
+            int n0, kbo;
+            for (long long i = 0; cur.next(p, n0, kbo); ++i) {
+                const long long j = i - p.pf_stages;
+                if (j >= 0) {
+                    const uint32_t bar = ptx::smem_u32(&full[j % C::STAGES]);
+                    const uint32_t par = static_cast<uint32_t>((j / C::STAGES) & 1);
+                    bool landed = false;
+                    const long long t0 = clock64_now();
+                    while (!(landed = ptx::mbar_try_wait(bar, par)) && !*abort_flag &&
+                           clock64_now() - t0 < kPrefetchWaitCycles) {
+                    }
+                    landed = __all_sync(0xffffffffu, landed);
+                    if (!landed) break;
+                }
+                prefetch_w_tile_l2(p, n0, kbo, lane);
+            }
+        }
     } else if (warp >= WARP_EPI0 && warp < WARP_EPI0 + NUM_EPI_WARPS) {
         // ---------------- epilogue: TMEM -> scale -> bf16 y (or fp32 partial) ----------------
+        ptx::grid_dep_wait();  // y, partials and counters may still be in use by the previous kernel
         const int q = warp & 3;
         const int row = q * 32 + lane;
         long long dpos = 0;
@@ -330,26 +490,39 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
             const bool n_ok = n < p.N;
             const float sc = n_ok ? __ldg(p.scale + n) : 0.f;
             const bool whole = (s.k0 == 0 && s.k1 == p.kb);
-            const uint32_t d_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0 + buf * NT;
+            const int mval = min(NT, p.M - m0);  // valid token columns of this tile
+            const uint32_t d_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + C::D_COL0 + buf * C::ACC_COLS;
             float *part = nullptr;
             if (!whole) part = p.partials + static_cast<size_t>(partial_slot(p, blockIdx.x, s.tile)) * (NT * BN);
             constexpr int CH = NT < 32 ? NT : 32;
 #pragma unroll 1
             for (int c0 = 0; c0 < NT; c0 += CH) {
+                if (c0 >= mval) break;
                 uint32_t v[32];
                 if constexpr (CH == 32) ptx::tmem_ld_32x32b_x32(d_lane + c0, v);
                 else ptx::tmem_ld_32x32b_x16(d_lane + c0, v);
                 ptx::tmem_wait_ld();
+#pragma unroll
+                for (int a = 1; a < C::NACC; ++a) {  // fold the other accumulators in, fixed order
+                    uint32_t u[32];
+                    if constexpr (CH == 32) ptx::tmem_ld_32x32b_x32(d_lane + a * NT + c0, u);
+                    else ptx::tmem_ld_32x32b_x16(d_lane + a * NT + c0, u);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < CH; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
+                }
                 if (whole) {
 #pragma unroll
                     for (int j = 0; j < CH; ++j) {
-                        const int m = m0 + c0 + j;
-                        if (n_ok && m < p.M)
-                            p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(__uint_as_float(v[j]) * sc);
+                        if (n_ok && c0 + j < mval)
+                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + n] =
+                                __float2bfloat16_rn(__uint_as_float(v[j]) * sc);
                     }
                 } else {
+                    // partial tile layout [token j][row]: one 128-byte line per warp per j
 #pragma unroll
-                    for (int j = 0; j < CH; ++j) part[(c0 + j) * BN + row] = __uint_as_float(v[j]);
+                    for (int j = 0; j < CH; ++j)
+                        if (c0 + j < mval) part[(c0 + j) * BN + row] = __uint_as_float(v[j]);
                 }
             }
             ptx::tc_fence_before();
@@ -374,16 +547,53 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 ptx::bar_sync(EPI_BAR, NUM_EPI_WARPS * 32);  // flag read by all before reuse
                 if (last) {
                     __threadfence();
+                    // Sum the segments' partials in segment order (deterministic).  Thread t
+                    // owns 4 consecutive rows (rq..rq+3) and tokens j = jb + 4i, so every
+                    // load is a float4 and a warp reads 512 contiguous bytes; all IC loads of
+                    // one segment are independent and in flight together.
+                    const int t = threadIdx.x - WARP_EPI0 * 32;
+                    const int rq = (t & 31) * 4;
+                    const int jb = t >> 5;
+                    const int nq = n_tile * BN + rq;
+                    float scq[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) scq[e] = (nq + e < p.N) ? __ldg(p.scale + nq + e) : 0.f;
+                    constexpr int NI = NT / 4;
+                    constexpr int IC = NI < 8 ? NI : 8;
 #pragma unroll 1
-                    for (int j = 0; j < NT; ++j) {
-                        const int m = m0 + j;
-                        if (m >= p.M) break;
-                        float acc = 0.f;
+                    for (int i0 = 0; i0 < NI; i0 += IC) {
+                        if (jb + 4 * i0 >= mval) break;
+                        float4 acc[IC];
+#pragma unroll
+                        for (int ii = 0; ii < IC; ++ii) acc[ii] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
                         for (int c = c_first; c <= c_last; ++c) {
-                            const float *pc = p.partials + static_cast<size_t>(partial_slot(p, c, s.tile)) * (NT * BN);
-                            acc += __ldcg(pc + j * BN + row);
+                            const float4 *pc = reinterpret_cast<const float4 *>(
+                                p.partials + static_cast<size_t>(partial_slot(p, c, s.tile)) * (NT * BN));
+                            float4 v[IC];
+#pragma unroll
+                            for (int ii = 0; ii < IC; ++ii) {
+                                const int j = jb + 4 * (i0 + ii);
+                                v[ii] = j < mval ? __ldcg(pc + ((j * BN + rq) >> 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int ii = 0; ii < IC; ++ii) {
+                                acc[ii].x += v[ii].x;
+                                acc[ii].y += v[ii].y;
+                                acc[ii].z += v[ii].z;
+                                acc[ii].w += v[ii].w;
+                            }
                         }
-                        if (n_ok) p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2bfloat16_rn(acc * sc);
+#pragma unroll
+                        for (int ii = 0; ii < IC; ++ii) {
+                            const int j = jb + 4 * (i0 + ii);
+                            if (j >= mval) continue;
+                            __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + nq;
+                            const float a4[4] = {acc[ii].x, acc[ii].y, acc[ii].z, acc[ii].w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (nq + e < p.N) yr[e] = __float2bfloat16_rn(a4[e] * scq[e]);
+                        }
                     }
                 }
             }
@@ -391,8 +601,12 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
 
     // ---------------- teardown ----------------
+    // In warps 0 and 1 only lane 0 ran the role loop; the compiler may place each branch's
+    // barrier separately, so the teardown barrier is the non-aligned form that counts every
+    // thread, and it waits for the epilogue before TMEM is freed.
+    __syncwarp();
     ptx::tc_fence_before();
-    __syncthreads();
+    ptx::cta_sync_all();
     if (warp == WARP_MMA) {
         __syncwarp();
         ptx::tc_fence_after();

@@ -25,14 +25,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+// Test for completion of the phase with `parity`; if it is not complete the thread is
+// suspended (it issues nothing) until the phase completes or `suspend_ns` elapses.  Waiting
+// warps share their SM sub-partition with the MMA issuer and the converters, so a wait must
+// sleep in hardware rather than spin.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t suspend_ns = 1000000u) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(suspend_ns)
         : "memory");
     return ok != 0;
 }
@@ -79,6 +83,30 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint
         " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
         : "memory");
+}
+// 1-D bulk copy global -> shared (one contiguous run, size % 16 == 0, both addresses 16-byte
+// aligned), completion counted in bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+// 1-D bulk prefetch of a contiguous run into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes) : "memory");
+}
+// Per-thread L2 prefetch of the 128-byte line holding `addr` (issued through the load/store
+// path, so it does not occupy the bulk-copy engine's request slots).
+__device__ __forceinline__ void prefetch_line_l2(const void *addr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(addr)));
+}
+// Bulk prefetch of one tensor-map box into L2 (no shared memory, no completion to track).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void *tmap, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
@@ -170,6 +198,21 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
+// 16 lanes x 256 bits, 8 repetitions along columns: thread t stores, for repetition r,
+// registers v[4r..4r+3] to (lane t/4, cols 8r+2(t%4), +1) and (lane t/4+8, the same cols).
+// `taddr` selects the first of the 16 lanes (within the warp's 32-lane quarter).
+__device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -200,13 +243,22 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- programmatic dependent launch -------------------------------------------------------
+// Block until every grid this one depends on (the previous kernel in the stream, when this
+// one was launched with programmatic stream serialization) has completed and its memory is
+// visible.  A no-op for an ordinary launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream (if launched with programmatic serialization) to be
+// scheduled before this grid finishes.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- named barrier over a subset of warps, with an AND vote ---------------------------
 __device__ __forceinline__ bool bar_and(int id, int nthreads, bool pred) {
     uint32_t out;
     asm volatile(
         "{\n\t.reg .pred pi, po;\n\t"
         "setp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.and.pred po, %2, %3, pi;\n\t"
+        "barrier.red.and.pred po, %2, %3, pi;\n\t"
         "selp.u32 %0, 1, 0, po;\n\t}"
         : "=r"(out)
         : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
@@ -214,8 +266,11 @@ __device__ __forceinline__ bool bar_and(int id, int nthreads, bool pred) {
     return out != 0;
 }
 __device__ __forceinline__ void bar_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// CTA-wide barrier that counts threads individually (non-.aligned form), so it is correct
+// even where the compiler has duplicated the call into divergent role branches.
+__device__ __forceinline__ void cta_sync_all() { asm volatile("barrier.sync 0;" ::: "memory"); }
 
 }  // namespace ptx
 }  // namespace lse

@@ -44,19 +44,26 @@ def _to_bf16(x: torch.Tensor) -> torch.Tensor:
 
 
 class Int8Linear(nn.Module):
-    """`y = x @ (weight * scale[:, None]).T` with int8 `weight [N, K]`, fp32 `scale [N]`."""
+    """`y = x @ (W * scale[:, None]).T` with int8 `W [N, K]`, fp32 `scale [N]`.
+
+    W is kept only in the tile-contiguous packed layout the kernels stream
+    (`ops.pack_weight`: every 128 x 128 tile is 16 KB of contiguous memory); `weight`
+    unpacks it on demand for inspection.
+    """
 
     def __init__(self, in_features: int, out_features: int, device=None):
         super().__init__()
         self.in_features = in_features
         self.out_features = out_features
-        self.register_buffer("weight", torch.zeros((out_features, in_features), dtype=torch.int8, device=device))
+        nbytes = ops.packed_weight_bytes(out_features, in_features) if device is not None and torch.device(device).type == "cuda" else 0
+        self.register_buffer("weight_packed", torch.zeros((nbytes,), dtype=torch.int8, device=device))
         self.register_buffer("scale", torch.ones((out_features,), dtype=torch.float32, device=device))
 
     @classmethod
     def from_quantized(cls, weight: torch.Tensor, scale: torch.Tensor) -> "Int8Linear":
-        mod = cls(weight.shape[1], weight.shape[0], device=weight.device)
-        mod.weight = weight.contiguous()
+        """From an int8 [N, K] weight and fp32 [N] scale already on the GPU."""
+        mod = cls(weight.shape[1], weight.shape[0], device=None)
+        mod.weight_packed = ops.pack_weight(weight)
         mod.scale = scale.to(torch.float32).contiguous()
         return mod
 
@@ -74,15 +81,19 @@ class Int8Linear(nn.Module):
         q, s = ops.quantize_per_channel(w)
         return cls.from_quantized(q, s)
 
+    @property
+    def weight(self) -> torch.Tensor:
+        return ops.unpack_weight(self.weight_packed, self.out_features, self.in_features)
+
     def dequantized(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         return (self.weight.to(torch.float32) * self.scale[:, None]).to(dtype)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = ops.int8_linear(_to_bf16(x), self.weight, self.scale)
+        y = ops.int8_linear_packed(_to_bf16(x), self.weight_packed, self.scale, self.out_features, self.in_features)
         return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
     def extra_repr(self) -> str:
-        return f"in_features={self.in_features}, out_features={self.out_features}, int8 per-channel"
+        return f"in_features={self.in_features}, out_features={self.out_features}, int8 per-channel, packed"
 
 
 class _SliceOf(nn.Module):
@@ -197,5 +208,5 @@ def int8_weight_bytes(model: nn.Module) -> int:
     total = 0
     for mod in model.modules():
         if isinstance(mod, Int8Linear):
-            total += mod.weight.numel() + 4 * mod.scale.numel()
+            total += mod.out_features * mod.in_features + 4 * mod.scale.numel()
     return total

@@ -25,17 +25,23 @@ from . import _lib
 
 __all__ = [
     "int8_linear",
+    "int8_linear_packed",
+    "pack_weight",
+    "unpack_weight",
+    "packed_weight_bytes",
     "quantize_per_channel",
     "workspace_for",
     "device_status",
     "ALGO_AUTO",
     "ALGO_GEMV",
     "ALGO_TCGEN05",
+    "ALGO_SKINNY",
 ]
 
 ALGO_AUTO = _lib.ALGO_AUTO
 ALGO_GEMV = _lib.ALGO_GEMV
 ALGO_TCGEN05 = _lib.ALGO_TCGEN05
+ALGO_SKINNY = _lib.ALGO_SKINNY
 
 _DTYPE_CODES = {torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16, torch.float32: _lib.DT_F32}
 
@@ -73,28 +79,20 @@ def workspace_for(device: torch.device, stream: torch.cuda.Stream | None = None)
     return ws
 
 
-def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
-                out: torch.Tensor | None = None, algo: int = ALGO_AUTO) -> torch.Tensor:
-    """y = bf16(x @ (weight * scale[:, None]).T): x bf16 [..., K] on CUDA, weight int8 [N, K]
-    contiguous, scale fp32 [N].  Returns bf16 [..., N] (or writes `out`, a [..., N] bf16
-    tensor whose last dim is contiguous)."""
-    if not (x.is_cuda and weight.is_cuda and scale.is_cuda):
+def _check_x(x: torch.Tensor, K: int, *tensors: torch.Tensor) -> None:
+    if not (x.is_cuda and all(t.is_cuda for t in tensors)):
         raise RuntimeError("int8_linear runs on CUDA only (no CPU fallback)")
-    if x.device != weight.device or x.device != scale.device:
-        raise ValueError(f"int8_linear: tensors on different devices ({x.device}, {weight.device}, {scale.device})")
+    if any(t.device != x.device for t in tensors):
+        raise ValueError(f"int8_linear: tensors on different devices ({x.device}, {[t.device for t in tensors]})")
     if x.dtype != torch.bfloat16:
         raise ValueError(f"int8_linear: x must be bfloat16, got {x.dtype}")
-    if weight.dtype != torch.int8 or weight.dim() != 2:
-        raise ValueError(f"int8_linear: weight must be int8 [N, K], got {weight.dtype} {tuple(weight.shape)}")
-    if scale.dtype != torch.float32 or scale.shape != (weight.shape[0],):
-        raise ValueError(f"int8_linear: scale must be float32 [{weight.shape[0]}], got {scale.dtype} {tuple(scale.shape)}")
-    N, K = weight.shape
     if x.shape[-1] != K:
         raise ValueError(f"int8_linear: x last dim {x.shape[-1]} != in_features {K}")
-    if not weight.is_contiguous():
-        raise ValueError("int8_linear: weight must be contiguous [N, K]")
     if K % 16 != 0:
         raise ValueError(f"int8_linear: in_features must be a multiple of 16, got {K}")
+
+
+def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, out, algo: int, packed: bool):
     lead = x.shape[:-1]
     x2 = x.reshape(-1, K)
     if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
@@ -113,11 +111,67 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
     ws = workspace_for(x.device, stream)
-    rc = _lib.load().lse_int8_linear_ex(
-        x2.data_ptr(), M, K, x2.stride(0), weight.data_ptr(), scale.data_ptr(), N,
-        y2.data_ptr(), y2.stride(0), ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
-    _lib.check(rc, "lse_int8_linear")
+    lib = _lib.load()
+    fn = lib.lse_int8_linear_packed if packed else lib.lse_int8_linear_ex
+    rc = fn(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N, y2.data_ptr(), y2.stride(0),
+            ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
+    _lib.check(rc, "lse_int8_linear_packed" if packed else "lse_int8_linear")
     return y
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                out: torch.Tensor | None = None, algo: int = ALGO_AUTO) -> torch.Tensor:
+    """y = bf16(x @ (weight * scale[:, None]).T): x bf16 [..., K] on CUDA, weight int8 [N, K]
+    contiguous (row-major), scale fp32 [N].  Returns bf16 [..., N] (or writes `out`, a
+    [..., N] bf16 tensor whose last dim is contiguous)."""
+    if weight.dtype != torch.int8 or weight.dim() != 2:
+        raise ValueError(f"int8_linear: weight must be int8 [N, K], got {weight.dtype} {tuple(weight.shape)}")
+    N, K = weight.shape
+    _check_x(x, K, weight, scale)
+    if scale.dtype != torch.float32 or scale.shape != (N,):
+        raise ValueError(f"int8_linear: scale must be float32 [{N}], got {scale.dtype} {tuple(scale.shape)}")
+    if not weight.is_contiguous():
+        raise ValueError("int8_linear: weight must be contiguous [N, K]")
+    return _launch(x, weight.data_ptr(), scale, N, K, out, algo, packed=False)
+
+
+def packed_weight_bytes(N: int, K: int) -> int:
+    return int(_lib.load().lse_int8_packed_weight_bytes(N, K))
+
+
+def pack_weight(q: torch.Tensor) -> torch.Tensor:
+    """int8 [N, K] (CUDA) -> the tile-contiguous packed layout (1-D int8), once at load."""
+    if not q.is_cuda or q.dtype != torch.int8 or q.dim() != 2:
+        raise ValueError("pack_weight: need a CUDA int8 [N, K] tensor")
+    if q.stride(1) != 1:
+        q = q.contiguous()
+    N, K = q.shape
+    out = torch.empty(packed_weight_bytes(N, K), dtype=torch.int8, device=q.device)
+    _ensure_device(q.device)
+    rc = _lib.load().lse_int8_pack_weight(q.data_ptr(), N, K, q.stride(0), out.data_ptr(),
+                                          torch.cuda.current_stream(q.device).cuda_stream)
+    _lib.check(rc, "lse_int8_pack_weight")
+    return out
+
+
+def unpack_weight(packed: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    out = torch.empty((N, K), dtype=torch.int8, device=packed.device)
+    _ensure_device(packed.device)
+    rc = _lib.load().lse_int8_unpack_weight(packed.data_ptr(), N, K, out.data_ptr(),
+                                            torch.cuda.current_stream(packed.device).cuda_stream)
+    _lib.check(rc, "lse_int8_unpack_weight")
+    return out
+
+
+def int8_linear_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: torch.Tensor, N: int, K: int,
+                       out: torch.Tensor | None = None, algo: int = ALGO_AUTO) -> torch.Tensor:
+    """int8_linear with the weight in the packed layout (`pack_weight`)."""
+    _check_x(x, K, w_packed, scale)
+    if w_packed.dtype != torch.int8 or w_packed.numel() != packed_weight_bytes(N, K) or not w_packed.is_contiguous():
+        raise ValueError(f"int8_linear_packed: w_packed must be the contiguous packed int8 buffer of [{N}, {K}]")
+    if scale.dtype != torch.float32 or scale.shape != (N,):
+        raise ValueError(f"int8_linear_packed: scale must be float32 [{N}]")
+    return _launch(x, w_packed.data_ptr(), scale, N, K, out, algo, packed=True)
 
 
 def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -1,0 +1,74 @@
+"""Launch one int8-linear shape a few times: the small, self-contained workload the ncu
+captures in profiles/ are taken on.
+
+    python -m llm_serving_engine_b200.profile_case --M 16 --shape gate_up --algo tcgen05 --launches 4
+
+Weights (in the packed layout the module stores) are rotated over enough distinct copies that each launch reads its weight from
+HBM, not from L2 (126 MB); the device footprint stays at a few GB.  Prints the CUDA-event
+time per launch of back-to-back launches captured in one CUDA graph (not meaningful under a
+profiler).  The graph is replayed twice: a capture of `--launches N` with ncu `-s N -c 1`
+profiles the first launch of the second replay.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import ops
+from .inputs import LLAMA3_8B_SHAPES, LLAMA3_70B_SHAPES, linear_bytes, linear_flops
+
+ALGOS = {"auto": ops.ALGO_AUTO, "gemv": ops.ALGO_GEMV, "tcgen05": ops.ALGO_TCGEN05, "skinny": ops.ALGO_SKINNY}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--M", type=int, default=16)
+    ap.add_argument("--shape", default="gate_up")
+    ap.add_argument("--model", choices=("8b", "70b"), default="8b")
+    ap.add_argument("--algo", choices=list(ALGOS), default="auto")
+    ap.add_argument("--launches", type=int, default=4)
+    ap.add_argument("--rowmajor", action="store_true", help="row-major W instead of the packed layout")
+    args = ap.parse_args(argv)
+    K, N = (LLAMA3_8B_SHAPES if args.model == "8b" else LLAMA3_70B_SHAPES)[args.shape]
+    copies = max(2, -(-3 * 128 * 2**20 // (N * K)))  # > 3x L2 of weights in rotation
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ws = [torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int8) for _ in range(copies)]
+    if not args.rowmajor:
+        ws = [ops.pack_weight(w) for w in ws]
+
+    def call(w):
+        if args.rowmajor:
+            ops.int8_linear(x, w, s, out=y, algo=algo)
+        else:
+            ops.int8_linear_packed(x, w, s, N, K, out=y, algo=algo)
+    s = torch.empty(N, device="cuda").uniform_(1e-4, 5e-4, generator=g)
+    x = torch.randn(args.M, K, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(args.M, N, device="cuda", dtype=torch.bfloat16)
+    algo = ALGOS[args.algo]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        call(ws[0])  # first call on the capture stream creates its workspace
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(args.launches):
+            call(ws[i % copies])
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.launches
+    print(f"M={args.M} {args.model}:{args.shape} K={K} N={N} algo={args.algo} {'row-major' if args.rowmajor else 'packed'}: {ms * 1e3:.2f} us/launch "
+          f"({linear_bytes(args.M, K, N) / ms / 1e6:.0f} GB/s, {linear_flops(args.M, K, N) / ms / 1e9:.1f} TFLOP/s, "
+          f"CUDA-graph launches)")
+    assert ops.device_status() == 0
+
+
+if __name__ == "__main__":
+    main()

@@ -39,6 +39,7 @@ __all__ = [
     "f32_to_bf16_bits",
     "ref_int8_linear",
     "ref_quantize",
+    "ref_pack_weight",
     "ref_fused_split",
     "ref_mlp",
     "parity_errors",
@@ -119,6 +120,21 @@ def ref_mlp(x: np.ndarray, q_gate, s_gate, q_up, s_up, q_down, s_down) -> np.nda
     u = ref_int8_linear(x, q_up, s_up)
     h = (g / (1.0 + np.exp(-g))) * u
     return ref_int8_linear(h, q_down, s_down)
+
+
+def ref_pack_weight(q: np.ndarray) -> np.ndarray:
+    """The build's fragment-major weight layout, restated with numpy (checker for the pack
+    kernel).  W is zero padded to multiples of 128 in both dimensions; for row block rb (16
+    rows) and 32-column chunk kc, the 512-byte chunk at (rb*KC + kc)*512 holds
+    W[rb*16 + rr*8 + r0][kc*32 + h*16 + 4*qq + e] at byte (4*r0 + qq)*16 + h*8 + rr*4 + e."""
+    N, K = q.shape
+    Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
+    pad = np.zeros((Np, Kp), dtype=np.int8)
+    pad[:N, :K] = q
+    RB, KC = Np // 16, Kp // 32
+    # axes: rb, rr, r0, kc, h, qq, e  ->  rb, kc, r0, qq, h, rr, e
+    v = pad.reshape(RB, 2, 8, KC, 2, 4, 4).transpose(0, 3, 2, 5, 4, 1, 6)
+    return (v.reshape(-1).view(np.uint8) ^ np.uint8(0x80)).view(np.int8).copy()
 
 
 def parity_errors(y: np.ndarray, ref: np.ndarray) -> tuple[float, bool, float]:

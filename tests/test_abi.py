@@ -69,6 +69,7 @@ def test_host_validation_rejects_before_launch():
     assert _call(x=24) == _lib.LSE_ERR_ALIGNMENT
     assert _call(w=8) == _lib.LSE_ERR_ALIGNMENT
     assert _call(algo=7) == _lib.LSE_ERR_INVALID_ARG
+    assert _call(algo=_lib.ALGO_SKINNY) == _lib.LSE_ERR_UNSUPPORTED  # skinny needs packed W
     lib = _lib.load()
     assert lib.lse_int8_quantize(None, 0, 4, 4, 4, None, None, None) == _lib.LSE_ERR_INVALID_ARG
     assert lib.lse_int8_quantize(16, 0, 4, 8, 4, 16, 16, None) == _lib.LSE_ERR_INVALID_ARG

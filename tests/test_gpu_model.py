@@ -39,8 +39,11 @@ def test_reference_fixture_projections(tiny, layer):
         y = mod(x.cuda())
         ref = ref_int8_linear(x.float().numpy(), tiny[f"{pre}.q"], tiny[f"{pre}.s"])
         check_parity(y, ref, pre)
-        # and the reference's own fp32 nn.Linear output, within bf16 input rounding
-        check_parity(y, tiny[f"{pre}.y"].astype(np.float64), pre + " vs reference")
+        # and the reference's own fp32 nn.Linear output on the fp32 activations: the kernel
+        # sees bf16-rounded x (relative error 2^-9 per element), so only the normwise bound
+        # applies to this comparison
+        yr = tiny[f"{pre}.y"].astype(np.float64)
+        assert np.max(np.abs(y.float().cpu().numpy() - yr)) / np.max(np.abs(yr)) <= 1e-2, pre
 
 
 @pytest.mark.parametrize("layer", [0, 1])
@@ -54,7 +57,8 @@ def test_reference_fixture_fused_qkv_and_mlp(tiny, layer):
     x = _bf16(tiny[f"{pre}.q_proj.x"]).cuda()
     outs = [qf(x), kf(x), vf(x)]
     for o, n in zip(outs, ("q_proj", "k_proj", "v_proj")):
-        check_parity(o, tiny[f"{pre}.{n}.y"].astype(np.float64), f"{pre}.{n} fused")
+        ref = ref_int8_linear(x.float().cpu().numpy(), tiny[f"{pre}.{n}.q"], tiny[f"{pre}.{n}.s"])
+        check_parity(o, ref, f"{pre}.{n} fused")
     gate_up = Int8Linear.from_quantized(
         torch.cat([torch.from_numpy(tiny[f"{pre}.gate_proj.q"]), torch.from_numpy(tiny[f"{pre}.up_proj.q"])]).cuda(),
         torch.cat([torch.from_numpy(tiny[f"{pre}.gate_proj.s"]), torch.from_numpy(tiny[f"{pre}.up_proj.s"])]).cuda())

@@ -20,7 +20,7 @@ from tests.gpu_helpers import Workspace, abi_linear, check_parity, oracle_rows
 
 pytestmark = pytest.mark.gpu
 
-ALGOS = {"gemv": _lib.ALGO_GEMV, "tcgen05": _lib.ALGO_TCGEN05, "auto": _lib.ALGO_AUTO}
+ALGOS = {"gemv": _lib.ALGO_GEMV, "tcgen05": _lib.ALGO_TCGEN05, "auto": _lib.ALGO_AUTO, "skinny": _lib.ALGO_SKINNY}
 
 
 @pytest.fixture(scope="module")
@@ -40,8 +40,8 @@ def _run_case(M, K, N, algo, ws, seed=0, sample=None):
 
 
 def test_config1_all_algos(ws):
-    for name, algo in ALGOS.items():
-        _run_case(8, 2048, 2048, algo, ws)
+    for name in ("gemv", "tcgen05", "auto"):
+        _run_case(8, 2048, 2048, ALGOS[name], ws)
     assert ws.counters_clear() and ws.guard_intact()
 
 
@@ -169,3 +169,84 @@ def test_ops_wrapper_leading_dims_and_errors():
 
 def test_device_status_clean():
     assert ops.device_status() == _lib.LSE_OK
+
+
+# ---- packed (tile-contiguous) weight layout ----------------------------------------------
+
+@pytest.mark.parametrize("N,K", [(8, 16), (200, 272), (4096, 4096), (300, 14336)])
+def test_pack_kernel_matches_layout_restatement(N, K):
+    from oracle.ref_linear import ref_pack_weight
+
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=torch.Generator().manual_seed(N + K))
+    packed = ops.pack_weight(w.cuda())
+    assert np.array_equal(packed.cpu().numpy(), ref_pack_weight(w.numpy()))
+    assert torch.equal(ops.unpack_weight(packed, N, K).cpu(), w)
+
+
+def _packed_call(x, packed, s, N, K, ws, algo, y=None, ldy=None):
+    M = x.shape[0]
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda") if y is None else y
+    ldy = y.stride(0) if ldy is None else ldy
+    rc = _lib.load().lse_int8_linear_packed(x.data_ptr(), M, K, x.stride(0), packed.data_ptr(), s.data_ptr(), N,
+                                            y.data_ptr(), ldy, ws.ptr, ws.nbytes, algo,
+                                            torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "lse_int8_linear_packed")
+    return y
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 16, 8), (3, 48, 17), (4, 4096, 6144), (9, 272, 200), (16, 144, 136),
+                                   (17, 14336, 4096), (32, 4096, 28672), (64, 14336, 4096), (65, 4112, 200),
+                                   (130, 1024, 640), (512, 4096, 4096)])
+@pytest.mark.parametrize("algo", ["skinny", "tcgen05", "auto"])
+def test_packed_path_parity(ws, M, K, N, algo):
+    if algo == "skinny" and M > 16:
+        pytest.skip("the skinny decode kernel serves M <= 16")
+    x, w, s = make_inputs(M, K, N, seed=M * 7 + K + N)
+    packed = ops.pack_weight(w.cuda())
+    xd, sd = x.cuda(), s.cuda()
+    y = _packed_call(xd, packed, sd, N, K, ws, ALGOS[algo])
+    torch.cuda.synchronize()
+    rows = np.arange(M) if M <= 64 else np.array([0, 1, M // 2, M - 1])
+    check_parity(y[torch.as_tensor(rows, device="cuda")], oracle_rows(x, w, s, rows), f"packed {algo} M={M} K={K} N={N}")
+    if algo == "tcgen05":
+        # packed and row-major tensor-core paths run the same arithmetic in the same order
+        y_rm = abi_linear(xd, w.cuda(), sd, ws, algo=_lib.ALGO_TCGEN05)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_rm)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+def test_packed_strided_and_layout_errors(ws):
+    M, K, N = 12, 256, 192
+    x, w, s = make_inputs(M, K, N, seed=4)
+    packed = ops.pack_weight(w.cuda())
+    big = torch.zeros(M, K + 64, dtype=torch.bfloat16, device="cuda")
+    big[:, :K] = x.cuda()
+    for algo in ("skinny", "tcgen05"):
+        ybig = torch.full((M, N + 24), 7.0, dtype=torch.bfloat16, device="cuda")
+        _packed_call(big, packed, s.cuda(), N, K, ws, ALGOS[algo], y=ybig)
+        torch.cuda.synchronize()
+        check_parity(ybig[:, :N], oracle_rows(x, w, s, np.arange(M)), f"packed strided {algo}")
+        assert torch.all(ybig[:, N:] == 7.0)
+    lib = _lib.load()
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.lse_int8_linear_packed(x.cuda().data_ptr(), M, K, K, packed.data_ptr(), s.cuda().data_ptr(), N,
+                                      y.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_GEMV, st) == _lib.LSE_ERR_UNSUPPORTED
+    x20 = torch.zeros(20, K, dtype=torch.bfloat16, device="cuda")
+    y20 = torch.empty(20, N, dtype=torch.bfloat16, device="cuda")
+    assert lib.lse_int8_linear_packed(x20.data_ptr(), 20, K, K, packed.data_ptr(), s.cuda().data_ptr(), N,
+                                      y20.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_SKINNY, st) == _lib.LSE_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("M", [1, 8, 9, 16])
+def test_skinny_deterministic_and_linear(ws, M):
+    K, N = 14336, 4096
+    x, w, s = make_inputs(M, K, N, seed=21)
+    packed = ops.pack_weight(w.cuda())
+    xd, sd = x.cuda(), s.cuda()
+    a = _packed_call(xd, packed, sd, N, K, ws, _lib.ALGO_SKINNY)
+    b = _packed_call(xd, packed, sd, N, K, ws, _lib.ALGO_SKINNY)
+    c = _packed_call(xd * 2, packed, sd, N, K, ws, _lib.ALGO_SKINNY)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(c, a * 2)
