@@ -70,9 +70,9 @@ struct Cfg {
     static constexpr int D_COL0 = 0;
     static constexpr int A_COL0 = ACC_BUFS * ACC_COLS;
     static_assert(A_COL0 + ASLOTS * A_SLOT_COLS <= TMEM_COLS, "TMEM budget");
-    // barrier block after the stages: full, empty (STAGES each), a_full, a_empty (ASLOTS),
+    // barrier block after the stages: full, empty (STAGES each), a_full (ASLOTS),
     // d_full, d_empty (ACC_BUFS), drain; then tmem address, abort flag, reduce flag.
-    static constexpr int NUM_BARS = 2 * STAGES + 2 * ASLOTS + 2 * ACC_BUFS + 1;
+    static constexpr int NUM_BARS = 2 * STAGES + ASLOTS + 2 * ACC_BUFS + 1;
     static constexpr int CTRL_BYTES = NUM_BARS * 8 + 16;
     static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + CTRL_BYTES;
     static constexpr uint32_t IDESC = ptx::idesc_bf16_f32(BN, NT);
@@ -215,8 +215,7 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     uint64_t *full = bars;
     uint64_t *empty = full + C::STAGES;
     uint64_t *a_full = empty + C::STAGES;
-    uint64_t *a_empty = a_full + ASLOTS;
-    uint64_t *d_full = a_empty + ASLOTS;
+    uint64_t *d_full = a_full + ASLOTS;
     uint64_t *d_empty = d_full + C::ACC_BUFS;
     uint64_t *drain = d_empty + C::ACC_BUFS;
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(drain + 1);
@@ -233,7 +232,6 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
         }
         for (int i = 0; i < ASLOTS; ++i) {
             ptx::mbar_init(ptx::smem_u32(&a_full[i]), NUM_CONV_WARPS / 2);
-            ptx::mbar_init(ptx::smem_u32(&a_empty[i]), 1);
         }
         for (int i = 0; i < C::ACC_BUFS; ++i) {
             ptx::mbar_init(ptx::smem_u32(&d_full[i]), 1);
@@ -341,8 +339,10 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const uint32_t ph = static_cast<uint32_t>((pos / C::STAGES) & 1);
                     const int as = static_cast<int>(apos % ASLOTS);
                     const uint32_t aph = static_cast<uint32_t>((apos / ASLOTS) & 1);
-                    if (!ptx::mbar_wait(ptx::smem_u32(&full[st]), ph, abort_flag) ||
-                        !ptx::mbar_wait(ptx::smem_u32(&a_full[as]), aph, abort_flag)) {
+                    // The converters arrive on a_full only after they observed the stage's
+                    // `full` barrier, so a_full also orders the x tile's arrival before the MMA.
+                    (void)ph;
+                    if (!ptx::mbar_wait(ptx::smem_u32(&a_full[as]), aph, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -358,8 +358,9 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         ptx::mma_bf16_ts(d_tmem + acc * NT, a0 + j * (UK / 2), b_desc, C::IDESC,
                                          (kb > s.k0 || j >= C::NACC) ? 1u : 0u);
                     }
+                    // One commit per stage: it frees the shared-memory stage (producer) and, seen
+                    // ASLOTS stages later, the stage's TMEM A slot (converters).
                     ptx::mma_commit(ptx::smem_u32(&empty[st]));
-                    ptx::mma_commit(ptx::smem_u32(&a_empty[as]));
                 }
                 if (!ok) break;
                 ptx::mma_commit(ptx::smem_u32(&d_full[buf]));
@@ -388,8 +389,17 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 const uint32_t ph = static_cast<uint32_t>((pos / C::STAGES) & 1);
                 const int as = static_cast<int>(pos % ASLOTS);
                 const uint32_t aph = static_cast<uint32_t>((pos / ASLOTS) & 1);
-                bool w_ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), ph, abort_flag) &&
-                            ptx::mbar_wait(ptx::smem_u32(&a_empty[as]), aph ^ 1, abort_flag);
+                // A slot `as` was last read by the MMAs of stage pos - ASLOTS; their completion is
+                // the last arrival on that stage's `empty` barrier (its converters arrived when
+                // they finished it).  That barrier's next phase needs this stage converted
+                // first, so its parity cannot alias.
+                (void)aph;
+                bool w_ok = ptx::mbar_wait(ptx::smem_u32(&full[st]), ph, abort_flag);
+                if (w_ok && pos >= ASLOTS) {
+                    const long long pp = pos - ASLOTS;
+                    w_ok = ptx::mbar_wait(ptx::smem_u32(&empty[pp % C::STAGES]),
+                                          static_cast<uint32_t>((pp / C::STAGES) & 1), abort_flag);
+                }
                 if (!__all_sync(0xffffffffu, w_ok)) {
                     ok = false;
                     break;
