@@ -15,6 +15,7 @@
  *   - `stream` is a cudaStream_t passed as void*; every launch goes to that stream, no
  *     entry point synchronizes, allocates device memory, or changes device settings, so
  *     each one can be captured in a CUDA graph (after lse_init on that device).
+ *     lse_int8_linear_packed_noalloc is outside this paragraph: its notes are its own.
  *   - Return value is an lse_status; nonzero means nothing was launched (argument errors)
  *     or the launch failed (LSE_ERR_CUDA).  The library never aborts or traps.
  *   - The caller owns every buffer.
@@ -141,6 +142,40 @@ const char *lse_last_cuda_error(void);
  * must be zeroed again before the next call.
  */
 int lse_device_status(int device, int reset);
+
+/*
+ * lse_int8_linear_packed_noalloc -- no counterpart in the reference: an addition of this
+ * library for callers that cannot allocate a workspace.
+ *
+ * Same result as lse_int8_linear_packed(..., LSE_ALGO_TCGEN05, ...), without the workspace
+ * arguments: the tensor-core kernel's scratch (stream-K arrival counters and partial tiles)
+ * is a fixed array of LSE_NOALLOC_SCRATCH_BYTES (12 MiB) per device, a static device
+ * variable of this library, so the call allocates nothing, neither device nor host memory.
+ * Who needs it: a binding that mirrors the engine's nn.Linear call (x, W, s -> y) has no
+ * workspace to pass and often no device allocator of its own (a plain C, ctypes or cgo
+ * host holding raw pointers another framework owns); and the engine hands about 95% of the
+ * HBM that is free after loading to its KV-cache pool (src/llm_serving_engine/config.py:
+ * 52-87), so a workspace allocated at the first projection call can find no memory.
+ *
+ *   x, w_packed, scale, y, strides: as lse_int8_linear_packed.
+ *   M: 1 .. LSE_NOALLOC_MAX_M (64) tokens -- the largest token tile whose partial tiles fit
+ *      the fixed array.  A larger M returns LSE_ERR_WORKSPACE before touching the GPU, with
+ *      the limit in lse_last_cuda_error(); use lse_int8_linear_packed with a workspace.
+ *      M == 0 or N == 0 is a no-op; K == 0 writes zeros.
+ *
+ * Every call on a device shares the one array, and the array keeps the last call's
+ * contents.  Calls that overlap on the GPU (different streams with no ordering between
+ * them) race on it and give wrong results: order them on one stream or with events.  Each
+ * call clears the arrival counters it uses (an asynchronous memset on `stream`) before its
+ * launch, so a call never depends on an earlier one having finished cleanly.  The first
+ * call on a device does the set-up (lse_init's work plus looking up the array's device
+ * address) and should come before any stream capture.
+ */
+#define LSE_NOALLOC_SCRATCH_BYTES 12582912
+#define LSE_NOALLOC_MAX_M 64
+int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                   const int8_t *w_packed, const float *scale, int64_t N,
+                                   void *y, int64_t ldy, void *stream);
 
 /* Library ABI version (LSE_ABI_VERSION). */
 #define LSE_ABI_VERSION 1

@@ -492,3 +492,93 @@ int lse_device_status(int device, int reset) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// lse_int8_linear_packed_noalloc: the tensor-core path with its scratch in a static device
+// array instead of a caller workspace, for callers that cannot allocate one (a binding of
+// the engine's x, W, s -> y call has no workspace argument, and the engine gives the HBM
+// left after loading to its KV-cache pool).  Allocates nothing.
+// ---------------------------------------------------------------------------------------
+namespace lse {
+namespace {
+
+// One array per device (module globals live in each device's context).  Without an
+// initializer it takes no space in the library file; its contents are never assumed: the
+// counters a call needs are cleared by that call, partial tiles are written before read.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[LSE_NOALLOC_SCRATCH_BYTES];
+
+struct NoAllocState {
+    std::once_flag once;
+    int status = LSE_ERR_CUDA;
+    void *ptr = nullptr;
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+// Device address of g_noalloc_scratch, looked up once per device with that device current
+// (the caller's current device: lse_int8_linear_packed_noalloc runs on it).
+int noalloc_scratch(int device, void **ptr) {
+    NoAllocState &s = g_noalloc[device];
+    std::call_once(s.once, [&] {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) { set_cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)"); return; }
+        if (!aligned16(p)) {
+            std::snprintf(t_last_error, sizeof(t_last_error), "no-alloc scratch at %p is not 16-byte aligned", p);
+            return;
+        }
+        s.ptr = p;
+        s.status = LSE_OK;
+    });
+    *ptr = s.ptr;
+    return s.status;
+}
+
+}  // namespace
+}  // namespace lse
+
+extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                              const int8_t *w_packed, const float *scale, int64_t N, void *y,
+                                              int64_t ldy, void *stream) {
+    // Host-side checks first (nothing touches the GPU before they pass): the same ones
+    // linear_impl makes, plus the token limit of the fixed scratch.
+    if (M > LSE_NOALLOC_MAX_M) {
+        std::snprintf(t_last_error, sizeof(t_last_error),
+                      "lse_int8_linear_packed_noalloc: M=%lld exceeds LSE_NOALLOC_MAX_M=%d (its fixed %d-byte "
+                      "scratch); use lse_int8_linear_packed with a workspace",
+                      static_cast<long long>(M), LSE_NOALLOC_MAX_M, LSE_NOALLOC_SCRATCH_BYTES);
+        return LSE_ERR_WORKSPACE;
+    }
+    if (M < 0 || N < 0 || K < 0) return LSE_ERR_INVALID_ARG;
+    if (M == 0 || N == 0) return LSE_OK;
+    if (!x || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
+    if (ldx < K || ldy < N) return LSE_ERR_INVALID_ARG;
+    if (N > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    void *scratch = nullptr;
+    rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (K > 0) {
+        const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
+        const size_t need = tc_workspace_bytes(pl.nt, pl.grid);
+        if (need > static_cast<size_t>(LSE_NOALLOC_SCRATCH_BYTES)) {  // only on parts with > 160 SMs
+            std::snprintf(t_last_error, sizeof(t_last_error),
+                          "lse_int8_linear_packed_noalloc: this shape needs %zu scratch bytes, the fixed array "
+                          "holds %d",
+                          need, LSE_NOALLOC_SCRATCH_BYTES);
+            return LSE_ERR_WORKSPACE;
+        }
+        // The stream-K arrival counters must start at zero; partial tiles need no clearing.
+        const long long sk_tiles = static_cast<long long>(pl.tiles) - pl.dp_tiles;
+        if (sk_tiles > 0) {
+            const cudaError_t e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(sk_tiles) * sizeof(int), st);
+            if (e != cudaSuccess) { set_cuda_error(e, "cudaMemsetAsync(no-alloc counters)"); return LSE_ERR_CUDA; }
+        }
+    }
+    return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, scratch, LSE_NOALLOC_SCRATCH_BYTES,
+                       LSE_ALGO_TCGEN05, true, stream);
+}
