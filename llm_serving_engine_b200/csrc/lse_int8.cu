@@ -56,19 +56,6 @@ cudaError_t set_tc_attrs() {
                                 tc::Cfg<NT>::SMEM_BYTES);
 }
 
-template <int MT, int KW>
-cudaError_t set_skinny_attr() {
-    return cudaFuncSetAttribute(skinny_i8_kernel<MT, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                SkinnyCfg<KW>::SMEM);
-}
-cudaError_t set_skinny_attrs() {
-    cudaError_t e = set_skinny_attr<1, 4>();
-    if (e == cudaSuccess) e = set_skinny_attr<2, 4>();
-    if (e == cudaSuccess) e = set_skinny_attr<1, 16>();
-    if (e == cudaSuccess) e = set_skinny_attr<2, 16>();
-    return e;
-}
-
 int init_device(int device) {
     if (device < 0 || device >= kMaxDevices) return LSE_ERR_INVALID_ARG;
     DeviceState &d = g_dev[device];
@@ -83,7 +70,6 @@ int init_device(int device) {
         if (e == cudaSuccess) e = set_tc_attrs<32>();
         if (e == cudaSuccess) e = set_tc_attrs<64>();
         if (e == cudaSuccess) e = set_tc_attrs<128>();
-        if (e == cudaSuccess) e = set_skinny_attrs();
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
         std::call_once(g_encode_once, [] {
             void *fn = nullptr;
@@ -264,37 +250,59 @@ int run_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, 
     return LSE_OK;
 }
 
-template <int MT, int KW>
+template <int MT, int KW, int R, int U, bool BF16, int MINB>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, cudaStream_t st) {
-    dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
+    const int64_t row_blocks = (N + 15) / 16;
+    dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, grid, dim3(KW * 32), SkinnyCfg<KW>::SMEM, st);
-    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW>, static_cast<const __nv_bfloat16 *>(x), ldx,
+    launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
+    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB>, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
                               static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)));
 }
 
-int num_sms_of_current() {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || g_dev[dev].num_sms <= 0) return 148;
-    return g_dev[dev].num_sms;
+// Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):
+//   * many row blocks (N/16 >= 2 x SMs: QKV, gate_up): CTAs of 8 warps on two row blocks,
+//     so every activation load serves 32 weight rows;
+//   * few row blocks (O, down): CTAs of 16 warps, one row block (two for M > 8, where the
+//     activation loads, not the weight stream, would otherwise saturate L1);
+//   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
+//     are).
+// LSE_SKINNY_VARIANT=<0..4> pins one configuration for tuning runs.
+int skinny_variant() {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_SKINNY_VARIANT");
+        return e ? std::atoi(e) : -1;
+    }();
+    return v;
+}
+
+template <int MT>
+cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp,
+                             const float *scale, int64_t N, void *y, int64_t ldy, int num_sms, cudaStream_t st) {
+    if (variant < 0) variant = ((N + 15) / 16 >= 2 * static_cast<int64_t>(num_sms)) ? 1 : 0;
+    constexpr bool BF = MT == 2;
+    switch (variant) {
+        case 1: return launch_skinny<MT, 8, 2, 4, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        case 4: return launch_skinny<MT, 16, 2, 4, BF, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        default:
+            if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            else return launch_skinny<2, 16, 2, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+    }
 }
 
 constexpr int64_t kSkinnyMaxM = 16;  // the decode kernel's token range (two 8-token tiles)
 
 int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale, int64_t N,
-               void *y, int64_t ldy, cudaStream_t st) {
+               void *y, int64_t ldy, int num_sms, cudaStream_t st) {
     if (M > kSkinnyMaxM) return LSE_ERR_UNSUPPORTED;
-    // Few row blocks (N / 16 below ~2 per SM): split K over 16 warps so every SM still holds
-    // enough warps (and bytes in flight); otherwise 4 warps per CTA and more CTAs per SM.
-    const bool wide = (N + 15) / 16 < 2 * num_sms_of_current();
-    cudaError_t e;
-    if (M <= 8) e = wide ? launch_skinny<1, 16>(x, M, K, ldx, wp, scale, N, y, ldy, st)
-                         : launch_skinny<1, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-    else e = wide ? launch_skinny<2, 16>(x, M, K, ldx, wp, scale, N, y, ldy, st)
-                  : launch_skinny<2, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+    const int variant = skinny_variant();
+    cudaError_t e = M <= 8 ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
+                           : launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -369,7 +377,7 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
     }
     if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed);
     if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);
-    if (algo == LSE_ALGO_SKINNY) return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, st);
+    if (algo == LSE_ALGO_SKINNY) return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, g_dev[dev].num_sms, st);
 
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))

@@ -1,31 +1,30 @@
-// Skinny int8 weight-only GEMM for decode (M <= 32 tokens), on the fragment-major packed
+// Skinny int8 weight-only GEMM for decode (M <= 16 tokens), on the fragment-major packed
 // weights of pack_w.cuh.
 //
 //   y[m, n] = s[n] * sum_k x[m, k] * w[n, k]
 //
-// Decode is bound by the weight stream (2 flop per weight byte per token), so the kernel is
-// shaped to keep HBM busy rather than to maximise tensor throughput:
-//   * one CTA of KW warps owns a block of 16 output channels over all of K; each warp
-//     streams its share of the block's contiguous 16*Kp-byte run through a private ring of
-//     4 KB slots in shared memory, each slot filled by ONE 1-D bulk copy issued by lane 0
-//     and completed on an mbarrier: the bytes in flight cost no registers and the lanes do
-//     no copy bookkeeping (the integer pipe, not HBM, bounded a per-lane-copy variant);
-//   * every lane's 16 bytes of a 512-byte chunk ARE two 16x16 A fragments (pack_w.cuh),
-//     widened to fp16 in registers with one byte permute + one fp16 subtraction per pair
-//     (exact: the packed bytes are biased, u = v + 128, and fp16 holds 1024 + u) and fed to
-//     16x8x16 warp MMAs with fp32 accumulation - every warp issues its own MMAs, so no
-//     single thread serialises the stream.  The integer pipe runs at half rate and was the
-//     bound with a bf16 widening (3 integer ops per pair, bf16 has 7 mantissa bits); the
-//     activations are rounded bf16 -> fp16 per fragment (exact for |x| in [2^-14, 65504],
-//     saturating beyond), which costs less than it saves;
-//   * the activation fragments of a slot are read from global memory (L1/L2-resident:
-//     every CTA on the SM reads the same rows) before the slot's weights are waited for, in
-//     the K order the packed layout implies;
-//   * the K split is reduced across the warps through shared memory, in a fixed order, and
-//     the per-channel scale is applied once to each reduced sum.
-// No workspace, no cross-CTA traffic.  The ring is filled before waiting on the previous
-// kernel (programmatic dependent launch): weights never depend on it.  Every mbarrier wait
-// is bounded; a wait that gives up records LSE_ERR_DEVICE_TIMEOUT and ends the CTA.
+// Decode is bound by the weight stream (2 flop per weight byte per token).  The kernel is
+// shaped so that nothing but HBM bounds it, and so that consecutive projections overlap:
+//   * one CTA of KW warps owns R blocks of 16 output channels over all of K; warp w takes
+//     every KW-th chunk (32 columns) of each block;
+//   * every lane loads its 16 bytes of a 512-byte chunk straight into registers with one
+//     128-bit streaming load (L1 no-allocate, L2 evict-first): those bytes ARE two 16x16 A
+//     fragments of a 16x8x16 warp MMA (pack_w.cuh), so there is no shared-memory staging,
+//     no copy bookkeeping and no wait on a barrier.  U chunks per block are kept in flight
+//     per lane (issued before the previous kernel is waited for: weights never depend on
+//     it);
+//   * weights are widened in registers - to fp16 with one byte permute + one fp16
+//     subtraction per pair (exact: the bytes are biased, u = v + 128, and fp16 holds
+//     1024 + u), with the activations rounded bf16 -> fp16 per fragment (exact for |x| in
+//     [2^-14, 65504], saturating beyond); or, with BF16 set, to bf16 (two logic ops + one
+//     bf16 subtraction per pair, exact) against the bf16 activations as they are - and fed
+//     to warp MMAs with fp32 accumulation;
+//   * the K split is reduced across the warps through shared memory in a fixed order and
+//     the per-channel scale is applied once to each reduced sum (deterministic);
+//   * the CTA signals programmatic launch completion on entry: it holds only a small
+//     reduction buffer in shared memory, so the next kernel's CTAs become resident as soon
+//     as registers free up and start their own weight streams under this kernel's tail.
+// No workspace, no cross-CTA traffic, no spin-waits.
 #pragma once
 
 #include <type_traits>
@@ -34,35 +33,54 @@
 
 namespace lse {
 
-// D (16x8 fp32) += A (16x16 f16, row) * B (16x8 f16, col).
+// D (16x8 fp32) += A (16x16, row) * B (16x8, col), fp16 or bf16 operands.
+template <bool BF16>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    if constexpr (BF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
-// Per warp: a ring of RS slots, each SC chunks (SC * 512 contiguous bytes of the warp's share
-// of the row block).  Small grids (few row blocks) split K over 16 warps, large grids over 4;
-// either way ~100-200 KB of weights per SM are in flight.
-template <int KW>
-struct SkinnyCfg {
-    static constexpr int SC = 8;                 // chunks per slot (4 KB)
-    static constexpr int RS = KW >= 16 ? 2 : 4;  // slots per warp
-    static constexpr int SLOT_BYTES = SC * 512;
-    static constexpr int RING_BYTES = RS * SLOT_BYTES;
-    static constexpr int SMEM = KW * RING_BYTES + KW * RS * 8 + 16;
-};
+// 16 weight bytes of one lane: streaming load, no L1 allocation, L2 evict-first (each
+// weight byte is read exactly once per call).  Volatile, so the compiler keeps every load
+// where it is issued - ahead of the wait on the previous kernel and U chunks ahead of its
+// use - instead of sinking it to the first use.
+__device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p), "l"(policy));
+    return r;
+}
 
-template <int MT, int KW>  // token tiles of 8 per CTA, warps splitting K
-__global__ void __launch_bounds__(KW * 32)
+// MT token tiles of 8 per CTA (M <= 8 * MT), KW warps splitting K, R row blocks per CTA
+// (sharing every activation load), U chunks per row block in flight per lane, BF16 selects
+// the bf16 MMA.
+//
+// Bytes in flight per SM (resident warps x U x 512), then instructions per chunk, bound this
+// kernel, so the main path is written for both: warp w streams a contiguous slice of the
+// row block's chunks in whole groups of U, with every load at a constant offset from a
+// pointer that moves once per group and no per-chunk predicate; the groups are visited in
+// an order rotated per CTA, so the CTAs resident together read different offsets of their
+// row blocks.  A slice that is not a whole number of groups (ragged K) takes a
+// bounds-checked path.
+template <int MT, int KW, int R, int U, bool BF16, int MINB>
+__global__ void __launch_bounds__(KW * 32, MINB)
 skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
                  __nv_bfloat16 *__restrict__ y, int64_t ldy, int Kp) {
-    using C = SkinnyCfg<KW>;
-    constexpr int SC = C::SC, RS = C::RS;
-    const int rb = blockIdx.x;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int rg = blockIdx.x;
     const int m0 = blockIdx.y * MT * 8;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = lane >> 2, q = lane & 3;
@@ -70,120 +88,169 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     const int kc_real = (K + 31) >> 5;  // chunks holding real columns
     const int per = (kc_real + KW - 1) / KW;
     const int c0 = min(kc_real, warp * per), c1 = min(kc_real, c0 + per);
-    const int nslots = (c1 - c0 + SC - 1) / SC;
-    const int8_t *wsrc = wp + (static_cast<int64_t>(rb) * kc_all + c0) * 512;
+    const int nch = c1 - c0;
+    // Whole groups, and every column < K (only the last chunk of the row can be partial).
+    const bool fast = nch > 0 && nch % U == 0 && c1 * 32 <= K;
+    const int ng = nch / U;
+    const int rot = fast ? rg % ng : 0;
 
-    extern __shared__ __align__(128) uint8_t skinny_smem[];
-    uint8_t *ring = skinny_smem + warp * C::RING_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(skinny_smem + KW * C::RING_BYTES) + warp * RS;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(skinny_smem + KW * C::RING_BYTES + KW * RS * 8);
+    const uint64_t pol = ptx::policy_evict_first();
+    // Row block rg*R + r (padded row blocks past N hold zeros) at wbase + r * rb_bytes.
+    const int64_t rb_bytes = static_cast<int64_t>(kc_all) * 512;
+    const int8_t *const wbase = wp + (static_cast<int64_t>(rg) * R * kc_all + c0) * 512 + lane * 16;
+    const int8_t *gp = wbase + rot * (U * 512);
+    uint4 wb[U][R];
+#pragma unroll
+    for (int j = 0; j < U; ++j)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            wb[j][r] = (fast || j < nch) ? ld_weight16(gp + r * rb_bytes + j * 512, pol) : make_uint4(0, 0, 0, 0);
 
-    auto issue = [&](int g) {  // lane 0 only: weights of slot g -> ring slot g % RS
-        const uint32_t bar = ptx::smem_u32(&bars[g % RS]);
-        const uint32_t nb = static_cast<uint32_t>(min(SC, c1 - c0 - g * SC) * 512);
-        ptx::mbar_arrive_expect_tx(bar, nb);
-        ptx::bulk_load(ptx::smem_u32(ring + (g % RS) * C::SLOT_BYTES), wsrc + static_cast<int64_t>(g) * C::SLOT_BYTES,
-                       nb, bar, ptx::policy_evict_first());
-    };
-    if (threadIdx.x == 0) *abort_flag = 0;
-    if (lane == 0) {
-        for (int i = 0; i < RS; ++i) ptx::mbar_init(ptx::smem_u32(&bars[i]), 1);
-        ptx::fence_mbar_init();
-        // Weights never depend on the previous kernel: fill the ring before waiting for it.
-        for (int g = 0; g < RS && g < nslots; ++g) issue(g);
-    }
-    __syncthreads();
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
 
     // Activation rows this lane feeds as the B fragment of token tile t: token m0 + 8t + r0,
-    // K quad 4q..4q+3 of each 16-column step (rows past M are never read and count as zero).
-    const __nv_bfloat16 *xrow[MT];
-    bool xok[MT];
+    // K quad 4q..4q+3 of each 16-column step.  A token past M reads the last real row
+    // instead: its MMA column is independent of the others and is never stored.
+    const __nv_bfloat16 *xbase[MT];
+    const __nv_bfloat16 *xp[MT];
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
-        const int m = m0 + 8 * t + r0;
-        xok[t] = m < M;
-        xrow[t] = x + static_cast<int64_t>(xok[t] ? m : 0) * ldx + 4 * q + static_cast<int64_t>(c0) * 32;
+        const int m = min(m0 + 8 * t + r0, M - 1);
+        xbase[t] = x + static_cast<int64_t>(m) * ldx + 4 * q + c0 * 32;
+        xp[t] = xbase[t] + rot * (U * 32);
     }
 
-    float acc[2][MT][4];  // two accumulator sets alternate by chunk parity
+    // With a single MMA chain (R * MT == 1) alternate two accumulator sets by chunk parity.
+    constexpr int NACC = R * MT == 1 ? 2 : 1;
+    float acc[NACC][R][MT][4];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < NACC; ++u)
 #pragma unroll
-        for (int t = 0; t < MT; ++t) acc[u][t][0] = acc[u][t][1] = acc[u][t][2] = acc[u][t][3] = 0.f;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < MT; ++t) acc[u][r][t][0] = acc[u][r][t][1] = acc[u][r][t][2] = acc[u][r][t][3] = 0.f;
 
-    const int kcols = K - c0 * 32;  // real columns from this warp's first chunk on
-    bool ok = true;
-    // One slot: activation fragments first (requested before waiting for the weights), then
-    // widen + MMA per chunk.  FULL slots (all SC chunks real, every column < K) skip the
-    // per-chunk bounds predicates.
-    auto run_slot = [&](int g, auto full_tag) -> bool {
-        constexpr bool FULL = decltype(full_tag)::value;
-        const int nch = FULL ? SC : min(SC, c1 - c0 - g * SC);
-        uint32_t xs[SC][MT][2][2];  // f16x2 B fragments
+    // One chunk: B fragments from the two activation quads, A fragments widened from the
+    // lane's 16 weight bytes of each row block, two 16x8x16 MMAs per token tile and block.
+    auto compute = [&](int j, const uint4 (&wr)[R], const uint2 (&xv)[MT][2]) {
+        uint32_t bx[MT][2][2];
 #pragma unroll
-        for (int j = 0; j < SC; ++j)
+        for (int t = 0; t < MT; ++t)
 #pragma unroll
-            for (int t = 0; t < MT; ++t)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int col = (g * SC + j) * 32 + h * 16;  // relative to chunk c0
-                    uint2 v = make_uint2(0, 0);
-                    if (xok[t] && (FULL || (j < nch && col < kcols)))
-                        v = __ldg(reinterpret_cast<const uint2 *>(xrow[t] + col));
-                    xs[j][t][h][0] = bf16x2_to_f16x2(v.x);
-                    xs[j][t][h][1] = bf16x2_to_f16x2(v.y);
-                }
-        const bool landed = ptx::mbar_wait(ptx::smem_u32(&bars[g % RS]), (g / RS) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, landed)) return false;
-        const uint8_t *sl = ring + (g % RS) * C::SLOT_BYTES + lane * 16;
-#pragma unroll
-        for (int j = 0; j < SC; ++j) {
-            if (FULL || j < nch) {
-                const uint4 wv = *reinterpret_cast<const uint4 *>(sl + j * 512);
-                const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    // words[2h] = row r0, words[2h+1] = row r0+8; K quad 4q..4q+3 each.  A
-                    // 16-column step past K holds zero weights and zero activations.
-                    uint32_t r_lo01, r_lo23, r_hi01, r_hi23;
-                    u8x4_to_f16x4(words[2 * h], r_lo01, r_lo23);
-                    u8x4_to_f16x4(words[2 * h + 1], r_hi01, r_hi23);
-                    const uint32_t a[4] = {r_lo01, r_hi01, r_lo23, r_hi23};
-#pragma unroll
-                    for (int t = 0; t < MT; ++t) mma_16816(acc[j & 1][t], a, xs[j][t][h][0], xs[j][t][h][1]);
+            for (int h = 0; h < 2; ++h) {
+                if constexpr (BF16) {
+                    bx[t][h][0] = xv[t][h].x;
+                    bx[t][h][1] = xv[t][h].y;
+                } else {
+                    bx[t][h][0] = bf16x2_to_f16x2(xv[t][h].x);
+                    bx[t][h][1] = bf16x2_to_f16x2(xv[t][h].y);
                 }
             }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const uint32_t words[4] = {wr[r].x, wr[r].y, wr[r].z, wr[r].w};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                // words[2h] = row r0, words[2h+1] = row r0+8; K quad 4q..4q+3 each.
+                uint32_t lo01, lo23, hi01, hi23;
+                if constexpr (BF16) {
+                    u8x4_to_bf16x4(words[2 * h], lo01, lo23);
+                    u8x4_to_bf16x4(words[2 * h + 1], hi01, hi23);
+                } else {
+                    u8x4_to_f16x4(words[2 * h], lo01, lo23);
+                    u8x4_to_f16x4(words[2 * h + 1], hi01, hi23);
+                }
+                const uint32_t a[4] = {lo01, hi01, lo23, hi23};
+#pragma unroll
+                for (int t = 0; t < MT; ++t)
+                    mma_16816<BF16>(acc[NACC == 2 ? (j & 1) : 0][r][t], a, bx[t][h][0], bx[t][h][1]);
+            }
         }
-        __syncwarp();  // every lane has read the slot: lane 0 may refill it
-        if (lane == 0 && g + RS < nslots) issue(g + RS);
-        return true;
     };
-    for (int g = 0; g < nslots && ok; ++g) {
-        const bool full = (g + 1) * SC <= c1 - c0 && (g + 1) * SC * 32 <= kcols;
-        ok = full ? run_slot(g, std::true_type{}) : run_slot(g, std::false_type{});
-    }
-    if (!ok && lane == 0) {
-        // a wait gave up: let this warp's outstanding copies land before shared memory is freed
-        for (int g = 0; g < nslots; ++g) ptx::mbar_drain(ptx::smem_u32(&bars[g % RS]), (g / RS) & 1);
-    }
+    // One whole group at gp / xp; with REFILL, slot j is reloaded from the next group (np)
+    // as soon as it has been read.
+    auto group = [&](const int8_t *np, auto refill_tag) {
+        constexpr bool REFILL = decltype(refill_tag)::value;
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            uint4 w[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                w[r] = wb[j][r];
+                if constexpr (REFILL) wb[j][r] = ld_weight16(np + r * rb_bytes + j * 512, pol);
+            }
+            uint2 xv[MT][2];
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                xv[t][0] = __ldg(reinterpret_cast<const uint2 *>(xp[t] + j * 32));
+                xv[t][1] = __ldg(reinterpret_cast<const uint2 *>(xp[t] + j * 32 + 16));
+            }
+            compute(j, w, xv);
+        }
+    };
 
-    // The grid runs in several waves: let the next kernel's CTAs in only as this CTA winds
-    // down, so they never take the slots of this kernel's later waves.
-    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (fast) {
+        int gi = rot;  // slice group being processed
+        for (int g = 0; g < ng; ++g) {
+            const bool wrap = gi + 1 == ng;  // the next group in the rotated order is group 0
+            const int8_t *np = wrap ? wbase : gp + U * 512;
+            if (g + 1 < ng) group(np, std::true_type{});
+            else group(np, std::false_type{});
+            gp = np;
+#pragma unroll
+            for (int t = 0; t < MT; ++t) xp[t] = wrap ? xbase[t] : xp[t] + U * 32;
+            gi = wrap ? 0 : gi + 1;
+        }
+    } else {
+        // Ragged slice: chunk by chunk with bounds checks; a 16-column half past K holds zero
+        // weights and its activations are not read.
+        const int kcols = K - c0 * 32;
+        for (int c = 0; c < nch; c += U) {
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                if (c + j < nch) {
+                    uint4 w[R];
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        w[r] = wb[j][r];
+                        if (c + j + U < nch) wb[j][r] = ld_weight16(gp + r * rb_bytes + (U + j) * 512, pol);
+                    }
+                    uint2 xv[MT][2];
+#pragma unroll
+                    for (int t = 0; t < MT; ++t)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int col = (c + j) * 32 + h * 16;
+                            xv[t][h] = col < kcols ? __ldg(reinterpret_cast<const uint2 *>(xp[t] + j * 32 + h * 16))
+                                                   : make_uint2(0, 0);
+                        }
+                    compute(j, w, xv);
+                }
+            }
+            gp += U * 512;
+#pragma unroll
+            for (int t = 0; t < MT; ++t) xp[t] += U * 32;
+        }
+    }
 
     // K-split reduction across the accumulator sets and warps (fixed order), scale, store.
-    __shared__ float red[KW][MT][4][32];
+    __shared__ float red[KW][R][MT][4][32];
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) red[warp][t][j][lane] = acc[0][t][j] + acc[1][t][j];
+        for (int t = 0; t < MT; ++t)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float v = acc[0][r][t][j];
+                if constexpr (NACC == 2) v += acc[1][r][t][j];
+                red[warp][r][t][j][lane] = v;
+            }
     __syncthreads();
-    // warps 0-3: warp j finishes accumulator register j of every token tile: row r0 + 8*(j>>1),
-    // token 2q + (j & 1) of the tile (16x8 accumulator layout).
-    if (warp < 4) {
-        const int j = warp;
-        const int n = rb * 16 + r0 + 8 * (j >> 1);
+    // warp (r, j) = (warp >> 2, warp & 3) finishes accumulator register j of row block r:
+    // row r0 + 8*(j>>1), token 2q + (j & 1) of each tile (16x8 accumulator layout).
+    if (warp < 4 * R) {
+        const int r = warp >> 2, j = warp & 3;
+        const int n = (rg * R + r) * 16 + r0 + 8 * (j >> 1);
         if (n < N) {
             const float sc = __ldg(scale + n);
 #pragma unroll
@@ -192,7 +259,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                 if (m < M) {
                     float v = 0.f;
 #pragma unroll
-                    for (int w = 0; w < KW; ++w) v += red[w][t][j][lane];
+                    for (int w = 0; w < KW; ++w) v += red[w][r][t][j][lane];
                     y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(v * sc);
                 }
             }
@@ -201,3 +268,4 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 }
 
 }  // namespace lse
+

@@ -268,6 +268,10 @@ __device__ __forceinline__ bool bar_and(int id, int nthreads, bool pred) {
 __device__ __forceinline__ void bar_sync(int id, int nthreads) {
     asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrive on named barrier `id` without waiting (counts toward `nthreads`).
+__device__ __forceinline__ void bar_arrive(int id, int nthreads) {
+    asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 // CTA-wide barrier that counts threads individually (non-.aligned form), so it is correct
 // even where the compiler has duplicated the call into divergent role branches.
 __device__ __forceinline__ void cta_sync_all() { asm volatile("barrier.sync 0;" ::: "memory"); }

@@ -195,6 +195,7 @@ def _packed_call(x, packed, s, N, K, ws, algo, y=None, ldy=None):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 16, 8), (3, 48, 17), (4, 4096, 6144), (9, 272, 200), (16, 144, 136),
+                                   (2, 4096, 28672), (16, 4096, 28672), (5, 8192, 1040), (12, 8208, 272),
                                    (17, 14336, 4096), (32, 4096, 28672), (64, 14336, 4096), (65, 4112, 200),
                                    (130, 1024, 640), (512, 4096, 4096)])
 @pytest.mark.parametrize("algo", ["skinny", "tcgen05", "auto"])
@@ -239,9 +240,9 @@ def test_packed_strided_and_layout_errors(ws):
                                       y20.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_SKINNY, st) == _lib.LSE_ERR_UNSUPPORTED
 
 
+@pytest.mark.parametrize("K,N", [(14336, 4096), (4096, 28672)])
 @pytest.mark.parametrize("M", [1, 8, 9, 16])
-def test_skinny_deterministic_and_linear(ws, M):
-    K, N = 14336, 4096
+def test_skinny_deterministic_and_linear(ws, M, K, N):
     x, w, s = make_inputs(M, K, N, seed=21)
     packed = ops.pack_weight(w.cuda())
     xd, sd = x.cuda(), s.cuda()
