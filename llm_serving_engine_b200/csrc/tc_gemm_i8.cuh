@@ -25,9 +25,10 @@
 // (data-parallel part); the remaining tiles are cut into 128-K units spread evenly over the
 // G CTAs (stream-K part).  A tile whose K range is split across CTAs is finished by
 // whichever CTA arrives last on the tile's counter: every segment writes its fp32 partial
-// to the workspace, bumps the counter, and the last one sums all partials in segment order
-// (deterministic), applies the scale, stores y and re-zeroes the counter.  No CTA ever
-// waits for another CTA.
+// to the workspace and bumps the counter; the last one re-zeroes the counter and, once its
+// role loops are done, sums all partials in segment order (deterministic) with all 512
+// threads and every segment's loads in flight together, applies the scale and stores y.
+// No CTA ever waits for another CTA.
 //
 // Every mbarrier wait is bounded (tc_ptx.cuh: mbar_wait); on a timeout the CTA raises an
 // abort flag, records LSE_ERR_DEVICE_TIMEOUT, drains its own copies and MMAs, frees TMEM
@@ -71,9 +72,10 @@ struct Cfg {
     static constexpr int A_COL0 = ACC_BUFS * ACC_COLS;
     static_assert(A_COL0 + ASLOTS * A_SLOT_COLS <= TMEM_COLS, "TMEM budget");
     // barrier block after the stages: full, empty (STAGES each), a_full (ASLOTS),
-    // d_full, d_empty (ACC_BUFS), drain; then tmem address, abort flag, reduce flag.
+    // d_full, d_empty (ACC_BUFS), drain; then tmem address, abort flag and the pending
+    // stream-K reductions (count + 2 x {tile, first CTA, last CTA}).
     static constexpr int NUM_BARS = 2 * STAGES + ASLOTS + 2 * ACC_BUFS + 1;
-    static constexpr int CTRL_BYTES = NUM_BARS * 8 + 16;
+    static constexpr int CTRL_BYTES = NUM_BARS * 8 + 48;
     static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + CTRL_BYTES;
     static constexpr uint32_t IDESC = ptx::idesc_bf16_f32(BN, NT);
 };
@@ -220,7 +222,7 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     uint64_t *drain = d_empty + C::ACC_BUFS;
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(drain + 1) + 1;
-    volatile int *reduce_flag = reinterpret_cast<volatile int *>(drain + 1) + 2;
+    volatile int *pending = reinterpret_cast<volatile int *>(drain + 1) + 2;  // [0] count, then triples
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -239,7 +241,7 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
         }
         ptx::mbar_init(ptx::smem_u32(drain), 1);
         *abort_flag = 0;
-        *reduce_flag = 0;
+        pending[0] = 0;
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tmap_w);
         ptx::prefetch_tmap(&tmap_x);
@@ -548,62 +550,15 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 ptx::bar_sync(EPI_BAR, NUM_EPI_WARPS * 32);
                 if (threadIdx.x == WARP_EPI0 * 32) {
                     const int old = atomicAdd(p.counters + ts, 1);
-                    const int last = (old == c_last - c_first);
-                    if (last) p.counters[ts] = 0;  // every segment has arrived: re-arm for next launch
-                    *reduce_flag = last;
-                }
-                ptx::bar_sync(EPI_BAR, NUM_EPI_WARPS * 32);
-                const bool last = *reduce_flag != 0;
-                ptx::bar_sync(EPI_BAR, NUM_EPI_WARPS * 32);  // flag read by all before reuse
-                if (last) {
-                    __threadfence();
-                    // Sum the segments' partials in segment order (deterministic).  Thread t
-                    // owns 4 consecutive rows (rq..rq+3) and tokens j = jb + 4i, so every
-                    // load is a float4 and a warp reads 512 contiguous bytes; all IC loads of
-                    // one segment are independent and in flight together.
-                    const int t = threadIdx.x - WARP_EPI0 * 32;
-                    const int rq = (t & 31) * 4;
-                    const int jb = t >> 5;
-                    const int nq = n_tile * BN + rq;
-                    float scq[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) scq[e] = (nq + e < p.N) ? __ldg(p.scale + nq + e) : 0.f;
-                    constexpr int NI = NT / 4;
-                    constexpr int IC = NI < 8 ? NI : 8;
-#pragma unroll 1
-                    for (int i0 = 0; i0 < NI; i0 += IC) {
-                        if (jb + 4 * i0 >= mval) break;
-                        float4 acc[IC];
-#pragma unroll
-                        for (int ii = 0; ii < IC; ++ii) acc[ii] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-                        for (int c = c_first; c <= c_last; ++c) {
-                            const float4 *pc = reinterpret_cast<const float4 *>(
-                                p.partials + static_cast<size_t>(partial_slot(p, c, s.tile)) * (NT * BN));
-                            float4 v[IC];
-#pragma unroll
-                            for (int ii = 0; ii < IC; ++ii) {
-                                const int j = jb + 4 * (i0 + ii);
-                                v[ii] = j < mval ? __ldcg(pc + ((j * BN + rq) >> 2)) : make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
-#pragma unroll
-                            for (int ii = 0; ii < IC; ++ii) {
-                                acc[ii].x += v[ii].x;
-                                acc[ii].y += v[ii].y;
-                                acc[ii].z += v[ii].z;
-                                acc[ii].w += v[ii].w;
-                            }
-                        }
-#pragma unroll
-                        for (int ii = 0; ii < IC; ++ii) {
-                            const int j = jb + 4 * (i0 + ii);
-                            if (j >= mval) continue;
-                            __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + nq;
-                            const float a4[4] = {acc[ii].x, acc[ii].y, acc[ii].z, acc[ii].w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                if (nq + e < p.N) yr[e] = __float2bfloat16_rn(a4[e] * scq[e]);
-                        }
+                    if (old == c_last - c_first) {
+                        // every segment has arrived: re-arm the counter for the next launch and
+                        // leave the tile to the CTA-wide reduction after the role loops
+                        p.counters[ts] = 0;
+                        const int k = pending[0];
+                        pending[1 + 3 * k] = s.tile;
+                        pending[2 + 3 * k] = c_first;
+                        pending[3 + 3 * k] = c_last;
+                        pending[0] = k + 1;
                     }
                 }
             }
@@ -617,6 +572,70 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
     __syncwarp();
     ptx::tc_fence_before();
     ptx::cta_sync_all();
+
+    // ---------------- stream-K reductions (all 512 threads) ----------------
+    // A tile whose last segment arrived here: sum every segment's partial in segment order
+    // (deterministic), scale, store y.  Item (token j, rows rq..rq+3): consecutive threads
+    // take consecutive row quads, so a warp reads 512 contiguous bytes of each partial; each
+    // thread keeps IPT items x SB segments of loads in flight per round.
+    if (!*abort_flag && pending[0] > 0) {
+        __threadfence();
+        constexpr int QUADS = BN / 4;
+        constexpr int IPT = (NT * QUADS + NUM_THREADS - 1) / NUM_THREADS;  // items per thread
+        constexpr int SB = IPT >= 16 ? 1 : 16 / IPT;                        // segments per round
+        const int npend = pending[0];
+        for (int pi = 0; pi < npend; ++pi) {
+            const int tile = pending[1 + 3 * pi], c_first = pending[2 + 3 * pi], c_last = pending[3 + 3 * pi];
+            const int n_tile = tile / p.m_tiles;
+            const int m0 = (tile % p.m_tiles) * NT;
+            const int mval = min(NT, p.M - m0);
+            // Partial slots of the segments: every CTA after the first starts inside this
+            // tile, so it is that CTA's first tile (slot 2c); only the first CTA may have
+            // started earlier (slot 2c + 1).  One division per tile instead of one per load.
+            const int first_off = partial_slot(p, c_first, tile) - 2 * c_first;
+            float4 acc[IPT];
+#pragma unroll
+            for (int i = 0; i < IPT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int cb = c_first; cb <= c_last; cb += SB) {
+                float4 v[IPT][SB];
+#pragma unroll
+                for (int i = 0; i < IPT; ++i) {
+                    const int item = threadIdx.x + i * NUM_THREADS;
+                    const int j = item / QUADS, rq = (item % QUADS) * 4;
+#pragma unroll
+                    for (int u = 0; u < SB; ++u) {
+                        v[i][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (j < mval && cb + u <= c_last)
+                            v[i][u] = __ldcg(reinterpret_cast<const float4 *>(
+                                p.partials + static_cast<size_t>(2 * (cb + u) + (cb + u == c_first ? first_off : 0)) * (NT * BN) +
+                                j * BN + rq));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < IPT; ++i)
+#pragma unroll
+                    for (int u = 0; u < SB; ++u) {
+                        acc[i].x += v[i][u].x;
+                        acc[i].y += v[i][u].y;
+                        acc[i].z += v[i][u].z;
+                        acc[i].w += v[i][u].w;
+                    }
+            }
+#pragma unroll
+            for (int i = 0; i < IPT; ++i) {
+                const int item = threadIdx.x + i * NUM_THREADS;
+                const int j = item / QUADS, rq = (item % QUADS) * 4;
+                if (j >= mval) continue;
+                const int n = n_tile * BN + rq;
+                __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+                const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (n + e < p.N) yr[e] = __float2bfloat16_rn(a4[e] * __ldg(p.scale + n + e));
+            }
+        }
+    }
+
     if (warp == WARP_MMA) {
         __syncwarp();
         ptx::tc_fence_after();
