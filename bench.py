@@ -42,7 +42,8 @@ import torch
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-from llm_serving_engine_b200.inputs import DECODE_M, LLAMA3_8B_SHAPES, PREFILL_M, linear_bytes, linear_flops  # noqa: E402
+from llm_serving_engine_b200.inputs import (DECODE_M, LLAMA3_8B_SHAPES, LLAMA3_70B_SHAPES, PREFILL_M,  # noqa: E402
+                                            linear_bytes, linear_flops)
 
 METRIC = "int8 linear HBM GB/s (M<=64) & TFLOP/s (prefill) vs roofline; decode tok/s"
 UNIT = "GB/s"
@@ -60,6 +61,7 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-70b", action="store_true", help="skip the Llama-3-70B column-split sweep (config 5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU sample length")
     return ap.parse_args()
@@ -228,6 +230,78 @@ def time_graph(g, reps: int) -> float:
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / reps
+
+
+# --------------------------------------------------------------------------------------
+TP_M = (1, 32, 256, 4096)
+
+
+def tp70b_sweep(world: int, rank: int, dev, ops, warm):
+    """Config 5: Llama-3-70B projection shapes with the output rows (N) split over the
+    `world` ranks.  Per point (max over ranks): the rank's kernel time on its N/world rows
+    (CUDA graph over rotated weight copies, so the weights come from HBM), the NCCL
+    all-gather of the output shards, and the end to end time of kernel + gather + column
+    reorder (llm_serving_engine_b200.parallel.gather_columns), each in a CUDA graph, CUDA
+    events."""
+    from llm_serving_engine_b200.parallel import gather_columns
+
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    pts = []
+    for name in SHAPE_ORDER:
+        K, N = LLAMA3_70B_SHAPES[name]
+        n = N // world
+        copies = max(1, min(8, -(-3 * 126 * 2**20 // (n * K))))
+        ws = []
+        for _ in range(copies):
+            w = torch.randint(-127, 128, (n, K), generator=g, device=dev, dtype=torch.int8)
+            ws.append(ops.pack_weight(w))
+            del w
+        s = torch.empty(n, device=dev).uniform_(1e-4, 5e-4, generator=g)
+        for M in TP_M:
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+
+            def one(x=x, y=y):
+                for wp in ws:
+                    ops.int8_linear_packed(x, wp, s, n, K, out=y)
+            g1 = capture(one, warm)
+            time_graph(g1, 2)
+            t_k = time_graph(g1, 5) / copies
+            del g1
+            t_g = 0.0
+            if world > 1:
+                # the NCCL gather alone, and kernel + gather, each captured in a CUDA graph (as a
+                # graphed decode step runs them); every rank captures the same sequence
+                def gather10(y=y):
+                    for _ in range(10):
+                        gather_columns(y)
+                g2 = capture(gather10, warm)
+                time_graph(g2, 1)
+                t_g = time_graph(g2, 3) / 10
+                del g2
+
+            def e2e10(x=x, y=y):
+                for i in range(10):
+                    ops.int8_linear_packed(x, ws[i % copies], s, n, K, out=y)
+                    gather_columns(y)
+            g3 = capture(e2e10, warm)
+            time_graph(g3, 1)
+            t_e = time_graph(g3, 3) / 10
+            del g3
+            t_k, t_g, t_e = (max_over_ranks(v, world) for v in (t_k, t_g, t_e))
+            pts.append({"M": M, "shape": name, "K": K, "N": N, "rows_per_gpu": n,
+                        "kernel_us": round(t_k * 1e3, 2), "gather_us": round(t_g * 1e3, 2),
+                        "e2e_us": round(t_e * 1e3, 2),
+                        "kernel_GBps_per_gpu": round(linear_bytes(M, K, n) / t_k / 1e6, 1),
+                        "kernel_TFLOPs_per_gpu": round(linear_flops(M, K, n) / t_k / 1e9, 1),
+                        "gather_bytes": M * N * 2 if world > 1 else 0})
+            del x, y
+        del ws
+        torch.cuda.empty_cache()
+    return {"workload": f"config5: Llama-3-70B (K,N) qkv 8192x10240, o 8192x8192, gate_up 8192x57344, "
+                        f"down 28672x8192; N split over {world} GPU(s); M in {list(TP_M)}",
+            "collective": "NCCL all_gather_into_tensor of the output shards + column reorder" if world > 1 else "none",
+            "points": pts}
 
 
 # --------------------------------------------------------------------------------------
@@ -433,6 +507,8 @@ def main():
                                 "peak_source": peak_src + " bf16_tflops (burst)"},
                    "points": pre_pts}
 
+    tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
+
     # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
     host_x = {k: v.cpu().pin_memory() for k, v in xs.items()}
     host_y = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
@@ -481,6 +557,8 @@ def main():
         }
         if prefill:
             line["prefill"] = prefill
+        if tp70b:
+            line["config5_70b_column_split"] = tp70b
         if cpu_base:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)

@@ -2,8 +2,8 @@
 
 The compute path is liblse_int8.so (hand-written CUDA for sm_100a, C ABI in
 include/lse_int8.h); this package is its host side: the ctypes binding (`_lib`), the
-torch-facing ops (`ops`), the drop-in modules and the model hook (`int8_linear`) and the
-seeded inputs (`inputs`).
+torch-facing ops (`ops`), the drop-in modules and the model hook (`int8_linear`), the
+output-column split over ranks (`parallel`) and the seeded inputs (`inputs`).
 """
 
 from .int8_linear import FusedInt8QKV, Int8Linear, Int8LlamaMLP, int8_weight_bytes, quantize_llama_  # noqa: F401

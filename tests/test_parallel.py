@@ -1,0 +1,126 @@
+"""Output-column split over ranks (llm_serving_engine_b200.parallel) on CPU gloo ranks.
+
+The per-rank kernel is replaced by the oracle (a `local_factory` returning bf16-rounded fp64
+results), so these tests check what the split itself must get right - which rows each rank
+holds, the gate/up interleave, the all-gather and its column order, leading dimensions - at
+world sizes 2 and 4, bit for bit against the unsplit computation.  The GPU run of the same
+module over NCCL is tests/test_gpu_multi.py.
+"""
+
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from llm_serving_engine_b200.parallel import (ColumnParallelInt8Linear, TensorParallelInt8MLP, gather_columns,
+                                              interleaved_rows, shard_rows)
+from oracle.ref_linear import ref_int8_linear, ref_quantize
+
+
+def oracle_local(q: torch.Tensor, s: torch.Tensor):
+    qn, sn = q.numpy(), s.numpy()
+
+    def run(x: torch.Tensor) -> torch.Tensor:
+        y = ref_int8_linear(x.reshape(-1, x.shape[-1]).float().numpy(), qn, sn)
+        return torch.from_numpy(y).to(torch.bfloat16).reshape(*x.shape[:-1], qn.shape[0])
+
+    return run
+
+
+def _weights(seed: int, N: int, K: int):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(N, K, generator=g) * torch.rand(N, 1, generator=g)
+    q, s = ref_quantize(w.numpy())
+    return torch.from_numpy(q), torch.from_numpy(s)
+
+
+def _x(seed: int, *shape):
+    return torch.randn(*shape, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+
+
+def _column_case(rank: int, world: int) -> None:
+    M, K, N = 5, 64, 48
+    q, s = _weights(1, N, K)
+    x = _x(2, M, K)
+    full = oracle_local(q, s)(x)
+    mod = ColumnParallelInt8Linear.from_quantized(q, s, local_factory=oracle_local)
+    y = mod(x)
+    assert y.shape == (M, N) and torch.equal(y, full)
+    # without the gather each rank keeps its own contiguous block
+    part = ColumnParallelInt8Linear.from_quantized(q, s, gather_output=False, local_factory=oracle_local)(x)
+    n = N // world
+    assert torch.equal(part, full[:, rank * n:(rank + 1) * n])
+    # any leading shape
+    x3 = _x(3, 2, 3, K)
+    assert torch.equal(mod(x3), oracle_local(q, s)(x3))
+
+
+def _mlp_case(rank: int, world: int) -> None:
+    H, I, M = 32, 64, 3
+    qg, sg = _weights(4, I, H)
+    qu, su = _weights(5, I, H)
+    qd, sd = _weights(6, H, I)
+    x = _x(7, M, H)
+    # the unsplit path with the same roundings: fused gate_up, SiLU * mul in bf16, down
+    gu = oracle_local(torch.cat([qg, qu]), torch.cat([sg, su]))(x)
+    h = F.silu(gu[:, :I]) * gu[:, I:]
+    ref = oracle_local(qd, sd)(h)
+    mlp = TensorParallelInt8MLP.from_quantized(qg, sg, qu, su, qd, sd, local_factory=oracle_local)
+    assert torch.equal(mlp(x), ref)
+
+
+def _gather_order_case(rank: int, world: int) -> None:
+    y = torch.full((2, 3), float(rank), dtype=torch.bfloat16)
+    out = gather_columns(y)
+    expect = torch.cat([torch.full((2, 3), float(r), dtype=torch.bfloat16) for r in range(world)], dim=1)
+    assert torch.equal(out, expect)
+
+
+def _worker(rank: int, world: int, port: int, case) -> None:
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        case(rank, world)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _run(case, world: int) -> None:
+    mp.spawn(_worker, args=(world, _free_port(), case), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_column_split_matches_unsplit(world):
+    _run(_column_case, world)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_mlp_matches_unsplit(world):
+    _run(_mlp_case, world)
+
+
+def test_gather_puts_rank_blocks_in_order():
+    _run(_gather_order_case, 2)
+
+
+def test_row_assignment():
+    assert torch.equal(shard_rows(12, 3, 1), torch.arange(4, 8))
+    assert torch.equal(interleaved_rows(8, 2, 1), torch.tensor([4, 5, 6, 7, 12, 13, 14, 15]))
+    # every row exactly once across the ranks
+    rows = torch.cat([interleaved_rows(8, 4, r) for r in range(4)])
+    assert sorted(rows.tolist()) == list(range(16))
+    with pytest.raises(ValueError):
+        shard_rows(10, 4, 0)
+    assert np.array_equal(np.concatenate([shard_rows(12, 4, r).numpy() for r in range(4)]), np.arange(12))
