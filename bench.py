@@ -62,6 +62,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-70b", action="store_true", help="skip the Llama-3-70B column-split sweep (config 5)")
+    ap.add_argument("--no-e2e-decode", action="store_true", help="skip the end-to-end model decode (config 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU sample length")
     return ap.parse_args()
@@ -305,6 +306,35 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
 
 
 # --------------------------------------------------------------------------------------
+def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
+    """Config 4: batched decode of a random-init Llama-3-8B-shaped model, 64 sequences at a
+    1024-token context, one CUDA graph per step, int8 projections vs bf16 projections on the
+    same weights (llm_serving_engine_b200.llama_decode).  tokens/s = 64 x steps / time."""
+    from llm_serving_engine_b200.llama_decode import LLAMA3_8B, DecodeModel, decode_bytes_per_step
+
+    B, ctx = 64, 1024
+    base = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=False)
+    q8 = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=True, weights=base.weights)
+    out = {"workload": "config4: Llama-3-8B shape (32 layers, hidden 4096, 32/8 heads, head_dim 128, MLP 14336, "
+                       "vocab 128256), random init, 64 sequences, 1024-token context, greedy, CUDA graph per step; "
+                       "attention: torch SDPA over a contiguous KV cache",
+           "unit": "tokens/s"}
+    for name, m in (("int8", q8), ("none", base)):
+        g = capture(m.step, warm)
+        time_graph(g, 3)
+        ms = time_graph(g, steps)
+        byts = decode_bytes_per_step(LLAMA3_8B, B, ctx, name == "int8")
+        out[name] = {"tokens_per_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+                     "bytes_per_step": byts, "GBps": round(byts / ms / 1e6, 1),
+                     "frac_of_hbm": round(byts / ms / 1e6 / hbm_peak, 4)}
+        del g
+    out["int8_speedup"] = round(out["int8"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
+    del base, q8
+    torch.cuda.empty_cache()
+    return out
+
+
+# --------------------------------------------------------------------------------------
 def cpu_reference_sample(seconds: float):
     """The reference's CPU path (float32 nn.Linear on the dequantized weight, all host
     threads) over one layer of the decode sweep, repeated for ~`seconds`."""
@@ -508,6 +538,7 @@ def main():
                    "points": pre_pts}
 
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
+    decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
     # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
     host_x = {k: v.cpu().pin_memory() for k, v in xs.items()}
@@ -559,6 +590,8 @@ def main():
             line["prefill"] = prefill
         if tp70b:
             line["config5_70b_column_split"] = tp70b
+        if decode4:
+            line["config4_e2e_decode"] = decode4
         if cpu_base:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)

@@ -1,0 +1,144 @@
+"""Batched decode step of a Llama-3-style decoder on the int8 projections: the vehicle for
+the end-to-end decode measurement (decode tokens/s with int8 vs bf16 projection weights).
+
+The step follows the reference's graphed decode step (src/llm_serving_engine/model/
+decode_graph.py:125-140 over `decoder_hidden`, model_runner.py:213-224): embedding, then per
+layer RMSNorm -> fused QKV -> RoPE -> K/V write -> attention over the sequence's cache ->
+o_proj -> residual -> RMSNorm -> gate_up -> SiLU * mul -> down -> residual, then the final
+norm, the lm_head and the greedy token.  The projections are this package's int8 modules
+(`quantize=True`) or bf16 `F.linear` on the same random weights (`quantize=False`, the
+reference's `quantize="none"`).
+
+Stated differences from the reference engine (none of them on the int8 path):
+  * the KV cache is one contiguous [B, Hkv, context + 1, head_dim] block per layer, not the
+    reference's paged pool, and attention is torch's scaled_dot_product_attention over it
+    (attention is outside this build; the reference uses its own Triton kernel);
+  * a timed step keeps its position fixed: it writes the new K/V into slot `context` and
+    attends over all context + 1 positions, so the CUDA graph's shapes are static and every
+    replay does exactly the work of a decode step at that context length.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .int8_linear import Int8Linear
+
+__all__ = ["LlamaShape", "LLAMA3_8B", "DecodeModel", "decode_bytes_per_step"]
+
+
+@dataclass(frozen=True)
+class LlamaShape:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+
+
+LLAMA3_8B = LlamaShape(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=14336, vocab=128256)
+
+
+def decode_bytes_per_step(shape: LlamaShape, batch: int, context: int, quantize: bool) -> int:
+    """HBM bytes one decode step must read at least: projection weights (int8 + fp32 scales,
+    or bf16), the K/V of every sequence (context + 1 positions), the lm_head and the new
+    tokens' embedding rows."""
+    H, hd = shape.hidden, shape.head_dim
+    n_qkv = (shape.heads + 2 * shape.kv_heads) * hd
+    per_layer = [(H, n_qkv), (shape.heads * hd, H), (H, 2 * shape.intermediate), (shape.intermediate, H)]
+    w = sum(k * n * (1 if quantize else 2) + (4 * n if quantize else 0) for k, n in per_layer) * shape.layers
+    kv = 2 * shape.layers * batch * shape.kv_heads * (context + 1) * hd * 2
+    return w + kv + shape.vocab * H * 2 + batch * H * 2
+
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    # x [B, heads, head_dim]; rotate-half convention (transformers' Llama)
+    x1, x2 = x.chunk(2, dim=-1)
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
+class DecodeModel:
+    """Random-init Llama decoder for `batch` sequences at `context` cached positions."""
+
+    def __init__(self, shape: LlamaShape, batch: int, context: int, device, seed: int = 0,
+                 quantize: bool = True, weights: list | None = None):
+        self.shape, self.batch, self.context, self.quantize = shape, batch, context, quantize
+        dev = torch.device(device)
+        g = torch.Generator(device=dev).manual_seed(seed)
+
+        def w(*size):
+            return (torch.randn(*size, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+        H, hd, I = shape.hidden, shape.head_dim, shape.intermediate
+        self.embed = w(shape.vocab, H)
+        self.lm_head = w(shape.vocab, H)
+        self.final_norm = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        # bf16 weights per layer: [q;k;v], o, [gate;up], down (shared with a quantized twin)
+        self.weights = weights if weights is not None else [
+            (torch.cat([w(shape.heads * hd, H), w(2 * shape.kv_heads * hd, H)]), w(H, shape.heads * hd),
+             torch.cat([w(I, H), w(I, H)]), w(H, I)) for _ in range(shape.layers)]
+        if quantize:
+            self.proj = [tuple(Int8Linear.from_float_weights(t) for t in layer) for layer in self.weights]
+        else:
+            self.proj = [tuple((lambda x, t=t: F.linear(x, t)) for t in layer) for layer in self.weights]
+        self.norms = [(torch.ones(H, device=dev, dtype=torch.bfloat16), torch.ones(H, device=dev, dtype=torch.bfloat16))
+                      for _ in range(shape.layers)]
+        # a prefilled context of `context` positions per sequence (+1 slot for the new token),
+        # from its own generator so that a twin sharing `weights` gets the same caches
+        gk = torch.Generator(device=dev).manual_seed(seed + 1)
+
+        def kv():
+            return torch.randn(batch, shape.kv_heads, context + 1, hd, generator=gk, device=dev).to(torch.bfloat16)
+        self.k_cache = [kv() for _ in range(shape.layers)]
+        self.v_cache = [kv() for _ in range(shape.layers)]
+        inv = 1.0 / (shape.rope_theta ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
+        ang = context * inv
+        self.cos = torch.cos(ang).to(torch.bfloat16)
+        self.sin = torch.sin(ang).to(torch.bfloat16)
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+
+    def _hidden(self, tokens: torch.Tensor, in_place: bool) -> torch.Tensor:
+        """Final-norm hidden state of one step.  `in_place` writes the new K/V into the
+        caches (the decode step); otherwise into copies (a side-effect-free check)."""
+        s = self.shape
+        B, hd, pos = self.batch, s.head_dim, self.context
+        h = self.embed[tokens]  # [B, H]
+        for li in range(s.layers):
+            qkv_p, o_p, gu_p, down_p = self.proj[li]
+            n_in, n_post = self.norms[li]
+            x = _rms_norm(h, n_in, s.eps)
+            qkv = qkv_p(x)
+            q = qkv[:, :s.heads * hd].view(B, s.heads, hd)
+            k = qkv[:, s.heads * hd:(s.heads + s.kv_heads) * hd].view(B, s.kv_heads, hd)
+            v = qkv[:, (s.heads + s.kv_heads) * hd:].view(B, s.kv_heads, hd)
+            q, k = _rope(q, self.cos, self.sin), _rope(k, self.cos, self.sin)
+            kc, vc = (self.k_cache[li], self.v_cache[li]) if in_place else (self.k_cache[li].clone(), self.v_cache[li].clone())
+            kc[:, :, pos] = k
+            vc[:, :, pos] = v
+            attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
+            h = h + o_p(attn.reshape(B, s.heads * hd))
+            x = _rms_norm(h, n_post, s.eps)
+            gu = gu_p(x)
+            h = h + down_p(F.silu(gu[:, :s.intermediate]) * gu[:, s.intermediate:])
+        return _rms_norm(h, self.final_norm, s.eps)
+
+    def step(self, tokens: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step for every sequence; returns the greedy next tokens [B]."""
+        h = self._hidden(self.tokens if tokens is None else tokens, in_place=True)
+        return F.linear(h, self.lm_head).argmax(-1)
+
+    def logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """fp32 logits of one step, leaving the caches untouched (parity checks)."""
+        return F.linear(self._hidden(tokens, in_place=False), self.lm_head).float()

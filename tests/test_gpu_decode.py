@@ -1,0 +1,47 @@
+"""The end-to-end decode harness (llm_serving_engine_b200.llama_decode) at a small shape:
+int8 projections against bf16 projections on the dequantized int8 weights, and the CUDA
+graph of a decode step against the eager step."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from llm_serving_engine_b200.llama_decode import DecodeModel, LlamaShape, decode_bytes_per_step
+
+pytestmark = pytest.mark.gpu
+
+TINY = LlamaShape(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=512, vocab=1000)
+
+
+def test_int8_step_matches_dequantized_bf16_step():
+    base = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=False)
+    q8 = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=True, weights=base.weights)
+    deq = [tuple(p.dequantized(torch.bfloat16) for p in layer) for layer in q8.proj]
+    ref = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=False, weights=deq)
+    tokens = torch.tensor([1, 7, 99, 512], device="cuda")
+    a, b = q8.logits(tokens), ref.logits(tokens)
+    err = ((a - b).abs().max() / b.abs().max()).item()
+    assert np.isfinite(err) and err < 2e-2, err
+
+
+def test_graph_replay_equals_eager_step():
+    m = DecodeModel(TINY, batch=8, context=32, device="cuda", seed=5, quantize=True)
+    m.tokens.copy_(torch.arange(8, device="cuda") * 11)
+    eager = m.step().clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        m.step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        out = m.step()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
+def test_bytes_per_step_counts_int8_weights():
+    assert decode_bytes_per_step(TINY, 4, 16, True) < decode_bytes_per_step(TINY, 4, 16, False)
