@@ -66,8 +66,6 @@ int init_device(int device) {
         if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) { set_cuda_error(e, "cudaSetDevice"); return; }
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        if (e == cudaSuccess) e = set_tc_attrs<16>();
-        if (e == cudaSuccess) e = set_tc_attrs<32>();
         if (e == cudaSuccess) e = set_tc_attrs<64>();
         if (e == cudaSuccess) e = set_tc_attrs<128>();
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
@@ -132,12 +130,11 @@ void launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&attr)[1], dim3
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int token_tile(int64_t M) {
-    if (M <= 16) return 16;
-    if (M <= 32) return 32;
-    if (M <= 64) return 64;
-    return 128;
-}
+// Token tile of the tensor-core kernel: 64 up to 64 tokens, 128 above.  A tcgen05.mma costs
+// the same issue time at N = 16, 32 or 64, so smaller tiles only add instructions per weight
+// byte (measured on B200: gate_up at M <= 32 runs 35 us with 64-token tiles, 52 us with
+// 16/32-token tiles).
+int token_tile(int64_t M) { return M <= 64 ? 64 : 128; }
 
 // Tensor-core kernel schedule: full waves data-parallel, the last one-to-two waves stream-K.
 struct TcPlan {
@@ -283,26 +280,36 @@ template <int MT>
 cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp,
                              const float *scale, int64_t N, void *y, int64_t ldy, int num_sms, cudaStream_t st) {
     if (variant < 0) variant = ((N + 15) / 16 >= 2 * static_cast<int64_t>(num_sms)) ? 1 : 0;
-    constexpr bool BF = MT == 2;
-    switch (variant) {
-        case 1: return launch_skinny<MT, 8, 2, 4, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-        case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-        case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-        case 4: return launch_skinny<MT, 16, 2, 4, BF, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-        default:
-            if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            else return launch_skinny<2, 16, 2, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+    if constexpr (MT == 4) {
+        // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
+        switch (variant) {
+            case 1: return launch_skinny<4, 8, 2, 4, true, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 2: return launch_skinny<4, 16, 1, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            default: return launch_skinny<4, 8, 1, 4, true, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        }
+    } else {
+        constexpr bool BF = MT == 2;
+        switch (variant) {
+            case 1: return launch_skinny<MT, 8, 2, 4, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 4: return launch_skinny<MT, 16, 2, 4, BF, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            default:
+                if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+                else return launch_skinny<2, 16, 2, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+        }
     }
 }
 
-constexpr int64_t kSkinnyMaxM = 16;  // the decode kernel's token range (two 8-token tiles)
+constexpr int64_t kSkinnyMaxM = 32;  // the decode kernel's token range (four 8-token tiles)
 
 int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale, int64_t N,
                void *y, int64_t ldy, int num_sms, cudaStream_t st) {
     if (M > kSkinnyMaxM) return LSE_ERR_UNSUPPORTED;
     const int variant = skinny_variant();
-    cudaError_t e = M <= 8 ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
-                           : launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st);
+    cudaError_t e = M <= 8    ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
+                    : M <= 16 ? launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
+                              : launch_skinny_mt<4>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -382,12 +389,8 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
         return LSE_ERR_WORKSPACE;
-    switch (pl.nt) {
-        case 16: return launch_tc<16>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
-        case 32: return launch_tc<32>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
-        case 64: return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
-        default: return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
-    }
+    if (pl.nt == 64) return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
+    return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
 }
 }  // namespace
 }  // namespace lse

@@ -196,12 +196,13 @@ def _packed_call(x, packed, s, N, K, ws, algo, y=None, ldy=None):
 
 @pytest.mark.parametrize("M,K,N", [(1, 16, 8), (3, 48, 17), (4, 4096, 6144), (9, 272, 200), (16, 144, 136),
                                    (2, 4096, 28672), (16, 4096, 28672), (5, 8192, 1040), (12, 8208, 272),
+                                   (24, 4096, 4096), (31, 1040, 528),
                                    (17, 14336, 4096), (32, 4096, 28672), (64, 14336, 4096), (65, 4112, 200),
                                    (130, 1024, 640), (512, 4096, 4096)])
 @pytest.mark.parametrize("algo", ["skinny", "tcgen05", "auto"])
 def test_packed_path_parity(ws, M, K, N, algo):
-    if algo == "skinny" and M > 16:
-        pytest.skip("the skinny decode kernel serves M <= 16")
+    if algo == "skinny" and M > 32:
+        pytest.skip("the skinny decode kernel serves M <= 32")
     x, w, s = make_inputs(M, K, N, seed=M * 7 + K + N)
     packed = ops.pack_weight(w.cuda())
     xd, sd = x.cuda(), s.cuda()
@@ -234,14 +235,14 @@ def test_packed_strided_and_layout_errors(ws):
     st = torch.cuda.current_stream().cuda_stream
     assert lib.lse_int8_linear_packed(x.cuda().data_ptr(), M, K, K, packed.data_ptr(), s.cuda().data_ptr(), N,
                                       y.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_GEMV, st) == _lib.LSE_ERR_UNSUPPORTED
-    x20 = torch.zeros(20, K, dtype=torch.bfloat16, device="cuda")
-    y20 = torch.empty(20, N, dtype=torch.bfloat16, device="cuda")
-    assert lib.lse_int8_linear_packed(x20.data_ptr(), 20, K, K, packed.data_ptr(), s.cuda().data_ptr(), N,
-                                      y20.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_SKINNY, st) == _lib.LSE_ERR_UNSUPPORTED
+    x40 = torch.zeros(40, K, dtype=torch.bfloat16, device="cuda")
+    y40 = torch.empty(40, N, dtype=torch.bfloat16, device="cuda")
+    assert lib.lse_int8_linear_packed(x40.data_ptr(), 40, K, K, packed.data_ptr(), s.cuda().data_ptr(), N,
+                                      y40.data_ptr(), N, ws.ptr, ws.nbytes, _lib.ALGO_SKINNY, st) == _lib.LSE_ERR_UNSUPPORTED
 
 
 @pytest.mark.parametrize("K,N", [(14336, 4096), (4096, 28672)])
-@pytest.mark.parametrize("M", [1, 8, 9, 16])
+@pytest.mark.parametrize("M", [1, 8, 9, 16, 17, 32])
 def test_skinny_deterministic_and_linear(ws, M, K, N):
     x, w, s = make_inputs(M, K, N, seed=21)
     packed = ops.pack_weight(w.cuda())
