@@ -247,6 +247,17 @@ int run_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, 
     return LSE_OK;
 }
 
+// Groups per row block the decode kernel prefetches into L2 ahead of its register loads
+// (one group measured best on B200)
+// (LSE_SKINNY_PF overrides; 0 disables).
+int skinny_prefetch_groups() {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_SKINNY_PF");
+        return e ? std::max(0, std::atoi(e)) : 1;
+    }();
+    return v;
+}
+
 template <int MT, int KW, int R, int U, bool BF16, int MINB>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, cudaStream_t st) {
@@ -257,7 +268,8 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
     launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
     return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB>, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
-                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)));
+                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)),
+                              skinny_prefetch_groups());
 }
 
 // Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):

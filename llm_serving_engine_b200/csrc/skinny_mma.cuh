@@ -73,12 +73,14 @@ __device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
 // pointer that moves once per group and no per-chunk predicate; the groups are visited in
 // an order rotated per CTA, so the CTAs resident together read different offsets of their
 // row blocks.  A slice that is not a whole number of groups (ragged K) takes a
-// bounds-checked path.
+// bounds-checked path.  `pf_groups` groups per row block beyond the U chunks in registers
+// are prefetched into L2 by lane 0 (bulk prefetches), which deepens the stream at no
+// register cost.
 template <int MT, int KW, int R, int U, bool BF16, int MINB>
 __global__ void __launch_bounds__(KW * 32, MINB)
 skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
-                 __nv_bfloat16 *__restrict__ y, int64_t ldy, int Kp) {
+                 __nv_bfloat16 *__restrict__ y, int64_t ldy, int Kp, int pf_groups) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int rg = blockIdx.x;
     const int m0 = blockIdx.y * MT * 8;
@@ -105,6 +107,19 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 #pragma unroll
         for (int r = 0; r < R; ++r)
             wb[j][r] = (fast || j < nch) ? ld_weight16(gp + r * rb_bytes + j * 512, pol) : make_uint4(0, 0, 0, 0);
+    // L2 prefetch of the group `v` visits ahead (lane 0, one bulk prefetch per row block): the
+    // register loads then hit L2, so the registers hold only U chunks while DRAM has
+    // pf_groups more groups per row block in flight.
+    auto prefetch_group = [&](int v) {
+        if (lane == 0 && v < ng) {
+            int gv = rot + v;
+            if (gv >= ng) gv -= ng;
+#pragma unroll
+            for (int r = 0; r < R; ++r) ptx::bulk_prefetch_l2(wbase + r * rb_bytes + gv * (U * 512), U * 512);
+        }
+    };
+    if (fast)
+        for (int v = 1; v <= pf_groups; ++v) prefetch_group(v);
 
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
 
@@ -192,6 +207,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     if (fast) {
         int gi = rot;  // slice group being processed
         for (int g = 0; g < ng; ++g) {
+            if (pf_groups > 0) prefetch_group(g + pf_groups + 1);
             const bool wrap = gi + 1 == ng;  // the next group in the rotated order is group 0
             const int8_t *np = wrap ? wbase : gp + U * 512;
             if (g + 1 < ng) group(np, std::true_type{});
