@@ -247,8 +247,9 @@ int run_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, 
     return LSE_OK;
 }
 
-// Groups per row block the decode kernel prefetches into L2 ahead of its register loads
-// (one group measured best on B200)
+// Groups per row block the decode kernel prefetches into L2 ahead of its register loads, for
+// M <= 8 (one group measured best on B200: 5-14% faster at M = 1 and 4; at M = 9..16, where
+// the activation loads weigh more, prefetching measured 3-5% slower and is off)
 // (LSE_SKINNY_PF overrides; 0 disables).
 int skinny_prefetch_groups() {
     static const int v = [] {
@@ -269,7 +270,7 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
     return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB>, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
                               static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)),
-                              skinny_prefetch_groups());
+                              MT == 1 ? skinny_prefetch_groups() : 0);
 }
 
 // Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):
