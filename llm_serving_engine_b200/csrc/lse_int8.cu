@@ -274,13 +274,15 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
 }
 
 // Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):
-//   * many row blocks (N/16 >= 2 x SMs: QKV, gate_up): CTAs of 8 warps on two row blocks,
-//     so every activation load serves 32 weight rows;
+//   * very many row blocks (N/16 >= 4 x SMs: gate_up): CTAs of 8 warps on one row block, four
+//     CTAs per SM (M <= 8; above that, two row blocks and three CTAs per SM);
+//   * many row blocks (N/16 >= 2 x SMs: QKV): CTAs of 8 warps on two row blocks, so every
+//     activation load serves 32 weight rows;
 //   * few row blocks (O, down): CTAs of 16 warps, one row block (two for M > 8, where the
 //     activation loads, not the weight stream, would otherwise saturate L1);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
-// LSE_SKINNY_VARIANT=<0..4> pins one configuration for tuning runs.
+// LSE_SKINNY_VARIANT=<0..8> pins one configuration for tuning runs.
 int skinny_variant() {
     static const int v = [] {
         const char *e = std::getenv("LSE_SKINNY_VARIANT");
@@ -292,7 +294,10 @@ int skinny_variant() {
 template <int MT>
 cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp,
                              const float *scale, int64_t N, void *y, int64_t ldy, int num_sms, cudaStream_t st) {
-    if (variant < 0) variant = ((N + 15) / 16 >= 2 * static_cast<int64_t>(num_sms)) ? 1 : 0;
+    if (variant < 0) {
+        const int64_t rb_per_sm = (N + 15) / 16 / num_sms;
+        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 5) : (rb_per_sm >= 2 ? 1 : 0);
+    }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
         switch (variant) {
@@ -307,6 +312,10 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
             case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
             case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
             case 4: return launch_skinny<MT, 16, 2, 4, BF, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 5: return launch_skinny<MT, 8, 2, 2, BF, 3>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 6: return launch_skinny<MT, 8, 2, 4, BF, 3>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 7: return launch_skinny<MT, 8, 1, 4, BF, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 8: return launch_skinny<MT, 16, 1, 2, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
             default:
                 if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
                 else return launch_skinny<2, 16, 2, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
