@@ -38,6 +38,7 @@ import sys
 import time
 
 import torch
+import torch.nn.functional as F
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -334,6 +335,45 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
     return out
 
 
+def fused_gate_up(weights, dev, warm, ops, hbm_peak):
+    """The decode MLP's first half, silu(x Wg^T) * (x Wu^T), for M in 1, 4, 16 over every
+    layer's gate_up weight: one fused kernel (lse_int8_gate_up_silu_packed, the gate and up
+    rows interleaved in 16-row blocks) vs the int8 gate_up projection followed by torch's
+    SiLU * mul.  The uniform random weights stand for an interleaved [gate; up] as they are."""
+    K, N2 = LLAMA3_8B_SHAPES["gate_up"]
+    inter = N2 // 2
+    gx = torch.Generator(device=dev).manual_seed(17)
+    out = {"workload": f"Llama-3-8B gate_up K={K}, I={inter}, {len(weights)} layers' weights per graph", "points": []}
+    for M in (1, 4, 16):
+        x = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
+        h = torch.empty(M, inter, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(M, N2, device=dev, dtype=torch.bfloat16)
+
+        def fused(x=x, h=h):
+            for layer in weights:
+                wp, s = layer["gate_up"]
+                ops.int8_gate_up_silu_packed(x, wp, s, inter, K, out=h)
+
+        def unfused(x=x, gu=gu, h=h):
+            for layer in weights:
+                wp, s = layer["gate_up"]
+                ops.int8_linear_packed(x, wp, s, N2, K, out=gu)
+                torch.mul(F.silu(gu[:, :inter]), gu[:, inter:], out=h)
+        pt = {"M": M}
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            g = capture(fn, warm)
+            time_graph(g, 2)
+            us = time_graph(g, 10) / len(weights) * 1e3
+            pt[name + "_us"] = round(us, 3)
+            del g
+        b = linear_bytes(M, K, N2) - M * N2 * 2 + M * inter * 2
+        pt["fused_GBps"] = round(b / pt["fused_us"] / 1e3, 1)
+        pt["fused_frac_of_hbm"] = round(b / pt["fused_us"] / 1e3 / hbm_peak, 4)
+        pt["speedup"] = round(pt["unfused_us"] / pt["fused_us"], 3)
+        out["points"].append(pt)
+    return out
+
+
 # --------------------------------------------------------------------------------------
 def cpu_reference_sample(seconds: float):
     """The reference's CPU path (float32 nn.Linear on the dequantized weight, all host
@@ -537,6 +577,7 @@ def main():
                                 "peak_source": peak_src + " bf16_tflops (burst)"},
                    "points": pre_pts}
 
+    fused_mlp = fused_gate_up(weights, dev, warm, ops, hbm_peak)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
@@ -588,6 +629,7 @@ def main():
         }
         if prefill:
             line["prefill"] = prefill
+        line["fused_gate_up_silu"] = fused_mlp
         if tp70b:
             line["config5_70b_column_split"] = tp70b
         if decode4:

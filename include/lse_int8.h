@@ -112,6 +112,24 @@ int lse_int8_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx,
                            void *workspace, size_t workspace_bytes,
                            int algo, void *stream);
 
+/*
+ * y[m, i] = bf16( silu(s_g[i] * sum_k x[m,k] * w_g[i,k]) * (s_u[i] * sum_k x[m,k] * w_u[i,k]) )
+ *
+ * The Llama MLP's gate and up projections and SiLU * mul (transformers' LlamaMLP.forward,
+ * reached at model_runner.py:223 and piecewise_graph.py:166) in one decode-kernel launch,
+ * for M <= 16 (LSE_ERR_UNSUPPORTED above: run lse_int8_linear_packed on the same weights
+ * and pair the columns).  No workspace.
+ *   w_packed  the packed layout (lse_int8_pack_weight) of a [2I, K] int8 matrix whose rows
+ *             interleave 8-row blocks: rows 16j..16j+7 are gate rows 8j..8j+7 and rows
+ *             16j+8..16j+15 the matching up rows
+ *   scale     fp32 [2I], interleaved the same way
+ *   y         bf16 [M, I], row stride ldy (>= I);  I % 8 == 0 (LSE_ERR_UNSUPPORTED otherwise)
+ * SiLU and the product are evaluated in fp32 and rounded to bf16 once.
+ */
+int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                 const int8_t *w_packed, const float *scale, int64_t I,
+                                 void *y, int64_t ldy, void *stream);
+
 /* Bytes of the counter region at the start of every workspace (must start zeroed). */
 #define LSE_WS_COUNTER_BYTES 65536
 

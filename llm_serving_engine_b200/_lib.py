@@ -38,6 +38,7 @@ DT_F32 = 2
 WS_COUNTER_BYTES = 65536
 NOALLOC_SCRATCH_BYTES = 12582912  # fixed scratch of lse_int8_linear_packed_noalloc, per device
 NOALLOC_MAX_M = 64
+GATE_UP_SILU_MAX_M = 16  # lse_int8_gate_up_silu_packed's token range
 ABI_VERSION = 1
 
 # Every symbol include/lse_int8.h declares, with its ctypes signature.
@@ -49,6 +50,7 @@ SIGNATURES = {
     "lse_int8_linear_workspace": ([_I64, _I64, _I64], _SZ),
     "lse_int8_linear_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
     "lse_int8_linear_packed_noalloc": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
+    "lse_int8_gate_up_silu_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "lse_int8_packed_weight_bytes": ([_I64, _I64], _SZ),
     "lse_int8_pack_weight": ([_P, _I64, _I64, _I64, _P, _P], _I32),
     "lse_int8_unpack_weight": ([_P, _I64, _I64, _P, _P], _I32),

@@ -259,15 +259,15 @@ int skinny_prefetch_groups() {
     return v;
 }
 
-template <int MT, int KW, int R, int U, bool BF16, int MINB>
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, cudaStream_t st) {
-    const int64_t row_blocks = (N + 15) / 16;
+    const int64_t row_blocks = SILU_MUL ? N / 8 : (N + 15) / 16;  // weight row blocks (SILU_MUL: 2N rows)
     dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
-    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB>, static_cast<const __nv_bfloat16 *>(x), ldx,
+    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL>, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
                               static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)),
                               MT == 1 ? skinny_prefetch_groups() : 0);
@@ -291,34 +291,36 @@ int skinny_variant() {
     return v;
 }
 
-template <int MT>
+// SILU (the fused gate_up + SiLU * mul): N is the intermediate size and the weight has 2N
+// rows, which set the shape tier.
+template <int MT, bool SILU = false>
 cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp,
                              const float *scale, int64_t N, void *y, int64_t ldy, int num_sms, cudaStream_t st) {
     if (variant < 0) {
-        const int64_t rb_per_sm = (N + 15) / 16 / num_sms;
+        const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
         variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 5) : (rb_per_sm >= 2 ? 1 : 0);
     }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
         switch (variant) {
-            case 1: return launch_skinny<4, 8, 2, 4, true, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 2: return launch_skinny<4, 16, 1, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            default: return launch_skinny<4, 8, 1, 4, true, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 1: return launch_skinny<4, 8, 2, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 2: return launch_skinny<4, 16, 1, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            default: return launch_skinny<4, 8, 1, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
         }
     } else {
         constexpr bool BF = MT == 2;
         switch (variant) {
-            case 1: return launch_skinny<MT, 8, 2, 4, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 4: return launch_skinny<MT, 16, 2, 4, BF, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 5: return launch_skinny<MT, 8, 2, 2, BF, 3>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 6: return launch_skinny<MT, 8, 2, 4, BF, 3>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 7: return launch_skinny<MT, 8, 1, 4, BF, 4>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 8: return launch_skinny<MT, 16, 1, 2, BF, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 1: return launch_skinny<MT, 8, 2, 4, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 4: return launch_skinny<MT, 16, 2, 4, BF, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 5: return launch_skinny<MT, 8, 2, 2, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 6: return launch_skinny<MT, 8, 2, 4, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 7: return launch_skinny<MT, 8, 1, 4, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 8: return launch_skinny<MT, 16, 1, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
             default:
-                if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-                else return launch_skinny<2, 16, 2, 4, true, 1>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+                if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+                else return launch_skinny<2, 16, 2, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
         }
     }
 }
@@ -614,4 +616,37 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
     }
     return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, scratch, LSE_NOALLOC_SCRATCH_BYTES,
                        LSE_ALGO_TCGEN05, true, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// lse_int8_gate_up_silu_packed: the MLP's gate and up projections and SiLU * mul in one
+// decode-kernel launch (M <= 16).
+// ---------------------------------------------------------------------------------------
+extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                                            const float *scale, int64_t I, void *y, int64_t ldy, void *stream) {
+    if (M < 0 || I < 0 || K < 0) return LSE_ERR_INVALID_ARG;
+    if (M == 0 || I == 0) return LSE_OK;
+    if (!x || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
+    if (ldx < K || ldy < I) return LSE_ERR_INVALID_ARG;
+    if (I % 8) return LSE_ERR_UNSUPPORTED;
+    if (M > 16 || 2 * I > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (K == 0) {  // silu(0) * 0
+        const cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(I) * 2,
+                                                static_cast<size_t>(M), st);
+        if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
+        return LSE_OK;
+    }
+    const int variant = skinny_variant();
+    const int num_sms = g_dev[dev].num_sms;
+    cudaError_t e = M <= 8 ? launch_skinny_mt<1, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, num_sms, st)
+                           : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, num_sms, st);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
 }

@@ -76,7 +76,14 @@ __device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
 // bounds-checked path.  `pf_groups` groups per row block beyond the U chunks in registers
 // are prefetched into L2 by lane 0 (bulk prefetches), which deepens the stream at no
 // register cost.
-template <int MT, int KW, int R, int U, bool BF16, int MINB>
+//
+// SILU_MUL: the weight rows interleave 8-row blocks of the MLP's gate and up projections
+// (row block b = gate rows 8b..8b+7, then the matching up rows 8b..8b+7), so the 16x8
+// accumulator of one lane holds gate row r0 (registers 0, 1) and up row r0 (registers 2, 3)
+// of the same tokens, and the epilogue writes y[m, 8b + r0] = silu(s_g * gate) * (s_u * up)
+// (fp32, one bf16 rounding) for the N = I intermediate columns; `scale` is interleaved the
+// same way.
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
 __global__ void __launch_bounds__(KW * 32, MINB)
 skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
@@ -262,6 +269,33 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                 red[warp][r][t][j][lane] = v;
             }
     __syncthreads();
+    if constexpr (SILU_MUL) {
+        // warp (r, jj) = (warp >> 1, warp & 1) finishes row block r: gate row r0 (register jj)
+        // and up row r0 (register 2 + jj), token 2q + jj of each tile.
+        if (warp < 2 * R) {
+            const int r = warp >> 1, jj = warp & 1;
+            const int b = rg * R + r;
+            const int n = b * 8 + r0;  // intermediate column
+            if (n < N) {
+                const float sg = __ldg(scale + b * 16 + r0), su = __ldg(scale + b * 16 + 8 + r0);
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    const int m = m0 + 8 * t + 2 * q + jj;
+                    if (m < M) {
+                        float vg = 0.f, vu = 0.f;
+#pragma unroll
+                        for (int w = 0; w < KW; ++w) {
+                            vg += red[w][r][t][jj][lane];
+                            vu += red[w][r][t][2 + jj][lane];
+                        }
+                        const float g = vg * sg, u = vu * su;
+                        y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
+                    }
+                }
+            }
+        }
+        return;
+    }
     // warp (r, j) = (warp >> 2, warp & 3) finishes accumulator register j of row block r:
     // row r0 + 8*(j>>1), token 2q + (j & 1) of each tile (16x8 accumulator layout).
     if (warp < 4 * R) {

@@ -19,8 +19,9 @@ with one activation `(1, M, hidden)`:
   projection once and `k_proj(x)` / `v_proj(x)` on the same `x` return column views of it,
   so callers that invoke the three projections in sequence (the runner, HF attention) run one
   kernel and stay unchanged;
-* `Int8LlamaMLP` replaces `layer.mlp`: one fused gate_up int8 projection (N = 2 * I), SiLU*mul,
-  and the int8 down projection - transformers' `LlamaMLP.forward`
+* `Int8LlamaMLP` replaces `layer.mlp`: one fused gate_up int8 projection (N = 2 * I, gate and
+  up rows interleaved in 8-row blocks), SiLU*mul (in the decode kernel's epilogue for up to
+  16 tokens), and the int8 down projection - transformers' `LlamaMLP.forward`
   (`down(act(gate(x)) * up(x))`).
 
 Weights are quantized on the GPU at load (`ops.quantize_per_channel`), once.  Activations
@@ -151,10 +152,20 @@ class FusedInt8QKV(nn.Module):
 
 
 class Int8LlamaMLP(nn.Module):
-    """`down(silu(gate(x)) * up(x))` with a fused int8 gate_up and an int8 down projection."""
+    """`down(silu(gate(x)) * up(x))` with a fused int8 gate_up and an int8 down projection.
 
-    def __init__(self, gate_up: Int8Linear, down: Int8Linear, intermediate: int, act=F.silu):
+    gate_up holds the gate and up rows interleaved in 8-row blocks (`ops.interleave_gate_up_rows`),
+    so for up to 16 tokens one kernel computes both projections and SiLU * mul
+    (`ops.int8_gate_up_silu_packed`); above that the tensor-core kernel computes the
+    interleaved [M, 2I] projection and the columns are paired here.
+    """
+
+    def __init__(self, gate_up: Int8Linear, down: Int8Linear, intermediate: int, act=F.silu,
+                 interleaved: bool = False):
         super().__init__()
+        if not interleaved:  # [gate; up] rows -> 16-row blocks interleaved
+            perm = ops.interleave_gate_up_rows(intermediate, device=gate_up.scale.device)
+            gate_up = Int8Linear.from_quantized(gate_up.weight.index_select(0, perm), gate_up.scale.index_select(0, perm))
         self.gate_up = gate_up
         self.down_proj = down
         self.intermediate_size = intermediate
@@ -170,10 +181,35 @@ class Int8LlamaMLP(nn.Module):
         gate_up = Int8Linear.from_float_weights(gate.weight, up.weight)
         return cls(gate_up, Int8Linear.from_linear(down), gate.out_features, act)
 
+    def _split(self, t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(gate rows, up rows) of an interleaved [2I, ...] tensor."""
+        v = t.view(self.intermediate_size // 8, 2, 8, *t.shape[1:])
+        return v[:, 0].reshape(self.intermediate_size, *t.shape[1:]), v[:, 1].reshape(self.intermediate_size, *t.shape[1:])
+
+    def gate_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Dequantized gate_proj weight [I, H]."""
+        return self._split(self.gate_up.dequantized(dtype))[0]
+
+    def up_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Dequantized up_proj weight [I, H]."""
+        return self._split(self.gate_up.dequantized(dtype))[1]
+
+    def _silu(self) -> bool:
+        # torch's SiLU, or transformers' SiLUActivation (ACT2FN["silu"], x * sigmoid(x))
+        return self.act is F.silu or type(self.act).__name__ in ("SiLU", "SiLUActivation")
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        gu = self.gate_up(x)
-        gate, up = gu.split(self.intermediate_size, dim=-1)
-        return self.down_proj(self.act(gate) * up)
+        I = self.intermediate_size
+        lead = x.shape[:-1]
+        x2 = _to_bf16(x).reshape(-1, x.shape[-1])
+        if x2.shape[0] <= ops.GATE_UP_SILU_MAX_M and self._silu():
+            h = ops.int8_gate_up_silu_packed(x2, self.gate_up.weight_packed, self.gate_up.scale, I,
+                                             self.gate_up.in_features)
+        else:
+            gu = self.gate_up(x2).view(-1, I // 8, 2, 8)
+            h = (self.act(gu[:, :, 0]) * gu[:, :, 1]).reshape(-1, I)
+        y = self.down_proj(h).reshape(*lead, -1)
+        return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
 def quantize_llama_(model: nn.Module, fuse: bool = True) -> nn.Module:

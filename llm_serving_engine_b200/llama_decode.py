@@ -25,7 +25,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from .int8_linear import Int8Linear
+from .int8_linear import Int8Linear, Int8LlamaMLP
 
 __all__ = ["LlamaShape", "LLAMA3_8B", "DecodeModel", "decode_bytes_per_step"]
 
@@ -69,6 +69,11 @@ def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
 
 
+def _bf16_mlp(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, inter: int) -> torch.Tensor:
+    gu = F.linear(x, w_gate_up)
+    return F.linear(F.silu(gu[:, :inter]) * gu[:, inter:], w_down)
+
+
 class DecodeModel:
     """Random-init Llama decoder for `batch` sequences at `context` cached positions."""
 
@@ -89,10 +94,16 @@ class DecodeModel:
         self.weights = weights if weights is not None else [
             (torch.cat([w(shape.heads * hd, H), w(2 * shape.kv_heads * hd, H)]), w(H, shape.heads * hd),
              torch.cat([w(I, H), w(I, H)]), w(H, I)) for _ in range(shape.layers)]
+        # per layer: (qkv, o, mlp) callables; the int8 MLP stores gate/up interleaved and runs
+        # the fused gate_up + SiLU * mul kernel for up to 16 sequences
         if quantize:
-            self.proj = [tuple(Int8Linear.from_float_weights(t) for t in layer) for layer in self.weights]
+            self.proj = [(Int8Linear.from_float_weights(wqkv), Int8Linear.from_float_weights(wo),
+                          Int8LlamaMLP(Int8Linear.from_float_weights(wgu), Int8Linear.from_float_weights(wd), I))
+                         for wqkv, wo, wgu, wd in self.weights]
         else:
-            self.proj = [tuple((lambda x, t=t: F.linear(x, t)) for t in layer) for layer in self.weights]
+            self.proj = [((lambda x, t=wqkv: F.linear(x, t)), (lambda x, t=wo: F.linear(x, t)),
+                          (lambda x, gu=wgu, d=wd: _bf16_mlp(x, gu, d, I)))
+                         for wqkv, wo, wgu, wd in self.weights]
         self.norms = [(torch.ones(H, device=dev, dtype=torch.bfloat16), torch.ones(H, device=dev, dtype=torch.bfloat16))
                       for _ in range(shape.layers)]
         # a prefilled context of `context` positions per sequence (+1 slot for the new token),
@@ -116,7 +127,7 @@ class DecodeModel:
         B, hd, pos = self.batch, s.head_dim, self.context
         h = self.embed[tokens]  # [B, H]
         for li in range(s.layers):
-            qkv_p, o_p, gu_p, down_p = self.proj[li]
+            qkv_p, o_p, mlp = self.proj[li]
             n_in, n_post = self.norms[li]
             x = _rms_norm(h, n_in, s.eps)
             qkv = qkv_p(x)
@@ -130,9 +141,17 @@ class DecodeModel:
             attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
             h = h + o_p(attn.reshape(B, s.heads * hd))
             x = _rms_norm(h, n_post, s.eps)
-            gu = gu_p(x)
-            h = h + down_p(F.silu(gu[:, :s.intermediate]) * gu[:, s.intermediate:])
+            h = h + mlp(x)
         return _rms_norm(h, self.final_norm, s.eps)
+
+    def dequantized_weights(self, dtype: torch.dtype = torch.bfloat16) -> list:
+        """Per layer the dequantized int8 weights in `weights` order ([q;k;v], o, [gate;up],
+        down): the bf16 twin that isolates the int8 kernels' arithmetic."""
+        if not self.quantize:
+            raise ValueError("dequantized_weights: the model is not quantized")
+        return [(qkv.dequantized(dtype), o.dequantized(dtype),
+                 torch.cat([mlp.gate_weight(dtype), mlp.up_weight(dtype)]), mlp.down_proj.dequantized(dtype))
+                for qkv, o, mlp in self.proj]
 
     def step(self, tokens: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step for every sequence; returns the greedy next tokens [B]."""

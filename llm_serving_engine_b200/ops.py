@@ -30,6 +30,9 @@ __all__ = [
     "unpack_weight",
     "packed_weight_bytes",
     "quantize_per_channel",
+    "interleave_gate_up_rows",
+    "int8_gate_up_silu_packed",
+    "GATE_UP_SILU_MAX_M",
     "workspace_for",
     "device_status",
     "ALGO_AUTO",
@@ -172,6 +175,52 @@ def int8_linear_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: torch.Ten
     if scale.dtype != torch.float32 or scale.shape != (N,):
         raise ValueError(f"int8_linear_packed: scale must be float32 [{N}]")
     return _launch(x, w_packed.data_ptr(), scale, N, K, out, algo, packed=True)
+
+
+GATE_UP_SILU_MAX_M = _lib.GATE_UP_SILU_MAX_M
+
+
+def interleave_gate_up_rows(intermediate: int, device=None) -> torch.Tensor:
+    """Row order of a fused [gate; up] weight (2 * intermediate rows) that interleaves 8-row
+    blocks: gate rows 8j..8j+7, then up rows 8j..8j+7, for every j (the layout
+    `int8_gate_up_silu_packed` reads: one 16-row block of the packed weight holds a gate row
+    and its up row in the same lane's accumulator)."""
+    if intermediate % 8:
+        raise ValueError(f"gate/up interleave: intermediate size {intermediate} is not a multiple of 8")
+    blk = torch.arange(intermediate, device=device).view(-1, 8)
+    return torch.stack([blk, blk + intermediate], dim=1).reshape(-1)
+
+
+def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: torch.Tensor, intermediate: int,
+                             K: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """`silu(x @ (Wg * sg).T) * (x @ (Wu * su).T)` for M <= 16 tokens in one kernel.  `w_packed`
+    is the packed layout of the gate/up rows in `interleave_gate_up_rows` order, `scale` the
+    scales in the same order; returns bf16 [..., intermediate]."""
+    _check_x(x, K, w_packed, scale)
+    I = intermediate
+    if w_packed.dtype != torch.int8 or w_packed.numel() != packed_weight_bytes(2 * I, K) or not w_packed.is_contiguous():
+        raise ValueError(f"int8_gate_up_silu_packed: w_packed must be the packed int8 buffer of [{2 * I}, {K}]")
+    if scale.dtype != torch.float32 or scale.shape != (2 * I,):
+        raise ValueError(f"int8_gate_up_silu_packed: scale must be float32 [{2 * I}]")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if M > GATE_UP_SILU_MAX_M:
+        raise ValueError(f"int8_gate_up_silu_packed: M={M} > {GATE_UP_SILU_MAX_M}")
+    if out is None:
+        out = torch.empty((*lead, I), dtype=torch.bfloat16, device=x.device)
+    elif out.dtype != torch.bfloat16 or out.shape != (*lead, I) or not out.is_contiguous():
+        raise ValueError("int8_gate_up_silu_packed: out must be contiguous bf16 [..., intermediate]")
+    if M == 0:
+        return out
+    _ensure_device(x.device)
+    stream = torch.cuda.current_stream(x.device)
+    rc = _lib.load().lse_int8_gate_up_silu_packed(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
+                                                  scale.data_ptr(), I, out.data_ptr(), I, stream.cuda_stream)
+    _lib.check(rc, "lse_int8_gate_up_silu_packed")
+    return out
 
 
 def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -15,12 +15,13 @@ pytestmark = pytest.mark.gpu
 TINY = LlamaShape(layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=512, vocab=1000)
 
 
-def test_int8_step_matches_dequantized_bf16_step():
-    base = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=False)
-    q8 = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=True, weights=base.weights)
-    deq = [tuple(p.dequantized(torch.bfloat16) for p in layer) for layer in q8.proj]
-    ref = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=3, quantize=False, weights=deq)
-    tokens = torch.tensor([1, 7, 99, 512], device="cuda")
+@pytest.mark.parametrize("batch", [4, 24])  # fused gate_up + SiLU * mul kernel / tensor-core projection
+def test_int8_step_matches_dequantized_bf16_step(batch):
+    base = DecodeModel(TINY, batch=batch, context=16, device="cuda", seed=3, quantize=False)
+    q8 = DecodeModel(TINY, batch=batch, context=16, device="cuda", seed=3, quantize=True, weights=base.weights)
+    deq = q8.dequantized_weights(torch.bfloat16)
+    ref = DecodeModel(TINY, batch=batch, context=16, device="cuda", seed=3, quantize=False, weights=deq)
+    tokens = (torch.arange(batch, device="cuda") * 37) % TINY.vocab
     a, b = q8.logits(tokens), ref.logits(tokens)
     err = ((a - b).abs().max() / b.abs().max()).item()
     assert np.isfinite(err) and err < 2e-2, err

@@ -98,10 +98,8 @@ def test_quantized_hf_llama_matches_dequantized_float_model():
         lf.self_attn.k_proj.weight.copy_(w[sq:sq + sk])
         lf.self_attn.v_proj.weight.copy_(w[sq + sk:])
         lf.self_attn.o_proj.weight.copy_(lq.self_attn.o_proj.dequantized())
-        gu = lq.mlp.gate_up.dequantized()
-        I = lq.mlp.intermediate_size
-        lf.mlp.gate_proj.weight.copy_(gu[:I])
-        lf.mlp.up_proj.weight.copy_(gu[I:])
+        lf.mlp.gate_proj.weight.copy_(lq.mlp.gate_weight())
+        lf.mlp.up_proj.weight.copy_(lq.mlp.up_weight())
         lf.mlp.down_proj.weight.copy_(lq.mlp.down_proj.dequantized())
     twin.model.embed_tokens.weight.copy_(model.model.embed_tokens.weight.float())
     twin.lm_head.weight.copy_(model.lm_head.weight.float())

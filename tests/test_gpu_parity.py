@@ -252,3 +252,73 @@ def test_skinny_deterministic_and_linear(ws, M, K, N):
     c = _packed_call(xd * 2, packed, sd, N, K, ws, _lib.ALGO_SKINNY)
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(c, a * 2)
+
+
+# ---- fused gate_up + SiLU * mul (decode) ------------------------------------------------
+def _silu_mul_ref(x, qg, sg, qu, su):
+    g = ref_int8_linear(x, qg, sg)
+    u = ref_int8_linear(x, qu, su)
+    return (g / (1.0 + np.exp(-g))) * u
+
+
+@pytest.mark.parametrize("M,K,I", [(1, 256, 512), (3, 512, 200), (5, 272, 496), (8, 4096, 2048), (9, 1024, 1024),
+                                   (13, 208, 1032), (16, 4096, 14336)])
+def test_gate_up_silu_fused_parity(M, K, I):
+    g = torch.Generator().manual_seed(M + K + I)
+    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16)
+    qg = torch.randint(-127, 128, (I, K), generator=g, dtype=torch.int8)
+    qu = torch.randint(-127, 128, (I, K), generator=g, dtype=torch.int8)
+    sg = torch.empty(I).uniform_(1e-4, 5e-4, generator=g)
+    su = torch.empty(I).uniform_(1e-4, 5e-4, generator=g)
+    perm = ops.interleave_gate_up_rows(I)
+    q = torch.cat([qg, qu]).index_select(0, perm)
+    s = torch.cat([sg, su]).index_select(0, perm)
+    packed = ops.pack_weight(q.cuda())
+    y = ops.int8_gate_up_silu_packed(x.cuda(), packed, s.cuda(), I, K)
+    torch.cuda.synchronize()
+    cols = np.arange(I) if I <= 2048 else np.unique(np.random.default_rng(0).choice(I, 2048, replace=False))
+    ref = _silu_mul_ref(x.float().numpy(), qg.numpy()[cols], sg.numpy()[cols], qu.numpy()[cols], su.numpy()[cols])
+    check_parity(y[:, torch.as_tensor(cols, device="cuda")], ref, f"gate_up silu M={M} K={K} I={I}")
+    assert ops.device_status() == 0
+
+
+def test_gate_up_silu_fused_limits():
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.zeros(17, 64, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(ops.packed_weight_bytes(64, 64), dtype=torch.int8, device="cuda")
+    s = torch.ones(64, device="cuda")
+    y = torch.empty(17, 32, dtype=torch.bfloat16, device="cuda")
+    assert lib.lse_int8_gate_up_silu_packed(x.data_ptr(), 17, 64, 64, w.data_ptr(), s.data_ptr(), 32, y.data_ptr(), 32,
+                                            st) == _lib.LSE_ERR_UNSUPPORTED
+    assert lib.lse_int8_gate_up_silu_packed(x.data_ptr(), 4, 64, 64, w.data_ptr(), s.data_ptr(), 20, y.data_ptr(), 32,
+                                            st) == _lib.LSE_ERR_UNSUPPORTED  # I % 8
+    # K == 0: silu(0) * 0 = 0
+    y.fill_(1.0)
+    assert lib.lse_int8_gate_up_silu_packed(x.data_ptr(), 4, 0, 64, w.data_ptr(), s.data_ptr(), 32, y.data_ptr(), 32,
+                                            st) == _lib.LSE_OK
+    torch.cuda.synchronize()
+    assert torch.all(y[:4] == 0)
+
+
+@pytest.mark.parametrize("M", [3, 16, 40])
+def test_mlp_module_fused_and_unfused_paths(M):
+    """Int8LlamaMLP takes the fused kernel for M <= 16 and the tensor-core path above; both
+    against the fp64 MLP oracle."""
+    from llm_serving_engine_b200.int8_linear import Int8LlamaMLP
+    from oracle.ref_linear import ref_mlp
+    H, I = 512, 1024
+    g = torch.Generator().manual_seed(M)
+    qg, qu = (torch.randint(-127, 128, (I, H), generator=g, dtype=torch.int8) for _ in range(2))
+    qd = torch.randint(-127, 128, (H, I), generator=g, dtype=torch.int8)
+    sg, su = (torch.empty(I).uniform_(1e-4, 5e-4, generator=g) for _ in range(2))
+    sd = torch.empty(H).uniform_(1e-4, 5e-4, generator=g)
+    from llm_serving_engine_b200.int8_linear import Int8Linear
+    mlp = Int8LlamaMLP(Int8Linear.from_quantized(torch.cat([qg, qu]).cuda(), torch.cat([sg, su]).cuda()),
+                       Int8Linear.from_quantized(qd.cuda(), sd.cuda()), I)
+    assert torch.equal(mlp.gate_weight().cpu(), (qg.float() * sg[:, None]))
+    x = (torch.randn(M, H, generator=g) * 4).to(torch.bfloat16)
+    y = mlp(x.cuda()).float().cpu().numpy()
+    ref = ref_mlp(x.float().numpy(), qg.numpy(), sg.numpy(), qu.numpy(), su.numpy(), qd.numpy(), sd.numpy())
+    # the bf16 rounding of the intermediate between the two projections adds ~1e-2
+    assert np.max(np.abs(y - ref)) / np.max(np.abs(ref)) < 2e-2
