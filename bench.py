@@ -374,6 +374,42 @@ def fused_gate_up(weights, dev, warm, ops, hbm_peak):
     return out
 
 
+def fused_residual(weights, dev, warm, ops):
+    """The decoder's residual add fused into the projection epilogue (o_proj and down, whose
+    outputs are added to the residual stream): `int8_linear_packed(..., residual=h)` vs the
+    projection followed by torch's add, at M in 1, 4, 16, 64 over every layer's weight."""
+    gx = torch.Generator(device=dev).manual_seed(19)
+    out = {"workload": f"Llama-3-8B o (4096x4096) and down (14336x4096), {len(weights)} layers' weights per graph",
+           "points": []}
+    for name in ("o", "down"):
+        K, N = LLAMA3_8B_SHAPES[name]
+        for M in DECODE_M:
+            x = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
+            h = torch.randn(M, N, generator=gx, device=dev).to(torch.bfloat16)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            h2 = torch.empty_like(h)
+
+            def fused(x=x, h=h, h2=h2, name=name, N=N, K=K):
+                for layer in weights:
+                    wp, s = layer[name]
+                    ops.int8_linear_packed(x, wp, s, N, K, out=h2, residual=h)
+
+            def unfused(x=x, h=h, y=y, h2=h2, name=name, N=N, K=K):
+                for layer in weights:
+                    wp, s = layer[name]
+                    ops.int8_linear_packed(x, wp, s, N, K, out=y)
+                    torch.add(h, y, out=h2)
+            pt = {"shape": name, "M": M}
+            for tag, fn in (("fused", fused), ("unfused", unfused)):
+                g = capture(fn, warm)
+                time_graph(g, 2)
+                pt[tag + "_us"] = round(time_graph(g, 10) / len(weights) * 1e3, 3)
+                del g
+            pt["speedup"] = round(pt["unfused_us"] / pt["fused_us"], 3)
+            out["points"].append(pt)
+    return out
+
+
 # --------------------------------------------------------------------------------------
 def cpu_reference_sample(seconds: float):
     """The reference's CPU path (float32 nn.Linear on the dequantized weight, all host
@@ -578,6 +614,7 @@ def main():
                    "points": pre_pts}
 
     fused_mlp = fused_gate_up(weights, dev, warm, ops, hbm_peak)
+    fused_res = fused_residual(weights, dev, warm, ops)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
@@ -630,6 +667,7 @@ def main():
         if prefill:
             line["prefill"] = prefill
         line["fused_gate_up_silu"] = fused_mlp
+        line["fused_residual"] = fused_res
         if tp70b:
             line["config5_70b_column_split"] = tp70b
         if decode4:

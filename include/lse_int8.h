@@ -113,6 +113,23 @@ int lse_int8_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx,
                            int algo, void *stream);
 
 /*
+ * y[m, n] = bf16( residual[m, n] + s[n] * sum_k x[m,k] * W[n,k] )
+ *
+ * lse_int8_linear_packed with the decoder layer's residual add fused into the epilogue (the
+ * `hidden = residual + o_proj(...)` and `hidden = residual + mlp(...)` steps of transformers'
+ * LlamaDecoderLayer.forward, reached at model_runner.py:213-224): the sum is formed in fp32
+ * and rounded to bf16 once.  residual: bf16 [M, N], row stride ldr (>= N), 2-byte aligned;
+ * it may be y itself (residual == y and ldr == ldy: in-place update), other overlaps are
+ * not allowed.  residual == NULL is LSE_ERR_INVALID_ARG.  All algorithms (LSE_ALGO_*).
+ */
+int lse_int8_linear_packed_residual(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                    const int8_t *w_packed, const float *scale, int64_t N,
+                                    const void *residual, int64_t ldr,
+                                    void *y, int64_t ldy,
+                                    void *workspace, size_t workspace_bytes,
+                                    int algo, void *stream);
+
+/*
  * y[m, i] = bf16( silu(s_g[i] * sum_k x[m,k] * w_g[i,k]) * (s_u[i] * sum_k x[m,k] * w_u[i,k]) )
  *
  * The Llama MLP's gate and up projections and SiLU * mul (transformers' LlamaMLP.forward,

@@ -49,6 +49,8 @@ SIGNATURES = {
     "lse_int8_linear_ex": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
     "lse_int8_linear_workspace": ([_I64, _I64, _I64], _SZ),
     "lse_int8_linear_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
+    "lse_int8_linear_packed_residual": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _P, _SZ, _I32, _P],
+                                        _I32),
     "lse_int8_linear_packed_noalloc": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "lse_int8_gate_up_silu_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "lse_int8_packed_weight_bytes": ([_I64, _I64], _SZ),

@@ -182,7 +182,8 @@ int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
 
 template <int NT>
 int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
-              const float *scale, int64_t N, void *y, int64_t ldy, void *ws, bool packed, cudaStream_t st) {
+              const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
+              cudaStream_t st) {
     CUtensorMap tw, tx;
     // Packed W: [Np/16 row blocks][16*Kp bytes] as 8-byte elements, box = one 128 x 128 tile
     // (8 row blocks x 2 KB), no swizzle.  Row-major W: [N][K] bytes, 128 x 128 box, 128B swizzle.
@@ -200,6 +201,8 @@ int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx
     p.K = static_cast<int>(K);
     p.y = static_cast<__nv_bfloat16 *>(y);
     p.ldy = ldy;
+    p.res = static_cast<const __nv_bfloat16 *>(res);
+    p.ldr = ldr;
     p.scale = scale;
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + LSE_WS_COUNTER_BYTES);
@@ -261,7 +264,7 @@ int skinny_prefetch_groups() {
 
 template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
-                          int64_t N, void *y, int64_t ldy, cudaStream_t st) {
+                          int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, cudaStream_t st) {
     const int64_t row_blocks = SILU_MUL ? N / 8 : (N + 15) / 16;  // weight row blocks (SILU_MUL: 2N rows)
     dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
     cudaLaunchConfig_t cfg = {};
@@ -269,7 +272,8 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
     launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
     return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL>, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
-                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<int>(packed_cols(K)),
+                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<const __nv_bfloat16 *>(res), ldr,
+                              static_cast<int>(packed_cols(K)),
                               MT == 1 ? skinny_prefetch_groups() : 0);
 }
 
@@ -295,7 +299,8 @@ int skinny_variant() {
 // rows, which set the shape tier.
 template <int MT, bool SILU = false>
 cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp,
-                             const float *scale, int64_t N, void *y, int64_t ldy, int num_sms, cudaStream_t st) {
+                             const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr,
+                             int num_sms, cudaStream_t st) {
     if (variant < 0) {
         const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
         variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 5) : (rb_per_sm >= 2 ? 1 : 0);
@@ -303,24 +308,24 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
         switch (variant) {
-            case 1: return launch_skinny<4, 8, 2, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 2: return launch_skinny<4, 16, 1, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            default: return launch_skinny<4, 8, 1, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 1: return launch_skinny<4, 8, 2, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 2: return launch_skinny<4, 16, 1, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            default: return launch_skinny<4, 8, 1, 4, true, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
         }
     } else {
         constexpr bool BF = MT == 2;
         switch (variant) {
-            case 1: return launch_skinny<MT, 8, 2, 4, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 4: return launch_skinny<MT, 16, 2, 4, BF, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 5: return launch_skinny<MT, 8, 2, 2, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 6: return launch_skinny<MT, 8, 2, 4, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 7: return launch_skinny<MT, 8, 1, 4, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-            case 8: return launch_skinny<MT, 16, 1, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+            case 1: return launch_skinny<MT, 8, 2, 4, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 2: return launch_skinny<MT, 16, 1, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 3: return launch_skinny<MT, 8, 2, 4, !BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 4: return launch_skinny<MT, 16, 2, 4, BF, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 5: return launch_skinny<MT, 8, 2, 2, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 6: return launch_skinny<MT, 8, 2, 4, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 7: return launch_skinny<MT, 8, 1, 4, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 8: return launch_skinny<MT, 16, 1, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             default:
-                if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
-                else return launch_skinny<2, 16, 2, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, st);
+                if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+                else return launch_skinny<2, 16, 2, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
         }
     }
 }
@@ -328,12 +333,12 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
 constexpr int64_t kSkinnyMaxM = 32;  // the decode kernel's token range (four 8-token tiles)
 
 int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale, int64_t N,
-               void *y, int64_t ldy, int num_sms, cudaStream_t st) {
+               void *y, int64_t ldy, const void *res, int64_t ldr, int num_sms, cudaStream_t st) {
     if (M > kSkinnyMaxM) return LSE_ERR_UNSUPPORTED;
     const int variant = skinny_variant();
-    cudaError_t e = M <= 8    ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
-                    : M <= 16 ? launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st)
-                              : launch_skinny_mt<4>(variant, x, M, K, ldx, wp, scale, N, y, ldy, num_sms, st);
+    cudaError_t e = M <= 8    ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+                    : M <= 16 ? launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+                              : launch_skinny_mt<4>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -385,8 +390,12 @@ size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N) {
 
 namespace lse {
 namespace {
+// res (may be null): y = bf16(res + s * acc), res bf16 [M, N] with row stride ldr; res may be
+// y itself (same pointer and stride): every element is read before it is written, by the
+// same thread.
 int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale, int64_t N,
-                void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo, bool packed, void *stream) {
+                void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo, bool packed, void *stream,
+                const void *res = nullptr, int64_t ldr = 0) {
     if (M < 0 || N < 0 || K < 0) return LSE_ERR_INVALID_ARG;
     if (M == 0 || N == 0) return LSE_OK;
     if (!x || !w || !scale || !y) return LSE_ERR_INVALID_ARG;
@@ -394,27 +403,34 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
     if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w)) return LSE_ERR_ALIGNMENT;
     if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
+    if (res && (ldr < N || (reinterpret_cast<uintptr_t>(res) & 1u))) return ldr < N ? LSE_ERR_INVALID_ARG : LSE_ERR_ALIGNMENT;
+    if (res == y && ldr != ldy) return LSE_ERR_INVALID_ARG;  // in place only element for element
     if (algo < LSE_ALGO_AUTO || algo > LSE_ALGO_SKINNY) return LSE_ERR_INVALID_ARG;
     if ((algo == LSE_ALGO_GEMV && packed) || (algo == LSE_ALGO_SKINNY && !packed)) return LSE_ERR_UNSUPPORTED;
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (K == 0) {
-        cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(N) * 2,
-                                          static_cast<size_t>(M), st);
-        if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
+    if (K == 0) {  // y = 0, or y = res
+        cudaError_t e = cudaSuccess;
+        if (!res) e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(N) * 2,
+                                        static_cast<size_t>(M), st);
+        else if (res != y)
+            e = cudaMemcpy2DAsync(y, static_cast<size_t>(ldy) * 2, res, static_cast<size_t>(ldr) * 2,
+                                  static_cast<size_t>(N) * 2, static_cast<size_t>(M), cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) { set_cuda_error(e, "K == 0 output"); return LSE_ERR_CUDA; }
         return LSE_OK;
     }
     if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed);
-    if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);
-    if (algo == LSE_ALGO_SKINNY) return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, g_dev[dev].num_sms, st);
+    if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);  // row-major: no res
+    if (algo == LSE_ALGO_SKINNY)
+        return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, res, ldr, g_dev[dev].num_sms, st);
 
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
         return LSE_ERR_WORKSPACE;
-    if (pl.nt == 64) return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
-    return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, workspace, packed, st);
+    if (pl.nt == 64) return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
+    return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
 }
 }  // namespace
 }  // namespace lse
@@ -437,6 +453,14 @@ int lse_int8_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx, con
                            const float *scale, int64_t N, void *y, int64_t ldy, void *workspace,
                            size_t workspace_bytes, int algo, void *stream) {
     return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, workspace, workspace_bytes, algo, true, stream);
+}
+
+int lse_int8_linear_packed_residual(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                                    const float *scale, int64_t N, const void *residual, int64_t ldr, void *y,
+                                    int64_t ldy, void *workspace, size_t workspace_bytes, int algo, void *stream) {
+    if (!residual) return LSE_ERR_INVALID_ARG;
+    return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, workspace, workspace_bytes, algo, true, stream,
+                       residual, ldr);
 }
 
 size_t lse_int8_packed_weight_bytes(int64_t N, int64_t K) {
@@ -644,8 +668,8 @@ extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K,
     }
     const int variant = skinny_variant();
     const int num_sms = g_dev[dev].num_sms;
-    cudaError_t e = M <= 8 ? launch_skinny_mt<1, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, num_sms, st)
-                           : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, num_sms, st);
+    cudaError_t e = M <= 8 ? launch_skinny_mt<1, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st)
+                           : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
     return LSE_OK;

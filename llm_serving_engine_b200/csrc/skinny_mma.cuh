@@ -63,6 +63,9 @@ __device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
     return r;
 }
 
+// y = bf16(s * acc), or bf16(res + s * acc) when `res` is given (it may be y itself: each
+// element is read, then written, by one thread).
+//
 // MT token tiles of 8 per CTA (M <= 8 * MT), KW warps splitting K, R row blocks per CTA
 // (sharing every activation load), U chunks per row block in flight per lane, BF16 selects
 // the bf16 MMA.
@@ -87,7 +90,7 @@ template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = fal
 __global__ void __launch_bounds__(KW * 32, MINB)
 skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
-                 __nv_bfloat16 *__restrict__ y, int64_t ldy, int Kp, int pf_groups) {
+                 __nv_bfloat16 *y, int64_t ldy, const __nv_bfloat16 *res, int64_t ldr, int Kp, int pf_groups) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int rg = blockIdx.x;
     const int m0 = blockIdx.y * MT * 8;
@@ -310,7 +313,9 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                     float v = 0.f;
 #pragma unroll
                     for (int w = 0; w < KW; ++w) v += red[w][r][t][j][lane];
-                    y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(v * sc);
+                    v *= sc;
+                    if (res) v += __bfloat162float(res[static_cast<int64_t>(m) * ldr + n]);
+                    y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(v);
                 }
             }
         }

@@ -14,7 +14,8 @@
 //   * x (bf16) arrives by TMA (128-byte swizzle, K-major) and is the B operand, read by the
 //     MMA through a shared-memory descriptor.
 //   * The fp32 accumulator lives in TMEM (double-buffered when it fits) and four epilogue
-//     warps read it with tcgen05.ld, apply s[n] and store bf16 y.
+//     warps read it with tcgen05.ld, apply s[n] (and add the optional residual) and store
+//     bf16 y.
 //
 // Warp roles (512 threads): warp 0 TMA producer, warp 1 TMEM allocator + single-thread MMA
 // issuer, warp 2 L2 prefetcher for the weight stream, warps 4-7 epilogue (TMEM lane quarter = warp % 4), warps 8-15 converters (two
@@ -84,6 +85,8 @@ struct Params {
     int M, N, K;
     __nv_bfloat16 *y;
     int64_t ldy;
+    const __nv_bfloat16 *res;  // null, or the residual added before rounding (may alias y)
+    int64_t ldr;
     const float *scale;
     float *partials;   // [2 * grid][NT][BN] fp32 partial tiles
     int *counters;     // [stream-K tiles] arrival counters, zero between launches
@@ -526,9 +529,11 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 if (whole) {
 #pragma unroll
                     for (int j = 0; j < CH; ++j) {
-                        if (n_ok && c0 + j < mval)
-                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + n] =
-                                __float2bfloat16_rn(__uint_as_float(v[j]) * sc);
+                        if (n_ok && c0 + j < mval) {
+                            float o = __uint_as_float(v[j]) * sc;
+                            if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + c0 + j) * p.ldr + n]);
+                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + n] = __float2bfloat16_rn(o);
+                        }
                     }
                 } else {
                     // partial tile layout [token j][row]: one 128-byte line per warp per j
@@ -631,7 +636,11 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                 const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    if (n + e < p.N) yr[e] = __float2bfloat16_rn(a4[e] * __ldg(p.scale + n + e));
+                    if (n + e < p.N) {
+                        float o = a4[e] * __ldg(p.scale + n + e);
+                        if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
+                        yr[e] = __float2bfloat16_rn(o);
+                    }
             }
         }
     }

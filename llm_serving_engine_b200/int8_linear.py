@@ -89,8 +89,13 @@ class Int8Linear(nn.Module):
     def dequantized(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         return (self.weight.to(torch.float32) * self.scale[:, None]).to(dtype)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = ops.int8_linear_packed(_to_bf16(x), self.weight_packed, self.scale, self.out_features, self.in_features)
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """`x @ W.T`, or `residual + x @ W.T` rounded once (the decoder's residual add fused
+        into the kernel; bf16 models only)."""
+        if residual is not None and x.dtype != torch.bfloat16:
+            return residual + self.forward(x)
+        y = ops.int8_linear_packed(_to_bf16(x), self.weight_packed, self.scale, self.out_features, self.in_features,
+                                   residual=residual)
         return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
     def extra_repr(self) -> str:
@@ -198,7 +203,11 @@ class Int8LlamaMLP(nn.Module):
         # torch's SiLU, or transformers' SiLUActivation (ACT2FN["silu"], x * sigmoid(x))
         return self.act is F.silu or type(self.act).__name__ in ("SiLU", "SiLUActivation")
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """`down(act(gate(x)) * up(x))`, plus `residual` added in the down projection's
+        epilogue when given (bf16)."""
+        if residual is not None and x.dtype != torch.bfloat16:
+            return residual + self.forward(x)
         I = self.intermediate_size
         lead = x.shape[:-1]
         x2 = _to_bf16(x).reshape(-1, x.shape[-1])
@@ -208,7 +217,8 @@ class Int8LlamaMLP(nn.Module):
         else:
             gu = self.gate_up(x2).view(-1, I // 8, 2, 8)
             h = (self.act(gu[:, :, 0]) * gu[:, :, 1]).reshape(-1, I)
-        y = self.down_proj(h).reshape(*lead, -1)
+        r2 = None if residual is None else residual.reshape(-1, residual.shape[-1])
+        y = self.down_proj(h, residual=r2).reshape(*lead, -1)
         return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 

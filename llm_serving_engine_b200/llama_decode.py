@@ -94,15 +94,16 @@ class DecodeModel:
         self.weights = weights if weights is not None else [
             (torch.cat([w(shape.heads * hd, H), w(2 * shape.kv_heads * hd, H)]), w(H, shape.heads * hd),
              torch.cat([w(I, H), w(I, H)]), w(H, I)) for _ in range(shape.layers)]
-        # per layer: (qkv, o, mlp) callables; the int8 MLP stores gate/up interleaved and runs
-        # the fused gate_up + SiLU * mul kernel for up to 16 sequences
+        # per layer: (qkv, o, mlp) callables, o and mlp taking the residual stream; the int8
+        # modules add it in their kernels' epilogue, and the int8 MLP stores gate/up
+        # interleaved and runs the fused gate_up + SiLU * mul kernel for up to 16 sequences
         if quantize:
             self.proj = [(Int8Linear.from_float_weights(wqkv), Int8Linear.from_float_weights(wo),
                           Int8LlamaMLP(Int8Linear.from_float_weights(wgu), Int8Linear.from_float_weights(wd), I))
                          for wqkv, wo, wgu, wd in self.weights]
         else:
-            self.proj = [((lambda x, t=wqkv: F.linear(x, t)), (lambda x, t=wo: F.linear(x, t)),
-                          (lambda x, gu=wgu, d=wd: _bf16_mlp(x, gu, d, I)))
+            self.proj = [((lambda x, t=wqkv: F.linear(x, t)), (lambda x, t=wo, residual=None: residual + F.linear(x, t)),
+                          (lambda x, gu=wgu, d=wd, residual=None: residual + _bf16_mlp(x, gu, d, I)))
                          for wqkv, wo, wgu, wd in self.weights]
         self.norms = [(torch.ones(H, device=dev, dtype=torch.bfloat16), torch.ones(H, device=dev, dtype=torch.bfloat16))
                       for _ in range(shape.layers)]
@@ -139,9 +140,9 @@ class DecodeModel:
             kc[:, :, pos] = k
             vc[:, :, pos] = v
             attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
-            h = h + o_p(attn.reshape(B, s.heads * hd))
+            h = o_p(attn.reshape(B, s.heads * hd), residual=h)  # residual + o_proj(attn)
             x = _rms_norm(h, n_post, s.eps)
-            h = h + mlp(x)
+            h = mlp(x, residual=h)
         return _rms_norm(h, self.final_norm, s.eps)
 
     def dequantized_weights(self, dtype: torch.dtype = torch.bfloat16) -> list:

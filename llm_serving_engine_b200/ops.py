@@ -95,7 +95,8 @@ def _check_x(x: torch.Tensor, K: int, *tensors: torch.Tensor) -> None:
         raise ValueError(f"int8_linear: in_features must be a multiple of 16, got {K}")
 
 
-def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, out, algo: int, packed: bool):
+def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, out, algo: int, packed: bool,
+            residual: torch.Tensor | None = None):
     lead = x.shape[:-1]
     x2 = x.reshape(-1, K)
     if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
@@ -109,12 +110,26 @@ def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, ou
             raise ValueError("int8_linear: out must be bf16 [..., N] with a contiguous last dim")
         y = out
         y2 = out.view(-1, N) if M > 0 else out.reshape(0, N)
+    r2 = None
+    if residual is not None:
+        if (residual.dtype != torch.bfloat16 or residual.device != x.device or residual.shape != (*lead, N)
+                or residual.stride(-1) != 1):
+            raise ValueError("int8_linear: residual must be bf16 [..., N] on x's device with a contiguous last dim")
+        r2 = residual.view(-1, N) if M > 0 else None
     if M == 0:
         return y
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
     ws = workspace_for(x.device, stream)
     lib = _lib.load()
+    if r2 is not None:
+        if r2.data_ptr() == y2.data_ptr() and r2.stride(0) != y2.stride(0):
+            raise ValueError("int8_linear: residual and out overlap with different strides")
+        rc = lib.lse_int8_linear_packed_residual(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N,
+                                                 r2.data_ptr(), r2.stride(0), y2.data_ptr(), y2.stride(0),
+                                                 ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
+        _lib.check(rc, "lse_int8_linear_packed_residual")
+        return y
     fn = lib.lse_int8_linear_packed if packed else lib.lse_int8_linear_ex
     rc = fn(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N, y2.data_ptr(), y2.stride(0),
             ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
@@ -167,14 +182,17 @@ def unpack_weight(packed: torch.Tensor, N: int, K: int) -> torch.Tensor:
 
 
 def int8_linear_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: torch.Tensor, N: int, K: int,
-                       out: torch.Tensor | None = None, algo: int = ALGO_AUTO) -> torch.Tensor:
-    """int8_linear with the weight in the packed layout (`pack_weight`)."""
+                       out: torch.Tensor | None = None, algo: int = ALGO_AUTO,
+                       residual: torch.Tensor | None = None) -> torch.Tensor:
+    """int8_linear with the weight in the packed layout (`pack_weight`).  With `residual`
+    (bf16 [..., N]) the result is bf16(residual + x @ (W * s).T), rounded once; `residual`
+    may be `out` itself (an in-place residual update)."""
     _check_x(x, K, w_packed, scale)
     if w_packed.dtype != torch.int8 or w_packed.numel() != packed_weight_bytes(N, K) or not w_packed.is_contiguous():
         raise ValueError(f"int8_linear_packed: w_packed must be the contiguous packed int8 buffer of [{N}, {K}]")
     if scale.dtype != torch.float32 or scale.shape != (N,):
         raise ValueError(f"int8_linear_packed: scale must be float32 [{N}]")
-    return _launch(x, w_packed.data_ptr(), scale, N, K, out, algo, packed=True)
+    return _launch(x, w_packed.data_ptr(), scale, N, K, out, algo, packed=True, residual=residual)
 
 
 GATE_UP_SILU_MAX_M = _lib.GATE_UP_SILU_MAX_M

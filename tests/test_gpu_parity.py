@@ -322,3 +322,55 @@ def test_mlp_module_fused_and_unfused_paths(M):
     ref = ref_mlp(x.float().numpy(), qg.numpy(), sg.numpy(), qu.numpy(), su.numpy(), qd.numpy(), sd.numpy())
     # the bf16 rounding of the intermediate between the two projections adds ~1e-2
     assert np.max(np.abs(y - ref)) / np.max(np.abs(ref)) < 2e-2
+
+
+# ---- residual add fused into the epilogue ------------------------------------------------
+@pytest.mark.parametrize("M,K,N,algo", [
+    (1, 4096, 1024, ops.ALGO_AUTO),      # skinny, fp16 MMA
+    (5, 1040, 528, ops.ALGO_AUTO),       # skinny, ragged K and N
+    (16, 2048, 2048, ops.ALGO_AUTO),     # skinny, bf16 MMA
+    (24, 1024, 1024, ops.ALGO_SKINNY),   # skinny, four token tiles
+    (64, 8192, 1024, ops.ALGO_AUTO),     # tensor cores, stream-K reductions
+    (300, 2048, 2176, ops.ALGO_AUTO),    # tensor cores, 128-token tiles
+])
+def test_residual_epilogue_parity(M, K, N, algo):
+    x, w, s = make_inputs(M, K, N, seed=M * 7 + N)
+    g = torch.Generator().manual_seed(M + K)
+    res = (torch.randn(M, N, generator=g) * 0.05).to(torch.bfloat16)
+    wp = ops.pack_weight(w.cuda())
+    y = ops.int8_linear_packed(x.cuda(), wp, s.cuda(), N, K, algo=algo, residual=res.cuda())
+    torch.cuda.synchronize()
+    ref = ref_int8_linear(x.float().numpy(), w.numpy(), s.numpy()) + res.double().numpy()
+    check_parity(y, ref, f"residual M={M} K={K} N={N}")
+    # in place: the residual stream is updated where it lies
+    h = res.cuda().clone()
+    out = ops.int8_linear_packed(x.cuda(), wp, s.cuda(), N, K, algo=algo, residual=h, out=h)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == h.data_ptr()
+    assert torch.equal(h, y)
+    assert ops.device_status() == 0
+
+
+def test_residual_argument_errors():
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.zeros(4, 64, dtype=torch.bfloat16, device="cuda")
+    wp = torch.zeros(ops.packed_weight_bytes(64, 64), dtype=torch.int8, device="cuda")
+    s = torch.ones(64, device="cuda")
+    y = torch.empty(4, 64, dtype=torch.bfloat16, device="cuda")
+    ws = ops.workspace_for(x.device)
+    args = (x.data_ptr(), 4, 64, 64, wp.data_ptr(), s.data_ptr(), 64)
+    tail = (ws.data_ptr(), ws.numel(), ops.ALGO_AUTO, st)
+    assert lib.lse_int8_linear_packed_residual(*args, None, 64, y.data_ptr(), 64, *tail) == _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_int8_linear_packed_residual(*args, y.data_ptr(), 32, y.data_ptr(), 64, *tail) == _lib.LSE_ERR_INVALID_ARG
+    r = torch.empty(4, 128, dtype=torch.bfloat16, device="cuda")
+    # same pointer as y with another row stride would overlap element for element differently
+    assert lib.lse_int8_linear_packed_residual(*args, y.data_ptr(), 128, y.data_ptr(), 64, *tail) == _lib.LSE_ERR_INVALID_ARG
+    # K == 0: y = residual
+    r[:, :64] = 3.0
+    assert lib.lse_int8_linear_packed_residual(x.data_ptr(), 4, 0, 64, wp.data_ptr(), s.data_ptr(), 64, r.data_ptr(), 128,
+                                               y.data_ptr(), 64, *tail) == _lib.LSE_OK
+    torch.cuda.synchronize()
+    assert torch.all(y == 3.0)
+    with pytest.raises(ValueError):
+        ops.int8_linear_packed(x, wp, s, 64, 64, residual=torch.zeros(4, 32, dtype=torch.bfloat16, device="cuda"))
