@@ -320,16 +320,18 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
                        "vocab 128256), random init, 64 sequences, 1024-token context, greedy, CUDA graph per step; "
                        "attention: torch SDPA over a contiguous KV cache",
            "unit": "tokens/s"}
-    for name, m in (("int8", q8), ("none", base)):
+    for name, m in (("int8", q8), ("int8_lm_head", q8), ("none", base)):
+        q8.set_lm_head_int8(name == "int8_lm_head")
         g = capture(m.step, warm)
         time_graph(g, 3)
         ms = time_graph(g, steps)
-        byts = decode_bytes_per_step(LLAMA3_8B, B, ctx, name == "int8")
+        byts = decode_bytes_per_step(LLAMA3_8B, B, ctx, name != "none", int8_lm_head=name == "int8_lm_head")
         out[name] = {"tokens_per_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
                      "bytes_per_step": byts, "GBps": round(byts / ms / 1e6, 1),
                      "frac_of_hbm": round(byts / ms / 1e6 / hbm_peak, 4)}
         del g
     out["int8_speedup"] = round(out["int8"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
+    out["int8_lm_head_speedup"] = round(out["int8_lm_head"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
     del base, q8
     torch.cuda.empty_cache()
     return out

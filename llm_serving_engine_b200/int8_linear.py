@@ -177,6 +177,15 @@ class Int8LlamaMLP(nn.Module):
         self.act = act
 
     @classmethod
+    def from_quantized(cls, q_gate_up: torch.Tensor, s_gate_up: torch.Tensor, q_down: torch.Tensor,
+                       s_down: torch.Tensor, intermediate: int, act=F.silu) -> "Int8LlamaMLP":
+        """From int8 weights already on the GPU: `q_gate_up [2I, H]` in [gate; up] row order
+        with its scales, and `q_down [H, I]` with its scales."""
+        perm = ops.interleave_gate_up_rows(intermediate, device=q_gate_up.device)
+        gate_up = Int8Linear.from_quantized(q_gate_up.index_select(0, perm), s_gate_up.index_select(0, perm))
+        return cls(gate_up, Int8Linear.from_quantized(q_down, s_down), intermediate, act, interleaved=True)
+
+    @classmethod
     def from_mlp(cls, mlp: nn.Module) -> "Int8LlamaMLP":
         gate, up, down = mlp.gate_proj, mlp.up_proj, mlp.down_proj
         for lin in (gate, up, down):
@@ -186,18 +195,18 @@ class Int8LlamaMLP(nn.Module):
         gate_up = Int8Linear.from_float_weights(gate.weight, up.weight)
         return cls(gate_up, Int8Linear.from_linear(down), gate.out_features, act)
 
-    def _split(self, t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """(gate rows, up rows) of an interleaved [2I, ...] tensor."""
+    def split_rows(self, t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(gate rows, up rows) of a tensor [2I, ...] in the interleaved row order."""
         v = t.view(self.intermediate_size // 8, 2, 8, *t.shape[1:])
         return v[:, 0].reshape(self.intermediate_size, *t.shape[1:]), v[:, 1].reshape(self.intermediate_size, *t.shape[1:])
 
     def gate_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         """Dequantized gate_proj weight [I, H]."""
-        return self._split(self.gate_up.dequantized(dtype))[0]
+        return self.split_rows(self.gate_up.dequantized(dtype))[0]
 
     def up_weight(self, dtype: torch.dtype = torch.float32) -> torch.Tensor:
         """Dequantized up_proj weight [I, H]."""
-        return self._split(self.gate_up.dequantized(dtype))[1]
+        return self.split_rows(self.gate_up.dequantized(dtype))[1]
 
     def _silu(self) -> bool:
         # torch's SiLU, or transformers' SiLUActivation (ACT2FN["silu"], x * sigmoid(x))
@@ -222,12 +231,14 @@ class Int8LlamaMLP(nn.Module):
         return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
-def quantize_llama_(model: nn.Module, fuse: bool = True) -> nn.Module:
+def quantize_llama_(model: nn.Module, fuse: bool = True, lm_head: bool = False) -> nn.Module:
     """In place: every decoder layer's q/k/v/o and MLP projections become int8.
 
     `model` is a Llama-family `*ForCausalLM` on a CUDA device (the layout
     `ModelRunner.check_custom_kernel_support` requires, `model_runner.py:77-94`).  The
-    embedding and lm_head stay in the model dtype.
+    embedding stays in the model dtype; so does the lm_head unless `lm_head=True`, which
+    makes it an `Int8Linear` too (vocab x hidden, the largest single matrix of the decode
+    step; it breaks a tie with the input embedding, which keeps its own weight).
     """
     decoder = getattr(model, "model", model)
     layers = getattr(decoder, "layers", None)
@@ -245,6 +256,11 @@ def quantize_llama_(model: nn.Module, fuse: bool = True) -> nn.Module:
             attn.v_proj = Int8Linear.from_linear(attn.v_proj)
         attn.o_proj = Int8Linear.from_linear(attn.o_proj)
         layer.mlp = Int8LlamaMLP.from_mlp(layer.mlp)
+    if lm_head:
+        head = getattr(model, "lm_head", None)
+        if not isinstance(head, nn.Linear):
+            raise RuntimeError(f"int8: {type(model).__name__} has no nn.Linear lm_head")
+        model.lm_head = Int8Linear.from_linear(head)
     torch.cuda.empty_cache()
     return model
 

@@ -46,16 +46,18 @@ class LlamaShape:
 LLAMA3_8B = LlamaShape(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=14336, vocab=128256)
 
 
-def decode_bytes_per_step(shape: LlamaShape, batch: int, context: int, quantize: bool) -> int:
+def decode_bytes_per_step(shape: LlamaShape, batch: int, context: int, quantize: bool,
+                          int8_lm_head: bool = False) -> int:
     """HBM bytes one decode step must read at least: projection weights (int8 + fp32 scales,
-    or bf16), the K/V of every sequence (context + 1 positions), the lm_head and the new
-    tokens' embedding rows."""
+    or bf16), the K/V of every sequence (context + 1 positions), the lm_head (bf16, or int8
+    + scales) and the new tokens' embedding rows."""
     H, hd = shape.hidden, shape.head_dim
     n_qkv = (shape.heads + 2 * shape.kv_heads) * hd
     per_layer = [(H, n_qkv), (shape.heads * hd, H), (H, 2 * shape.intermediate), (shape.intermediate, H)]
     w = sum(k * n * (1 if quantize else 2) + (4 * n if quantize else 0) for k, n in per_layer) * shape.layers
     kv = 2 * shape.layers * batch * shape.kv_heads * (context + 1) * hd * 2
-    return w + kv + shape.vocab * H * 2 + batch * H * 2
+    head = shape.vocab * H + 4 * shape.vocab if int8_lm_head else shape.vocab * H * 2
+    return w + kv + head + batch * H * 2
 
 
 def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -78,7 +80,7 @@ class DecodeModel:
     """Random-init Llama decoder for `batch` sequences at `context` cached positions."""
 
     def __init__(self, shape: LlamaShape, batch: int, context: int, device, seed: int = 0,
-                 quantize: bool = True, weights: list | None = None):
+                 quantize: bool = True, weights: list | None = None, quantize_lm_head: bool = False):
         self.shape, self.batch, self.context, self.quantize = shape, batch, context, quantize
         dev = torch.device(device)
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -120,6 +122,16 @@ class DecodeModel:
         self.cos = torch.cos(ang).to(torch.bfloat16)
         self.sin = torch.sin(ang).to(torch.bfloat16)
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.lm_head_int8 = None
+        if quantize_lm_head:
+            self.set_lm_head_int8(True)
+
+    def set_lm_head_int8(self, on: bool) -> None:
+        """Serve the lm_head (vocab x hidden) from an int8 copy of its weight, or from bf16."""
+        self.lm_head_int8 = Int8Linear.from_float_weights(self.lm_head) if on else None
+
+    def _head(self, h: torch.Tensor) -> torch.Tensor:
+        return self.lm_head_int8(h) if self.lm_head_int8 is not None else F.linear(h, self.lm_head)
 
     def _hidden(self, tokens: torch.Tensor, in_place: bool) -> torch.Tensor:
         """Final-norm hidden state of one step.  `in_place` writes the new K/V into the
@@ -157,8 +169,8 @@ class DecodeModel:
     def step(self, tokens: torch.Tensor | None = None) -> torch.Tensor:
         """One decode step for every sequence; returns the greedy next tokens [B]."""
         h = self._hidden(self.tokens if tokens is None else tokens, in_place=True)
-        return F.linear(h, self.lm_head).argmax(-1)
+        return self._head(h).argmax(-1)
 
     def logits(self, tokens: torch.Tensor) -> torch.Tensor:
         """fp32 logits of one step, leaving the caches untouched (parity checks)."""
-        return F.linear(self._hidden(tokens, in_place=False), self.lm_head).float()
+        return self._head(self._hidden(tokens, in_place=False)).float()

@@ -46,3 +46,17 @@ def test_graph_replay_equals_eager_step():
 
 def test_bytes_per_step_counts_int8_weights():
     assert decode_bytes_per_step(TINY, 4, 16, True) < decode_bytes_per_step(TINY, 4, 16, False)
+
+
+def test_int8_lm_head_matches_dequantized_head():
+    m = DecodeModel(TINY, batch=4, context=16, device="cuda", seed=7, quantize=True)
+    tokens = torch.tensor([3, 5, 8, 13], device="cuda")
+    bf = m.logits(tokens)
+    m.set_lm_head_int8(True)
+    q = m.logits(tokens)
+    deq = m.lm_head_int8.dequantized(torch.float32)
+    h = m._hidden(tokens, in_place=False).float()
+    ref = h @ deq.T
+    assert ((q - ref).abs().max() / ref.abs().max()).item() < 1e-2
+    assert ((q - bf).abs().max() / bf.abs().max()).item() < 5e-2
+    assert decode_bytes_per_step(TINY, 4, 16, True, int8_lm_head=True) < decode_bytes_per_step(TINY, 4, 16, True)

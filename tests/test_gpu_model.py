@@ -150,3 +150,43 @@ def test_cuda_graph_capture_replays_int8_layers_exactly():
             torch.cuda.synchronize()
             assert torch.equal(static_out, eager), (M, trial)
         pos_ids_cache[M] = True
+
+
+@torch.no_grad()
+@pytest.mark.parametrize("fuse", [True, False])
+def test_int8_checkpoint_save_load_reproduces_the_quantized_model(tmp_path, fuse):
+    """quantize -> save -> load into a fresh model with the same non-projection weights:
+    identical int8 weights and scales, and bit-identical logits."""
+    from llm_serving_engine_b200.checkpoint import int8_state_dict, load_int8_checkpoint_, save_int8_checkpoint
+
+    model = _tiny_llama()
+    quantize_llama_(model, fuse=fuse)
+    path = str(tmp_path / "int8.safetensors")
+    save_int8_checkpoint(model, path)
+    fresh = _tiny_llama()  # same seed: same embedding, norms and lm_head; float projections ignored
+    load_int8_checkpoint_(fresh, path, fuse=fuse)
+    a, _ = int8_state_dict(model)
+    b, _ = int8_state_dict(fresh)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    ids = torch.randint(0, 128, (1, 20), device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+    assert torch.equal(model(ids).logits, fresh(ids).logits)
+
+
+@torch.no_grad()
+def test_int8_lm_head_and_its_checkpoint(tmp_path):
+    from llm_serving_engine_b200.checkpoint import load_int8_checkpoint_, save_int8_checkpoint
+
+    model = _tiny_llama()
+    head_w = model.lm_head.weight.detach().clone()
+    quantize_llama_(model, lm_head=True)
+    assert isinstance(model.lm_head, Int8Linear)
+    err = (model.lm_head.dequantized() - head_w.float()).abs().max() / head_w.float().abs().max()
+    assert err < 1e-2
+    path = str(tmp_path / "int8_head.safetensors")
+    save_int8_checkpoint(model, path)
+    fresh = _tiny_llama()
+    load_int8_checkpoint_(fresh, path)
+    assert isinstance(fresh.lm_head, Int8Linear)
+    ids = torch.randint(0, 128, (1, 12), device="cuda", generator=torch.Generator("cuda").manual_seed(4))
+    assert torch.equal(model(ids).logits, fresh(ids).logits)
