@@ -262,15 +262,29 @@ int skinny_prefetch_groups() {
     return v;
 }
 
-template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false, int P = 0>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, cudaStream_t st) {
     const int64_t row_blocks = SILU_MUL ? N / 8 : (N + 15) / 16;  // weight row blocks (SILU_MUL: 2N rows)
     dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
+    constexpr int smem = P > 0 ? skinny_ring_bytes<KW, R, U, P>() : 0;
+    auto kernel = skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL, P>;
+    if constexpr (smem > 48 * 1024) {  // opt in to the cp.async ring's shared memory, once per device
+        static std::once_flag once[kMaxDevices];
+        static cudaError_t set_err[kMaxDevices];
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        std::call_once(once[dev], [&] {
+            set_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        });
+        if (set_err[dev] != cudaSuccess) return set_err[dev];
+    }
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
-    return cudaLaunchKernelEx(&cfg, skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL>, static_cast<const __nv_bfloat16 *>(x), ldx,
+    launch_config(cfg, attr, grid, dim3(KW * 32), smem, st);
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
                               static_cast<__nv_bfloat16 *>(y), ldy, static_cast<const __nv_bfloat16 *>(res), ldr,
                               static_cast<int>(packed_cols(K)),
@@ -279,14 +293,16 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
 
 // Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):
 //   * very many row blocks (N/16 >= 4 x SMs: gate_up): CTAs of 8 warps on one row block, four
-//     CTAs per SM (M <= 8; above that, two row blocks and three CTAs per SM);
+//     CTAs per SM (M <= 8; above that, four row blocks per CTA, so that each activation load,
+//     which costs eight L1 wavefronts, serves 64 weight rows);
 //   * many row blocks (N/16 >= 2 x SMs: QKV): CTAs of 8 warps on two row blocks, so every
 //     activation load serves 32 weight rows;
 //   * few row blocks (O, down): CTAs of 16 warps, one row block (two for M > 8, where the
 //     activation loads, not the weight stream, would otherwise saturate L1);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
-// LSE_SKINNY_VARIANT=<0..8> pins one configuration for tuning runs.
+// LSE_SKINNY_VARIANT=<0..14> pins one configuration for tuning runs (9, 10: the cp.async
+// shared-memory weight ring, measured no faster than registers on B200).
 int skinny_variant() {
     static const int v = [] {
         const char *e = std::getenv("LSE_SKINNY_VARIANT");
@@ -303,7 +319,7 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
                              int num_sms, cudaStream_t st) {
     if (variant < 0) {
         const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
-        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 5) : (rb_per_sm >= 2 ? 1 : 0);
+        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 11) : (rb_per_sm >= 2 ? 1 : 0);
     }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
@@ -323,6 +339,14 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
             case 6: return launch_skinny<MT, 8, 2, 4, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 7: return launch_skinny<MT, 8, 1, 4, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 8: return launch_skinny<MT, 16, 1, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            // cp.async shared-memory weight ring (P groups of U chunks in flight per lane)
+            case 9: return launch_skinny<MT, 8, 1, 4, BF, 3, SILU, 4>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 10: return launch_skinny<MT, 16, 1, 4, BF, 2, SILU, 3>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            // four row blocks per CTA: each activation load serves 64 weight rows
+            case 11: return launch_skinny<MT, 8, 4, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 12: return launch_skinny<MT, 4, 4, 2, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 13: return launch_skinny<MT, 4, 4, 2, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 14: return launch_skinny<MT, 8, 4, 1, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             default:
                 if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
                 else return launch_skinny<2, 16, 2, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);

@@ -63,6 +63,28 @@ __device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
     return r;
 }
 
+// 16 weight bytes of one lane into its own shared-memory slot (cp.async, L2 only, evict-first
+// hint).  Only the issuing lane reads the slot back, after its own wait_group, so no barrier
+// is involved.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const int8_t *src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr)
+                 : "memory");
+    return r;
+}
+
+// Dynamic shared memory of the cp.async weight ring: KW warps x P groups x U chunks x R row
+// blocks x 512 bytes (16 per lane).
+template <int KW, int R, int U, int P>
+constexpr int skinny_ring_bytes() { return KW * P * U * R * 512; }
+
 // y = bf16(s * acc), or bf16(res + s * acc) when `res` is given (it may be y itself: each
 // element is read, then written, by one thread).
 //
@@ -80,13 +102,20 @@ __device__ __forceinline__ uint4 ld_weight16(const int8_t *p, uint64_t policy) {
 // are prefetched into L2 by lane 0 (bulk prefetches), which deepens the stream at no
 // register cost.
 //
+// P > 0 stages the weight stream through shared memory instead of registers: each lane
+// keeps P groups of U chunks (per row block) in flight with cp.async into its own 16-byte
+// slots, and reads a group back with shared loads once its cp.async group has completed.
+// The depth in flight is then set by shared memory (P * U * R * 16 bytes per lane), not by
+// registers, which matters for M > 8 where the accumulators and activation fragments take
+// the registers a deeper register ring would need.
+//
 // SILU_MUL: the weight rows interleave 8-row blocks of the MLP's gate and up projections
 // (row block b = gate rows 8b..8b+7, then the matching up rows 8b..8b+7), so the 16x8
 // accumulator of one lane holds gate row r0 (registers 0, 1) and up row r0 (registers 2, 3)
 // of the same tokens, and the epilogue writes y[m, 8b + r0] = silu(s_g * gate) * (s_u * up)
 // (fp32, one bf16 rounding) for the N = I intermediate columns; `scale` is interleaved the
 // same way.
-template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false, int P = 0>
 __global__ void __launch_bounds__(KW * 32, MINB)
 skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
@@ -111,12 +140,34 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     const int64_t rb_bytes = static_cast<int64_t>(kc_all) * 512;
     const int8_t *const wbase = wp + (static_cast<int64_t>(rg) * R * kc_all + c0) * 512 + lane * 16;
     const int8_t *gp = wbase + rot * (U * 512);
+    // cp.async ring (P > 0, whole-group slices): this lane's slot for (ring group p, chunk j,
+    // row block r) is at ring_lane + ((p * U + j) * R + r) * 512.
+    extern __shared__ __align__(16) uint4 ring_smem[];
+    const uint32_t ring_lane = ptx::smem_u32(ring_smem) + ((warp * P * U * R) * 32 + lane) * 16;
+    auto issue_group = [&](int p, int gv) {  // slice group gv -> ring group p, one commit group
+#pragma unroll
+        for (int j = 0; j < U; ++j)
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                cp_async16(ring_lane + ((p * U + j) * R + r) * 512, wbase + gv * (U * 512) + r * rb_bytes + j * 512, pol);
+    };
+    constexpr bool RING = P > 0;
     uint4 wb[U][R];
+    if (RING && fast) {
+        // groups rot, rot + 1, ... (mod ng) into ring groups 0..P-1; one commit per ring group
+        // (empty when the slice has fewer groups) so wait_group counts stay uniform
 #pragma unroll
-    for (int j = 0; j < U; ++j)
+        for (int p = 0; p < (RING ? P : 1); ++p) {
+            if (p < ng) issue_group(p, rot + p < ng ? rot + p : rot + p - ng);
+            cp_async_commit();
+        }
+    } else {
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-            wb[j][r] = (fast || j < nch) ? ld_weight16(gp + r * rb_bytes + j * 512, pol) : make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < U; ++j)
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                wb[j][r] = (fast || j < nch) ? ld_weight16(gp + r * rb_bytes + j * 512, pol) : make_uint4(0, 0, 0, 0);
+    }
     // L2 prefetch of the group `v` visits ahead (lane 0, one bulk prefetch per row block): the
     // register loads then hit L2, so the registers hold only U chunks while DRAM has
     // pf_groups more groups per row block in flight.
@@ -128,7 +179,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
             for (int r = 0; r < R; ++r) ptx::bulk_prefetch_l2(wbase + r * rb_bytes + gv * (U * 512), U * 512);
         }
     };
-    if (fast)
+    if (fast && !RING)
         for (int v = 1; v <= pf_groups; ++v) prefetch_group(v);
 
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
@@ -214,7 +265,38 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
         }
     };
 
-    if (fast) {
+    if (RING && fast) {
+        int gi = rot;                              // slice group being processed
+        int gn = rot + P < ng ? rot + P : rot + P - ng;  // slice group P ahead (valid while g + P < ng)
+        for (int g = 0; g < ng; ++g) {
+            cp_async_wait<(RING ? P : 1) - 1>();  // this lane's copies of group g have landed
+            const int p = g % (RING ? P : 1);
+            uint4 w[U][R];
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+#pragma unroll
+                for (int r = 0; r < R; ++r) w[j][r] = lds16(ring_lane + ((p * U + j) * R + r) * 512);
+            if (g + P < ng) {  // refill the ring group just read (same lane, program order)
+                issue_group(p, gn);
+                gn = gn + 1 == ng ? 0 : gn + 1;
+            }
+            cp_async_commit();
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                uint2 xv[MT][2];
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                    xv[t][0] = __ldg(reinterpret_cast<const uint2 *>(xp[t] + j * 32));
+                    xv[t][1] = __ldg(reinterpret_cast<const uint2 *>(xp[t] + j * 32 + 16));
+                }
+                compute(j, w[j], xv);
+            }
+            const bool wrap = gi + 1 == ng;
+#pragma unroll
+            for (int t = 0; t < MT; ++t) xp[t] = wrap ? xbase[t] : xp[t] + U * 32;
+            gi = wrap ? 0 : gi + 1;
+        }
+    } else if (fast) {
         int gi = rot;  // slice group being processed
         for (int g = 0; g < ng; ++g) {
             if (pf_groups > 0) prefetch_group(g + pf_groups + 1);
@@ -273,10 +355,10 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
             }
     __syncthreads();
     if constexpr (SILU_MUL) {
-        // warp (r, jj) = (warp >> 1, warp & 1) finishes row block r: gate row r0 (register jj)
+        // item (r, jj) = (wi >> 1, wi & 1) finishes row block r: gate row r0 (register jj)
         // and up row r0 (register 2 + jj), token 2q + jj of each tile.
-        if (warp < 2 * R) {
-            const int r = warp >> 1, jj = warp & 1;
+        for (int wi = warp; wi < 2 * R; wi += KW) {  // KW may be smaller than 2R
+            const int r = wi >> 1, jj = wi & 1;
             const int b = rg * R + r;
             const int n = b * 8 + r0;  // intermediate column
             if (n < N) {
@@ -297,12 +379,11 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                 }
             }
         }
-        return;
-    }
-    // warp (r, j) = (warp >> 2, warp & 3) finishes accumulator register j of row block r:
+    } else {
+    // item (r, j) = (wi >> 2, wi & 3) finishes accumulator register j of row block r:
     // row r0 + 8*(j>>1), token 2q + (j & 1) of each tile (16x8 accumulator layout).
-    if (warp < 4 * R) {
-        const int r = warp >> 2, j = warp & 3;
+    for (int wi = warp; wi < 4 * R; wi += KW) {  // KW may be smaller than 4R
+        const int r = wi >> 2, j = wi & 3;
         const int n = (rg * R + r) * 16 + r0 + 8 * (j >> 1);
         if (n < N) {
             const float sc = __ldg(scale + n);
@@ -319,6 +400,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                 }
             }
         }
+    }
     }
 }
 
