@@ -314,13 +314,17 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
     from llm_serving_engine_b200.llama_decode import LLAMA3_8B, DecodeModel, decode_bytes_per_step
 
     B, ctx = 64, 1024
-    base = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=False)
-    q8 = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=True, weights=base.weights)
+    base = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=False, attention="sdpa")
+    q8 = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=True, weights=base.weights, kv=base.kv,
+                     attention="sdpa")
+    q8_paged = DecodeModel(LLAMA3_8B, B, ctx, dev, seed=11, quantize=True, weights=base.weights, attention="paged")
+    q8_paged.proj = q8.proj  # same int8 modules, the paged-pool attention kernel
     out = {"workload": "config4: Llama-3-8B shape (32 layers, hidden 4096, 32/8 heads, head_dim 128, MLP 14336, "
                        "vocab 128256), random init, 64 sequences, 1024-token context, greedy, CUDA graph per step; "
-                       "attention: torch SDPA over a contiguous KV cache",
+                       "attention: torch SDPA (cuDNN) over a contiguous cache; int8_paged: this package's paged "
+                       "decode-attention kernel over a block_size-16 pool in the reference's layout",
            "unit": "tokens/s"}
-    for name, m in (("int8", q8), ("int8_lm_head", q8), ("none", base)):
+    for name, m in (("int8", q8), ("int8_lm_head", q8), ("none", base), ("int8_paged", q8_paged)):
         q8.set_lm_head_int8(name == "int8_lm_head")
         g = capture(m.step, warm)
         time_graph(g, 3)
@@ -332,7 +336,7 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
         del g
     out["int8_speedup"] = round(out["int8"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
     out["int8_lm_head_speedup"] = round(out["int8_lm_head"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
-    del base, q8
+    del base, q8, q8_paged
     torch.cuda.empty_cache()
     return out
 
@@ -409,6 +413,39 @@ def fused_residual(weights, dev, warm, ops):
                 del g
             pt["speedup"] = round(pt["unfused_us"] / pt["fused_us"], 3)
             out["points"].append(pt)
+    return out
+
+
+def decode_attention(dev, warm, ops, hbm_peak):
+    """The paged decode-attention kernel alone: Llama-3-8B attention shape (32 query / 8 KV
+    heads, head_dim 128), 1025 positions per sequence in a block_size-16 pool with a shuffled
+    block table, one pool per layer for 32 layers in a CUDA graph (the K/V stream exceeds L2
+    for E >= 16).  GB/s = K and V bytes read / time."""
+    H, H_kv, D, bs, ctx, layers = 32, 8, 128, 16, 1025, 32
+    out = {"workload": f"H={H}, H_kv={H_kv}, D={D}, block_size={bs}, context {ctx}, {layers} layers' pools per graph",
+           "points": []}
+    g = torch.Generator(device=dev).manual_seed(23)
+    for E in (1, 16, 64):
+        nbps = -(-ctx // bs)
+        nb = E * nbps + 1
+        bt = torch.randperm(nb, device=dev, generator=g)[: E * nbps].view(E, nbps).to(torch.int32)
+        cl = torch.full((E,), ctx, dtype=torch.int32, device=dev)
+        pools = [(torch.randn(nb, bs, H_kv, D, device=dev, generator=g).to(torch.bfloat16),
+                  torch.randn(nb, bs, H_kv, D, device=dev, generator=g).to(torch.bfloat16)) for _ in range(layers)]
+        q = torch.randn(E, H, D, device=dev, generator=g).to(torch.bfloat16)
+        o = torch.empty_like(q)
+
+        def run(q=q, o=o, pools=pools, bt=bt, cl=cl):
+            for kp, vp in pools:
+                ops.paged_decode_attention(q, kp, vp, bt, cl, ctx, out=o)
+        gr = capture(run, warm)
+        time_graph(gr, 2)
+        us = time_graph(gr, 10) / layers * 1e3
+        byts = E * ctx * H_kv * D * 2 * 2
+        out["points"].append({"E": E, "us": round(us, 3), "GBps": round(byts / us / 1e3, 1),
+                              "frac_of_hbm": round(byts / us / 1e3 / hbm_peak, 4)})
+        del gr, pools
+        torch.cuda.empty_cache()
     return out
 
 
@@ -617,6 +654,7 @@ def main():
 
     fused_mlp = fused_gate_up(weights, dev, warm, ops, hbm_peak)
     fused_res = fused_residual(weights, dev, warm, ops)
+    attn = decode_attention(dev, warm, ops, hbm_peak)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
@@ -670,6 +708,7 @@ def main():
             line["prefill"] = prefill
         line["fused_gate_up_silu"] = fused_mlp
         line["fused_residual"] = fused_res
+        line["decode_attention"] = attn
         if tp70b:
             line["config5_70b_column_split"] = tp70b
         if decode4:

@@ -147,6 +147,40 @@ int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ld
                                  const int8_t *w_packed, const float *scale, int64_t I,
                                  void *y, int64_t ldy, void *stream);
 
+/*
+ * Paged decode attention, one query token per sequence (the decode-step call of the
+ * reference's paged_attention_forward, src/llm_serving_engine/kernels/flash_attention.py:
+ * 287-332, with q_len = 1 and query_offset = context_len - 1):
+ *
+ *   o[e, h, :] = softmax_p( q[e, h, :] . K[e, p, h / G, :] * scale ) V[e, p, h / G, :],
+ *                p = 0 .. context_len[e] - 1,  G = H / H_kv
+ *
+ *   q        bf16, element (e, h, d) at q[e * q_stride_e + h * q_stride_h + d]
+ *   k_pool, v_pool  bf16 [num_blocks, block_size, H_kv, D], contiguous; position p of
+ *            sequence e is block block_table[e * bt_stride + p / block_size], slot
+ *            p % block_size
+ *   context_len  int32 [E], each <= max_context (the launch is sized for max_context; a
+ *            larger entry is cut there and reported as LSE_ERR_INVALID_ARG by
+ *            lse_device_status, as is a block id outside [0, num_blocks))
+ *   o        bf16, element (e, h, d) at o[e * o_stride_e + h * o_stride_h + d]
+ *   workspace  >= lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, block_size)
+ *            bytes
+ *            (0 allowed when that is 0), 16-byte aligned, zeroed once before its first use
+ *            and then kept for this launch shape (E, H, H_kv, D, max_context) on one stream:
+ *            the split-K arrival counters at its start are laid out per shape and left at
+ *            zero by every call
+ * D = 64 or 128 and G in {1, 2, 4, 8} (LSE_ERR_UNSUPPORTED otherwise).  fp32 softmax and
+ * accumulation, one bf16 rounding of o.  A sequence with context_len 0 gets zeros.
+ */
+size_t lse_paged_decode_attention_workspace(int64_t E, int64_t H, int64_t H_kv, int64_t D, int64_t max_context,
+                                            int64_t block_size);
+int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, int64_t q_stride_e,
+                               int64_t q_stride_h, const void *k_pool, const void *v_pool, int64_t num_blocks,
+                               int64_t block_size, int64_t H_kv, const int32_t *block_table, int64_t bt_stride,
+                               const int32_t *context_len, int64_t max_context, float scale, void *o,
+                               int64_t o_stride_e, int64_t o_stride_h, void *workspace, size_t workspace_bytes,
+                               void *stream);
+
 /* Bytes of the counter region at the start of every workspace (must start zeroed). */
 #define LSE_WS_COUNTER_BYTES 65536
 

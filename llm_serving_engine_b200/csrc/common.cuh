@@ -15,6 +15,10 @@ namespace lse {
 // The library is one translation unit, so the definition lives here.
 __device__ int g_device_status;
 
+// First nonzero status wins (a kernel that finds a bad argument on the device, e.g. a block
+// id outside the pool, records it and skips the access).
+__device__ __forceinline__ void report_status(int status) { atomicCAS(&g_device_status, LSE_OK, status); }
+
 __device__ __forceinline__ void report_timeout() {
     atomicCAS(&g_device_status, LSE_OK, LSE_ERR_DEVICE_TIMEOUT);
 }

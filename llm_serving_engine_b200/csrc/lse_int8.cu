@@ -8,12 +8,14 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/lse_int8.h"
+#include "decode_attn.cuh"
 #include "gemv_i8.cuh"
 #include "pack_w.cuh"
 #include "quantize.cuh"
@@ -696,5 +698,156 @@ extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K,
                            : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// lse_paged_decode_attention: decode attention over the paged K/V pool (decode_attn.cuh).
+// ---------------------------------------------------------------------------------------
+namespace lse {
+namespace {
+
+struct AttnPlan {
+    int splits, chunk;
+};
+
+// Split the positions of each (sequence, KV head) pair so that the grid covers the GPU about
+// twice (two CTAs fit per SM), keeping chunks of >= 256 positions while that still leaves a
+// full wave (shorter CTAs pay their pipeline fill more often), else down to 64 (small batch).
+constexpr int kAttnCtasPerSm = 2;  // paged_decode_kernel residency (shared memory bound)
+AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_size, int num_sms) {
+    const int64_t pairs = std::max<int64_t>(1, E * H_kv);
+    const int64_t slots = static_cast<int64_t>(kAttnCtasPerSm) * num_sms;
+    const int64_t cap256 = std::max<int64_t>(1, (max_context + 255) / 256);
+    const int64_t cap64 = std::max<int64_t>(1, (max_context + 63) / 64);
+    int64_t splits;
+    if (pairs * cap256 >= slots) splits = std::min<int64_t>((2 * slots + pairs - 1) / pairs, cap256);
+    else splits = std::min<int64_t>((slots + pairs - 1) / pairs, cap64);
+    splits = std::max<int64_t>(1, splits);
+    int64_t chunk = (max_context + splits - 1) / splits;
+    chunk = std::max<int64_t>(32, (chunk + 31) / 32 * 32);
+    splits = std::max<int64_t>(1, (max_context + chunk - 1) / chunk);
+    return {static_cast<int>(splits), static_cast<int>(chunk)};
+}
+
+size_t attn_counter_bytes(int64_t E, int64_t H_kv) { return static_cast<size_t>((E * H_kv * 4 + 255) / 256 * 256); }
+
+size_t attn_workspace_bytes(const AttnPlan &pl, int64_t E, int64_t H, int64_t H_kv, int64_t D) {
+    if (pl.splits <= 1) return 0;
+    const int64_t G = H / H_kv;
+    return attn_counter_bytes(E, H_kv) + static_cast<size_t>(E * H_kv) * pl.splits * G * (D + 2) * sizeof(float);
+}
+
+template <int D, int G>
+cudaError_t launch_attn(const attn::Params &p, int64_t E, cudaStream_t st) {
+    constexpr int smem = attn::attn_smem_bytes<D>();
+    auto kernel = attn::paged_decode_kernel<D, G>;
+    {  // opt in to the ring's shared memory (with the static part it exceeds 48 KB), once per device
+        static std::once_flag once[kMaxDevices];
+        static cudaError_t set_err[kMaxDevices];
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        std::call_once(once[dev], [&] {
+            set_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        });
+        if (set_err[dev] != cudaSuccess) return set_err[dev];
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(p.splits, p.H_kv, static_cast<unsigned>(E)), dim3(attn::THREADS), smem, st);
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+}  // namespace
+}  // namespace lse
+
+extern "C" size_t lse_paged_decode_attention_workspace(int64_t E, int64_t H, int64_t H_kv, int64_t D,
+                                                       int64_t max_context, int64_t block_size) {
+    if (E <= 0 || H <= 0 || H_kv <= 0 || D <= 0 || max_context <= 0 || block_size <= 0 || H % H_kv) return 0;
+    int dev = 0;
+    if (current_device(&dev)) return 0;
+    return attn_workspace_bytes(plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms), E, H, H_kv, D);
+}
+
+extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, int64_t q_stride_e,
+                                          int64_t q_stride_h, const void *k_pool, const void *v_pool,
+                                          int64_t num_blocks, int64_t block_size, int64_t H_kv,
+                                          const int32_t *block_table, int64_t bt_stride, const int32_t *context_len,
+                                          int64_t max_context, float scale, void *o, int64_t o_stride_e,
+                                          int64_t o_stride_h, void *workspace, size_t workspace_bytes,
+                                          void *stream) {
+    if (E < 0 || H <= 0 || H_kv <= 0 || D <= 0 || num_blocks <= 0 || block_size <= 0 || max_context < 0)
+        return LSE_ERR_INVALID_ARG;
+    if (E == 0) return LSE_OK;
+    if (!q || !k_pool || !v_pool || !block_table || !context_len || !o) return LSE_ERR_INVALID_ARG;
+    if (H % H_kv) return LSE_ERR_INVALID_ARG;
+    const int64_t G = H / H_kv;
+    if ((D != 64 && D != 128) || (G != 1 && G != 2 && G != 4 && G != 8)) return LSE_ERR_UNSUPPORTED;
+    if (E > 65535 || H_kv > 65535 || num_blocks * block_size > INT32_MAX / 2 || max_context > INT32_MAX / 2)
+        return LSE_ERR_UNSUPPORTED;
+    if (bt_stride < (max_context + block_size - 1) / block_size) return LSE_ERR_INVALID_ARG;
+    // K/V rows are copied in 16-byte chunks; q is read as bf16 pairs
+    if ((reinterpret_cast<uintptr_t>(q) & 3u) || (reinterpret_cast<uintptr_t>(k_pool) & 15u) ||
+        (reinterpret_cast<uintptr_t>(v_pool) & 15u) || (q_stride_e % 2) || (q_stride_h % 2) ||
+        (reinterpret_cast<uintptr_t>(o) & 1u) || (reinterpret_cast<uintptr_t>(block_table) & 3u) ||
+        (reinterpret_cast<uintptr_t>(context_len) & 3u))
+        return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (max_context == 0) {  // no positions: softmax over nothing is 0 here
+        for (int64_t e = 0; e < E; ++e) {
+            const cudaError_t e2 = cudaMemset2DAsync(static_cast<__nv_bfloat16 *>(o) + e * o_stride_e,
+                                                     static_cast<size_t>(o_stride_h) * 2, 0,
+                                                     static_cast<size_t>(D) * 2, static_cast<size_t>(H), st);
+            if (e2 != cudaSuccess) { set_cuda_error(e2, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
+        }
+        return LSE_OK;
+    }
+    const AttnPlan pl = plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms);
+    const size_t need = attn_workspace_bytes(pl, E, H, H_kv, D);
+    if (need && (!workspace || workspace_bytes < need || !aligned16(workspace))) return LSE_ERR_WORKSPACE;
+    attn::Params p{};
+    p.q = static_cast<const __nv_bfloat16 *>(q);
+    p.q_stride_e = q_stride_e;
+    p.q_stride_h = q_stride_h;
+    p.k_pool = static_cast<const __nv_bfloat16 *>(k_pool);
+    p.v_pool = static_cast<const __nv_bfloat16 *>(v_pool);
+    p.block_table = block_table;
+    p.bt_stride = bt_stride;
+    p.context_len = context_len;
+    p.o = static_cast<__nv_bfloat16 *>(o);
+    p.o_stride_e = o_stride_e;
+    p.o_stride_h = o_stride_h;
+    p.E = static_cast<int>(E);
+    p.H_kv = static_cast<int>(H_kv);
+    p.block_size = static_cast<int>(block_size);
+    p.num_blocks = static_cast<int>(num_blocks);
+    p.chunk = pl.chunk;
+    p.splits = pl.splits;
+    p.scale_log2 = scale * 1.4426950408889634f;  // log2(e): softmax in base 2
+    p.counters = static_cast<int *>(workspace);
+    p.part = need ? reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + attn_counter_bytes(E, H_kv)) : nullptr;
+    cudaError_t e;
+    if (D == 128) {
+        switch (G) {
+            case 1: e = launch_attn<128, 1>(p, E, st); break;
+            case 2: e = launch_attn<128, 2>(p, E, st); break;
+            case 4: e = launch_attn<128, 4>(p, E, st); break;
+            default: e = launch_attn<128, 8>(p, E, st); break;
+        }
+    } else {
+        switch (G) {
+            case 1: e = launch_attn<64, 1>(p, E, st); break;
+            case 2: e = launch_attn<64, 2>(p, E, st); break;
+            case 4: e = launch_attn<64, 4>(p, E, st); break;
+            default: e = launch_attn<64, 8>(p, E, st); break;
+        }
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "paged_decode_attention launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }

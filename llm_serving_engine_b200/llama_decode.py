@@ -9,10 +9,13 @@ norm, the lm_head and the greedy token.  The projections are this package's int8
 (`quantize=True`) or bf16 `F.linear` on the same random weights (`quantize=False`, the
 reference's `quantize="none"`).
 
+Attention (`attention="paged"`, the default) runs this package's sm_100a paged decode
+kernel (`ops.paged_decode_attention`) over K/V pools in the reference's layout
+([num_blocks, block_size, H_kv, head_dim] per layer, a shuffled block table, one spare
+block); `attention="sdpa"` keeps one contiguous [B, H_kv, context + 1, head_dim] cache per
+layer and torch's scaled_dot_product_attention, for comparison.
+
 Stated differences from the reference engine (none of them on the int8 path):
-  * the KV cache is one contiguous [B, Hkv, context + 1, head_dim] block per layer, not the
-    reference's paged pool, and attention is torch's scaled_dot_product_attention over it
-    (attention is outside this build; the reference uses its own Triton kernel);
   * a timed step keeps its position fixed: it writes the new K/V into slot `context` and
     attends over all context + 1 positions, so the CUDA graph's shapes are static and every
     replay does exactly the work of a decode step at that context length.
@@ -25,6 +28,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import ops
 from .int8_linear import Int8Linear, Int8LlamaMLP
 
 __all__ = ["LlamaShape", "LLAMA3_8B", "DecodeModel", "decode_bytes_per_step"]
@@ -80,8 +84,12 @@ class DecodeModel:
     """Random-init Llama decoder for `batch` sequences at `context` cached positions."""
 
     def __init__(self, shape: LlamaShape, batch: int, context: int, device, seed: int = 0,
-                 quantize: bool = True, weights: list | None = None, quantize_lm_head: bool = False):
+                 quantize: bool = True, weights: list | None = None, quantize_lm_head: bool = False,
+                 attention: str = "paged", kv: dict | None = None, block_size: int = 16):
+        if attention not in ("paged", "sdpa"):
+            raise ValueError(f"attention must be 'paged' or 'sdpa', got {attention!r}")
         self.shape, self.batch, self.context, self.quantize = shape, batch, context, quantize
+        self.attention, self.block_size = attention, block_size
         dev = torch.device(device)
         g = torch.Generator(device=dev).manual_seed(seed)
 
@@ -110,13 +118,9 @@ class DecodeModel:
         self.norms = [(torch.ones(H, device=dev, dtype=torch.bfloat16), torch.ones(H, device=dev, dtype=torch.bfloat16))
                       for _ in range(shape.layers)]
         # a prefilled context of `context` positions per sequence (+1 slot for the new token),
-        # from its own generator so that a twin sharing `weights` gets the same caches
-        gk = torch.Generator(device=dev).manual_seed(seed + 1)
-
-        def kv():
-            return torch.randn(batch, shape.kv_heads, context + 1, hd, generator=gk, device=dev).to(torch.bfloat16)
-        self.k_cache = [kv() for _ in range(shape.layers)]
-        self.v_cache = [kv() for _ in range(shape.layers)]
+        # from its own generator so that a twin sharing `weights` gets the same caches; `kv`
+        # shares another model's caches outright
+        self.kv = kv if kv is not None else self._make_kv(dev, seed)
         inv = 1.0 / (shape.rope_theta ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
         ang = context * inv
         self.cos = torch.cos(ang).to(torch.bfloat16)
@@ -125,6 +129,30 @@ class DecodeModel:
         self.lm_head_int8 = None
         if quantize_lm_head:
             self.set_lm_head_int8(True)
+
+    def _make_kv(self, dev: torch.device, seed: int) -> dict:
+        """paged: per layer K and V pools [num_blocks, block_size, H_kv, hd] (the reference's
+        layout, plus one spare block as the reference keeps) with a shuffled block table;
+        sdpa: per layer contiguous [B, H_kv, context + 1, hd] caches."""
+        s, B, hd = self.shape, self.batch, self.shape.head_dim
+        gk = torch.Generator(device=dev).manual_seed(seed + 1)
+        if self.attention == "sdpa":
+            def kv():
+                return torch.randn(B, s.kv_heads, self.context + 1, hd, generator=gk, device=dev).to(torch.bfloat16)
+            return {"k": [kv() for _ in range(s.layers)], "v": [kv() for _ in range(s.layers)]}
+        bs = self.block_size
+        nbps = -(-(self.context + 1) // bs)
+        nb = B * nbps + 1
+        gp = torch.Generator().manual_seed(seed + 2)
+        table = torch.randperm(nb, generator=gp)[: B * nbps].view(B, nbps).to(torch.int32).to(dev)
+
+        def pool():
+            return torch.randn(nb, bs, s.kv_heads, hd, generator=gk, device=dev).to(torch.bfloat16)
+        pos = self.context  # the new token's position
+        slot = table[:, pos // bs].long() * bs + pos % bs  # its pool slot per sequence
+        return {"k": [pool() for _ in range(s.layers)], "v": [pool() for _ in range(s.layers)],
+                "block_table": table, "slot": slot,
+                "context_len": torch.full((B,), self.context + 1, dtype=torch.int32, device=dev)}
 
     def set_lm_head_int8(self, on: bool) -> None:
         """Serve the lm_head (vocab x hidden) from an int8 copy of its weight, or from bf16."""
@@ -148,10 +176,19 @@ class DecodeModel:
             k = qkv[:, s.heads * hd:(s.heads + s.kv_heads) * hd].view(B, s.kv_heads, hd)
             v = qkv[:, (s.heads + s.kv_heads) * hd:].view(B, s.kv_heads, hd)
             q, k = _rope(q, self.cos, self.sin), _rope(k, self.cos, self.sin)
-            kc, vc = (self.k_cache[li], self.v_cache[li]) if in_place else (self.k_cache[li].clone(), self.v_cache[li].clone())
-            kc[:, :, pos] = k
-            vc[:, :, pos] = v
-            attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
+            kc, vc = self.kv["k"][li], self.kv["v"][li]
+            if not in_place:
+                kc, vc = kc.clone(), vc.clone()
+            if self.attention == "paged":
+                nb, bs = kc.shape[0], kc.shape[1]
+                kc.view(nb * bs, s.kv_heads, hd).index_copy_(0, self.kv["slot"], k)
+                vc.view(nb * bs, s.kv_heads, hd).index_copy_(0, self.kv["slot"], v)
+                attn = ops.paged_decode_attention(q, kc, vc, self.kv["block_table"], self.kv["context_len"],
+                                                  self.context + 1)
+            else:
+                kc[:, :, pos] = k
+                vc[:, :, pos] = v
+                attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
             h = o_p(attn.reshape(B, s.heads * hd), residual=h)  # residual + o_proj(attn)
             x = _rms_norm(h, n_post, s.eps)
             h = mlp(x, residual=h)

@@ -33,6 +33,7 @@ __all__ = [
     "interleave_gate_up_rows",
     "int8_gate_up_silu_packed",
     "GATE_UP_SILU_MAX_M",
+    "paged_decode_attention",
     "workspace_for",
     "device_status",
     "ALGO_AUTO",
@@ -261,6 +262,66 @@ def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
                                        q.data_ptr(), s.data_ptr(), stream.cuda_stream)
     _lib.check(rc, "lse_int8_quantize")
     return q, s
+
+
+# Split-K scratch of the decode attention, one zero-initialised buffer per (device, stream,
+# launch shape): the arrival counters at its start are laid out per shape, so a buffer is
+# never shared between shapes.  Created outside captures only.
+_attn_ws: dict[tuple, torch.Tensor] = {}
+
+
+def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
+                           context_len: torch.Tensor, max_context: int, scale: float | None = None,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention over the paged K/V pool: one query token per sequence.
+
+    q: bf16 [E, H, D] (d contiguous); k_pool / v_pool: bf16 [num_blocks, block_size, H_KV, D]
+    contiguous (the reference's per-layer pool, already holding this step's K/V);
+    block_table: int32 [E, >= ceil(max_context / block_size)]; context_len: int32 [E], every
+    entry <= max_context (a launch-shape bound, fixed per captured graph).  Returns bf16
+    [E, H, D] = softmax(q K^T * scale) V over each sequence's positions, scale = 1/sqrt(D) by
+    default (`paged_attention_forward`, `kernels/flash_attention.py:287-332`, with q_len 1).
+    """
+    if not all(t.is_cuda for t in (q, k_pool, v_pool, block_table, context_len)):
+        raise RuntimeError("paged_decode_attention runs on CUDA only (no CPU fallback)")
+    if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or v_pool.dtype != torch.bfloat16:
+        raise ValueError("paged_decode_attention: q and the pools must be bfloat16")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("paged_decode_attention: q must be [E, H, D] with a contiguous last dim")
+    if k_pool.shape != v_pool.shape or k_pool.dim() != 4 or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+        raise ValueError("paged_decode_attention: pools must be contiguous [num_blocks, block_size, H_KV, D]")
+    E, H, D = q.shape
+    nb, bs, H_kv, Dk = k_pool.shape
+    if Dk != D:
+        raise ValueError(f"paged_decode_attention: head_dim {D} != pool head_dim {Dk}")
+    if block_table.dtype != torch.int32 or context_len.dtype != torch.int32 or block_table.dim() != 2 \
+            or block_table.stride(1) != 1 or context_len.shape != (E,) or block_table.shape[0] != E:
+        raise ValueError("paged_decode_attention: block_table int32 [E, n] and context_len int32 [E]")
+    if out is None:
+        out = torch.empty((E, H, D), dtype=torch.bfloat16, device=q.device)
+    elif out.dtype != torch.bfloat16 or out.shape != (E, H, D) or out.stride(-1) != 1:
+        raise ValueError("paged_decode_attention: out must be bf16 [E, H, D] with a contiguous last dim")
+    if E == 0:
+        return out
+    _ensure_device(q.device)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(q.device)
+    need = int(lib.lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, bs))
+    key = (q.device.index, stream.cuda_stream, E, H, H_kv, D, int(max_context), bs)
+    ws = _attn_ws.get(key)
+    if need and ws is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("paged_decode_attention: workspace must grow outside a CUDA graph capture; "
+                               "run one eager call with the same shapes on the capture stream first")
+        ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
+        _attn_ws[key] = ws
+    scale = 1.0 / float(D) ** 0.5 if scale is None else float(scale)
+    rc = lib.lse_paged_decode_attention(
+        q.data_ptr(), E, H, D, q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), nb, bs, H_kv,
+        block_table.data_ptr(), block_table.stride(0), context_len.data_ptr(), int(max_context), scale,
+        out.data_ptr(), out.stride(0), out.stride(1), ws.data_ptr() if need else None, need, stream.cuda_stream)
+    _lib.check(rc, "lse_paged_decode_attention")
+    return out
 
 
 def device_status(device: int | torch.device | None = None, reset: bool = True) -> int:

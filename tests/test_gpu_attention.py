@@ -1,0 +1,113 @@
+"""Paged decode attention (sm_100a kernel) against the fp64 oracle restating the reference's
+`paged_attention_2` for one query token per sequence: GQA group sizes 1-8, head_dim 64 and
+128, ragged context lengths (0, 1, block boundaries, long), shuffled block tables, the
+split-K path (few sequences) and the single-pass path (many), determinism, graph replay, and
+an out-of-range block id reported on the device status word without a fault."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from llm_serving_engine_b200 import _lib, ops
+from oracle.ref_attention import ref_paged_decode_attention
+from tests.gpu_helpers import check_parity
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(E, H, H_kv, D, bs, ctx, seed=0, spare_blocks=3):
+    g = torch.Generator().manual_seed(seed)
+    ctx = np.asarray(ctx, dtype=np.int64)
+    max_ctx = int(ctx.max())
+    nbps = max(1, -(-max_ctx // bs))
+    nb = E * nbps + spare_blocks
+    perm = torch.randperm(nb, generator=g)[: E * nbps].view(E, nbps).to(torch.int32)  # shuffled blocks
+    k_pool = (torch.randn(nb, bs, H_kv, D, generator=g)).to(torch.bfloat16)
+    v_pool = (torch.randn(nb, bs, H_kv, D, generator=g)).to(torch.bfloat16)
+    q = (torch.randn(E, H, D, generator=g) * 2).to(torch.bfloat16)
+    return q, k_pool, v_pool, perm, torch.as_tensor(ctx, dtype=torch.int32), max_ctx
+
+
+def _run(q, k_pool, v_pool, bt, ctx, max_ctx):
+    return ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda(), ctx.cuda(), max_ctx)
+
+
+@pytest.mark.parametrize("E,H,H_kv,D,bs,ctx", [
+    (1, 32, 8, 128, 16, [1025]),                       # one sequence: many splits
+    (4, 32, 8, 128, 16, [1, 17, 300, 1024]),           # ragged, block boundaries
+    (64, 32, 8, 128, 16, list(range(962, 1026))),      # Llama-3-8B decode batch
+    (3, 8, 8, 64, 8, [0, 5, 129]),                     # G = 1, head_dim 64, an empty context
+    (2, 64, 8, 128, 16, [700, 33]),                    # G = 8 (Llama-3-70B)
+    (5, 16, 8, 128, 32, [31, 32, 33, 64, 1000]),       # G = 2, block_size 32
+    (6, 8, 2, 64, 16, [4096, 1, 2048, 15, 16, 3000]),  # long contexts, G = 4
+])
+def test_paged_decode_attention_parity(E, H, H_kv, D, bs, ctx):
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(E, H, H_kv, D, bs, ctx, seed=E + H + D)
+    o = _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    torch.cuda.synchronize()
+    ref = ref_paged_decode_attention(q.float().numpy(), k_pool.float().numpy(), v_pool.float().numpy(),
+                                     bt.numpy(), cl.numpy())
+    check_parity(o.reshape(E * H, D), ref.reshape(E * H, D), f"attention E={E} H={H}/{H_kv} D={D} bs={bs}")
+    empty = np.where(cl.numpy() == 0)[0]
+    if len(empty):
+        assert torch.all(o[torch.as_tensor(empty)] == 0)
+    assert ops.device_status() == 0
+    o2 = _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o2), "not deterministic"
+
+
+def test_strided_q_and_out():
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(3, 32, 8, 128, 16, [10, 400, 77], seed=5)
+    big = torch.zeros(3, 48, 128, dtype=torch.bfloat16, device="cuda")
+    big[:, :32] = q.cuda()
+    out = torch.full((3, 40, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    ops.paged_decode_attention(big[:, :32], k_pool.cuda(), v_pool.cuda(), bt.cuda(), cl.cuda(), max_ctx,
+                               out=out[:, :32])
+    ref = _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, :32], ref)
+    assert torch.all(out[:, 32:] == 7.0)
+
+
+def test_graph_replay_matches_eager():
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(8, 32, 8, 128, 16, [1025] * 8, seed=9)
+    q, k_pool, v_pool, bt, cl = q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda(), cl.cuda()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.paged_decode_attention(q, k_pool, v_pool, bt, cl, max_ctx)  # workspace for this stream
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        out = ops.paged_decode_attention(q, k_pool, v_pool, bt, cl, max_ctx)
+    for trial in range(3):
+        q.copy_(torch.randn_like(q, dtype=torch.float32).to(torch.bfloat16))
+        cl.copy_(torch.randint(1, 1026, (8,), dtype=torch.int32, device="cuda"))
+        g.replay()
+        eager = ops.paged_decode_attention(q, k_pool, v_pool, bt, cl, max_ctx)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager), trial
+
+
+def test_bad_block_id_is_reported_not_read():
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(2, 8, 2, 64, 16, [40, 40], seed=3)
+    bt[1, 1] = 10_000  # outside the pool
+    ops.device_status()  # clear
+    _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    assert ops.device_status() == _lib.LSE_ERR_INVALID_ARG
+    assert ops.device_status() == 0
+
+
+def test_argument_errors():
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(2, 12, 8, 128, 16, [5, 6])  # H % H_kv != 0
+    with pytest.raises(_lib.LseError):
+        _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(2, 8, 8, 96, 16, [5, 6])  # head_dim 96
+    with pytest.raises(_lib.LseError):
+        _run(q, k_pool, v_pool, bt, cl, max_ctx)
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(2, 8, 8, 64, 16, [5, 6])
+    with pytest.raises(ValueError):
+        ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda().long(), cl.cuda(), max_ctx)

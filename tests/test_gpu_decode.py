@@ -60,3 +60,23 @@ def test_int8_lm_head_matches_dequantized_head():
     assert ((q - ref).abs().max() / ref.abs().max()).item() < 1e-2
     assert ((q - bf).abs().max() / bf.abs().max()).item() < 5e-2
     assert decode_bytes_per_step(TINY, 4, 16, True, int8_lm_head=True) < decode_bytes_per_step(TINY, 4, 16, True)
+
+
+def test_paged_attention_step_matches_sdpa_on_the_same_cache():
+    """The decode step with the paged kernel over a shuffled pool equals the step with torch
+    SDPA over the same K/V laid out contiguously."""
+    paged = DecodeModel(TINY, batch=5, context=37, device="cuda", seed=13, quantize=True, attention="paged")
+    sdpa = DecodeModel(TINY, batch=5, context=37, device="cuda", seed=13, quantize=True, attention="sdpa",
+                       weights=paged.weights)
+    sdpa.proj = paged.proj
+    bs, bt = paged.block_size, paged.kv["block_table"].long()
+    pos = torch.arange(38, device="cuda")
+    for li in range(TINY.layers):
+        for name in ("k", "v"):
+            pool = paged.kv[name][li]  # [nb, bs, Hkv, hd]
+            gathered = pool[bt[:, pos // bs], pos % bs]  # [B, ctx + 1, Hkv, hd]
+            sdpa.kv[name][li].copy_(gathered.permute(0, 2, 1, 3))
+    tokens = torch.tensor([1, 2, 3, 500, 999], device="cuda")
+    a, b = paged.logits(tokens), sdpa.logits(tokens)
+    err = ((a - b).abs().max() / b.abs().max()).item()
+    assert err < 2e-2, err

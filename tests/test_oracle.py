@@ -167,3 +167,28 @@ def test_parity_metric_definition():
     bad = good.copy()
     bad[1, 2] = -bad[1, 2]
     assert not parity_errors(bad, good)[1]
+
+
+def test_attention_oracle_matches_torch_sdpa_in_float64():
+    """Pin the paged decode-attention oracle: gathered through a shuffled block table, it
+    equals torch's scaled_dot_product_attention (float64, GQA) on the contiguous K/V."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle.ref_attention import gather_kv, ref_paged_decode_attention
+
+    g = torch.Generator().manual_seed(0)
+    E, H, H_kv, D, bs = 3, 8, 2, 16, 4
+    ctx = np.array([1, 9, 13])
+    nbps = 4
+    bt = torch.randperm(E * nbps + 2, generator=g)[: E * nbps].view(E, nbps).numpy()
+    k_pool = torch.randn(E * nbps + 2, bs, H_kv, D, generator=g, dtype=torch.float64).numpy()
+    v_pool = torch.randn(E * nbps + 2, bs, H_kv, D, generator=g, dtype=torch.float64).numpy()
+    q = torch.randn(E, H, D, generator=g, dtype=torch.float64).numpy()
+    out = ref_paged_decode_attention(q, k_pool, v_pool, bt, ctx)
+    for e in range(E):
+        k = torch.from_numpy(gather_kv(k_pool, bt, e, int(ctx[e]))).permute(1, 0, 2)[None]
+        v = torch.from_numpy(gather_kv(v_pool, bt, e, int(ctx[e]))).permute(1, 0, 2)[None]
+        ref = F.scaled_dot_product_attention(torch.from_numpy(q[e])[None, :, None], k, v, enable_gqa=True)
+        np.testing.assert_allclose(out[e], ref[0, :, 0].numpy(), rtol=1e-12, atol=1e-12)
+    assert np.all(ref_paged_decode_attention(q, k_pool, v_pool, bt, np.array([0, 0, 0])) == 0)
