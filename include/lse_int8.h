@@ -181,6 +181,25 @@ int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, i
                                int64_t o_stride_e, int64_t o_stride_h, void *workspace, size_t workspace_bytes,
                                void *stream);
 
+/*
+ * RoPE and K/V write on the fused QKV output (the reference's write_kv_and_project_q,
+ * src/llm_serving_engine/model/model_runner.py:342-355, with transformers'
+ * apply_rotary_pos_emb): for token m (of M) and head h of qkv [M, (H + 2 H_kv) * D] (row stride
+ * ld_qkv; q heads, then k heads, then v heads),
+ *   q and k are rotated (rotate-half): out[d] = x[d] cos[m,d] - x[d+D/2] sin[m,d],
+ *                                      out[d+D/2] = x[d+D/2] cos[m,d+D/2] + x[d] sin[m,d+D/2]
+ *   q_out[h, m, :]                                   rotated q, bf16 [H, M, D]
+ *   k_dst[kv_offset[m] + kvh * kv_head_stride + :]   rotated k, bf16
+ *   v_dst[kv_offset[m] + kvh * kv_head_stride + :]   v as it is, bf16
+ * cos, sin: [M, D] with row stride ld_cs, fp32 (LSE_F32) or bf16 (LSE_BF16).  For the
+ * reference's pool [num_blocks, block_size, H_kv, D], kv_offset[m] =
+ * (dest_block_id[m] * block_size + dest_within[m]) * H_kv * D and kv_head_stride = D.
+ * fp32 arithmetic, one bf16 rounding per output.
+ */
+int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
+                      const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
+                      void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride, void *stream);
+
 /* Bytes of the counter region at the start of every workspace (must start zeroed). */
 #define LSE_WS_COUNTER_BYTES 65536
 

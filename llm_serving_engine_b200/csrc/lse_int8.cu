@@ -16,6 +16,7 @@
 
 #include "../../include/lse_int8.h"
 #include "decode_attn.cuh"
+#include "rope_kv.cuh"
 #include "gemv_i8.cuh"
 #include "pack_w.cuh"
 #include "quantize.cuh"
@@ -849,5 +850,55 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "paged_decode_attention launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// lse_rope_kv_write: RoPE on q and k of the fused QKV output, q transposed to
+// (heads, tokens, head_dim), k and v written to their per-token slots (rope_kv.cuh).
+// ---------------------------------------------------------------------------------------
+extern "C" int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
+                                 const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
+                                 void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride,
+                                 void *stream) {
+    if (M < 0 || H <= 0 || H_kv <= 0 || D <= 0 || (D & 1)) return LSE_ERR_INVALID_ARG;
+    if (M == 0) return LSE_OK;
+    if (!qkv || !cos || !sin || !q_out || !k_dst || !v_dst || !kv_offset) return LSE_ERR_INVALID_ARG;
+    if (ld_qkv < (H + 2 * H_kv) * D || ld_cs < D) return LSE_ERR_INVALID_ARG;
+    if (cs_dtype != LSE_F32 && cs_dtype != LSE_BF16) return LSE_ERR_INVALID_ARG;
+    if (M > INT32_MAX || (H + 2 * H_kv) * D > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(qkv) & 1u) || (reinterpret_cast<uintptr_t>(q_out) & 1u) ||
+        (reinterpret_cast<uintptr_t>(k_dst) & 1u) || (reinterpret_cast<uintptr_t>(v_dst) & 1u) ||
+        (reinterpret_cast<uintptr_t>(kv_offset) & 7u) ||
+        (reinterpret_cast<uintptr_t>(cos) & (cs_dtype == LSE_F32 ? 3u : 1u)) ||
+        (reinterpret_cast<uintptr_t>(sin) & (cs_dtype == LSE_F32 ? 3u : 1u)))
+        return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    rope::Params p{};
+    p.qkv = static_cast<const __nv_bfloat16 *>(qkv);
+    p.ld_qkv = ld_qkv;
+    p.cos = cos;
+    p.sin = sin;
+    p.ld_cs = ld_cs;
+    p.cs_bf16 = cs_dtype == LSE_BF16;
+    p.q_out = static_cast<__nv_bfloat16 *>(q_out);
+    p.k_dst = static_cast<__nv_bfloat16 *>(k_dst);
+    p.v_dst = static_cast<__nv_bfloat16 *>(v_dst);
+    p.kv_off = kv_offset;
+    p.kv_head_stride = kv_head_stride;
+    p.M = static_cast<int>(M);
+    p.H = static_cast<int>(H);
+    p.H_kv = static_cast<int>(H_kv);
+    p.D = static_cast<int>(D);
+    const int64_t total = M * (H + 2 * H_kv) * (D / 2);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 8LL * g_dev[dev].num_sms);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, rope::rope_kv_kernel, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "rope_kv_write launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }

@@ -69,12 +69,6 @@ def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
 
 
-def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    # x [B, heads, head_dim]; rotate-half convention (transformers' Llama)
-    x1, x2 = x.chunk(2, dim=-1)
-    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
-
-
 def _bf16_mlp(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, inter: int) -> torch.Tensor:
     gu = F.linear(x, w_gate_up)
     return F.linear(F.silu(gu[:, :inter]) * gu[:, inter:], w_down)
@@ -123,8 +117,9 @@ class DecodeModel:
         self.kv = kv if kv is not None else self._make_kv(dev, seed)
         inv = 1.0 / (shape.rope_theta ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
         ang = context * inv
-        self.cos = torch.cos(ang).to(torch.bfloat16)
-        self.sin = torch.sin(ang).to(torch.bfloat16)
+        # transformers' rotary embedding at the step's position (duplicated halves), per token
+        self.cos_full = torch.cat([torch.cos(ang), torch.cos(ang)]).expand(batch, hd).contiguous()
+        self.sin_full = torch.cat([torch.sin(ang), torch.sin(ang)]).expand(batch, hd).contiguous()
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
         self.lm_head_int8 = None
         if quantize_lm_head:
@@ -139,7 +134,10 @@ class DecodeModel:
         if self.attention == "sdpa":
             def kv():
                 return torch.randn(B, s.kv_heads, self.context + 1, hd, generator=gk, device=dev).to(torch.bfloat16)
-            return {"k": [kv() for _ in range(s.layers)], "v": [kv() for _ in range(s.layers)]}
+            T = self.context + 1  # the new token's slot: position `context` of every sequence
+            return {"k": [kv() for _ in range(s.layers)], "v": [kv() for _ in range(s.layers)],
+                    "kv_off": (torch.arange(B, device=dev) * s.kv_heads * T + self.context) * hd,
+                    "kv_head_stride": T * hd}
         bs = self.block_size
         nbps = -(-(self.context + 1) // bs)
         nb = B * nbps + 1
@@ -151,7 +149,7 @@ class DecodeModel:
         pos = self.context  # the new token's position
         slot = table[:, pos // bs].long() * bs + pos % bs  # its pool slot per sequence
         return {"k": [pool() for _ in range(s.layers)], "v": [pool() for _ in range(s.layers)],
-                "block_table": table, "slot": slot,
+                "block_table": table, "kv_off": slot * s.kv_heads * hd, "kv_head_stride": hd,
                 "context_len": torch.full((B,), self.context + 1, dtype=torch.int32, device=dev)}
 
     def set_lm_head_int8(self, on: bool) -> None:
@@ -172,22 +170,17 @@ class DecodeModel:
             n_in, n_post = self.norms[li]
             x = _rms_norm(h, n_in, s.eps)
             qkv = qkv_p(x)
-            q = qkv[:, :s.heads * hd].view(B, s.heads, hd)
-            k = qkv[:, s.heads * hd:(s.heads + s.kv_heads) * hd].view(B, s.kv_heads, hd)
-            v = qkv[:, (s.heads + s.kv_heads) * hd:].view(B, s.kv_heads, hd)
-            q, k = _rope(q, self.cos, self.sin), _rope(k, self.cos, self.sin)
             kc, vc = self.kv["k"][li], self.kv["v"][li]
             if not in_place:
                 kc, vc = kc.clone(), vc.clone()
+            # RoPE on q and k, k and v into their slots, q as (heads, B, hd): one kernel
+            qh = ops.rope_kv_write(qkv, s.heads, s.kv_heads, hd, self.cos_full, self.sin_full, kc, vc,
+                                   self.kv["kv_off"], self.kv["kv_head_stride"])
+            q = qh.transpose(0, 1)  # [B, heads, hd] view
             if self.attention == "paged":
-                nb, bs = kc.shape[0], kc.shape[1]
-                kc.view(nb * bs, s.kv_heads, hd).index_copy_(0, self.kv["slot"], k)
-                vc.view(nb * bs, s.kv_heads, hd).index_copy_(0, self.kv["slot"], v)
                 attn = ops.paged_decode_attention(q, kc, vc, self.kv["block_table"], self.kv["context_len"],
                                                   self.context + 1)
             else:
-                kc[:, :, pos] = k
-                vc[:, :, pos] = v
                 attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
             h = o_p(attn.reshape(B, s.heads * hd), residual=h)  # residual + o_proj(attn)
             x = _rms_norm(h, n_post, s.eps)

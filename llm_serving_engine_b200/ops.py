@@ -34,6 +34,8 @@ __all__ = [
     "int8_gate_up_silu_packed",
     "GATE_UP_SILU_MAX_M",
     "paged_decode_attention",
+    "rope_kv_write",
+    "pool_slot_offsets",
     "workspace_for",
     "device_status",
     "ALGO_AUTO",
@@ -262,6 +264,54 @@ def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
                                        q.data_ptr(), s.data_ptr(), stream.cuda_stream)
     _lib.check(rc, "lse_int8_quantize")
     return q, s
+
+
+def pool_slot_offsets(dest_block_id: torch.Tensor, dest_within: torch.Tensor, k_pool: torch.Tensor) -> torch.Tensor:
+    """int64 element offsets of tokens' slots (KV head 0) in a [num_blocks, block_size, H_kv, D]
+    pool, from the reference's `dest_block_id` / `dest_within` (`model_runner.py:342-355`)."""
+    _nb, bs, h_kv, d = k_pool.shape
+    return (dest_block_id.long() * bs + dest_within.long()) * (h_kv * d)
+
+
+def rope_kv_write(qkv: torch.Tensor, n_heads: int, n_kv_heads: int, head_dim: int, cos: torch.Tensor,
+                  sin: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor, kv_offset: torch.Tensor,
+                  kv_head_stride: int | None = None, q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE on q and k of the fused QKV output, k and v written to their slots, q returned as
+    (n_heads, tokens, head_dim) - `write_kv_and_project_q` after the projection, in one launch.
+
+    qkv: bf16 [M, (H + 2 H_kv) * D] (last dim contiguous); cos / sin: [M, D] fp32 or bf16
+    (transformers' per-token rotary embedding, duplicated halves); k_dst / v_dst: bf16 caches
+    (e.g. the [num_blocks, block_size, H_kv, D] pools); kv_offset: int64 [M] element offsets
+    of each token's slot for KV head 0 (`pool_slot_offsets`), KV heads kv_head_stride apart
+    (default head_dim).
+    """
+    M = qkv.shape[0]
+    D = head_dim
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 2 or qkv.stride(-1) != 1 or qkv.shape[1] != (n_heads + 2 * n_kv_heads) * D:
+        raise ValueError("rope_kv_write: qkv must be bf16 [M, (H + 2 H_kv) * D] with a contiguous last dim")
+    if cos.shape != (M, D) or sin.shape != (M, D) or cos.dtype != sin.dtype or cos.stride() != sin.stride() \
+            or cos.stride(-1) != 1 or cos.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("rope_kv_write: cos / sin must be [M, D] fp32 or bf16 with equal, row-contiguous strides")
+    if k_dst.dtype != torch.bfloat16 or v_dst.dtype != torch.bfloat16 or not (k_dst.is_contiguous() and v_dst.is_contiguous()):
+        raise ValueError("rope_kv_write: k_dst / v_dst must be contiguous bf16")
+    if kv_offset.dtype != torch.int64 or kv_offset.shape != (M,) or not kv_offset.is_contiguous():
+        raise ValueError("rope_kv_write: kv_offset must be int64 [M]")
+    if not all(t.is_cuda and t.device == qkv.device for t in (cos, sin, k_dst, v_dst, kv_offset)):
+        raise RuntimeError("rope_kv_write runs on CUDA only, all tensors on qkv's device")
+    if q_out is None:
+        q_out = torch.empty((n_heads, M, D), dtype=torch.bfloat16, device=qkv.device)
+    elif q_out.dtype != torch.bfloat16 or q_out.shape != (n_heads, M, D) or not q_out.is_contiguous():
+        raise ValueError("rope_kv_write: q_out must be contiguous bf16 [H, M, D]")
+    if M == 0:
+        return q_out
+    _ensure_device(qkv.device)
+    cs = _lib.DT_F32 if cos.dtype == torch.float32 else _lib.DT_BF16
+    rc = _lib.load().lse_rope_kv_write(
+        qkv.data_ptr(), M, qkv.stride(0), n_heads, n_kv_heads, D, cos.data_ptr(), sin.data_ptr(), cos.stride(0), cs,
+        q_out.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), kv_offset.data_ptr(),
+        D if kv_head_stride is None else int(kv_head_stride), torch.cuda.current_stream(qkv.device).cuda_stream)
+    _lib.check(rc, "lse_rope_kv_write")
+    return q_out
 
 
 # Split-K scratch of the decode attention, one zero-initialised buffer per (device, stream,

@@ -111,3 +111,40 @@ def test_argument_errors():
     q, k_pool, v_pool, bt, cl, max_ctx = _case(2, 8, 8, 64, 16, [5, 6])
     with pytest.raises(ValueError):
         ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda().long(), cl.cuda(), max_ctx)
+
+
+# ---- RoPE + K/V write on the fused QKV output ------------------------------------------
+def _rope_ref(x, cos, sin):
+    """transformers' rotate-half RoPE in fp32: x [M, heads, D], cos/sin [M, D]."""
+    half = x.shape[-1] // 2
+    rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+    return x * cos[:, None, :] + rot * sin[:, None, :]
+
+
+@pytest.mark.parametrize("M,H,H_kv,D,cs_dtype", [(1, 32, 8, 128, torch.float32), (7, 32, 8, 128, torch.bfloat16),
+                                                 (64, 8, 2, 64, torch.float32), (130, 4, 4, 128, torch.bfloat16)])
+def test_rope_kv_write_matches_torch(M, H, H_kv, D, cs_dtype):
+    g = torch.Generator().manual_seed(M + H)
+    qkv = torch.randn(M, (H + 2 * H_kv) * D, generator=g).to(torch.bfloat16).cuda()
+    pos = torch.randint(0, 4096, (M,), generator=g).float()
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2).float() / D))
+    ang = pos[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(cs_dtype).cuda()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(cs_dtype).cuda()
+    bs, nb = 16, M + 5
+    k_pool = torch.zeros(nb, bs, H_kv, D, dtype=torch.bfloat16, device="cuda")
+    v_pool = torch.zeros_like(k_pool)
+    dest_block = torch.randperm(nb, generator=g)[:M].cuda()
+    dest_within = torch.randint(0, bs, (M,), generator=g).cuda()
+    off = ops.pool_slot_offsets(dest_block, dest_within, k_pool)
+    q = ops.rope_kv_write(qkv, H, H_kv, D, cos, sin, k_pool, v_pool, off)
+    torch.cuda.synchronize()
+    x = qkv.float().view(M, H + 2 * H_kv, D)
+    qr = _rope_ref(x[:, :H], cos.float(), sin.float())
+    kr = _rope_ref(x[:, H:H + H_kv], cos.float(), sin.float())
+    torch.testing.assert_close(q.float(), qr.transpose(0, 1).contiguous(), rtol=8e-3, atol=1e-2)
+    torch.testing.assert_close(k_pool[dest_block, dest_within].float(), kr, rtol=8e-3, atol=1e-2)
+    assert torch.equal(v_pool[dest_block, dest_within], qkv.view(M, H + 2 * H_kv, D)[:, H + H_kv:])
+    untouched = torch.ones(nb, bs, dtype=torch.bool, device="cuda")
+    untouched[dest_block, dest_within] = False
+    assert torch.all(k_pool[untouched] == 0) and torch.all(v_pool[untouched] == 0)
