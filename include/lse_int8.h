@@ -200,6 +200,16 @@ int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int
                       const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
                       void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride, void *stream);
 
+/*
+ * RMSNorm of bf16 rows (transformers' LlamaRMSNorm, every decoder layer's input and
+ * post-attention norm and the final norm):
+ *   y[m, :] = bf16( x[m, :] * rsqrt(mean_n x[m, n]^2 + eps) * weight[:] )   (fp32 arithmetic)
+ * x [M, N] row stride ldx, weight bf16 [N], y [M, N] row stride ldy (may be x itself);
+ * N, ldx, ldy multiples of 8, x / weight / y 16-byte aligned.
+ */
+int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
+                 int64_t ldy, void *stream);
+
 /* Bytes of the counter region at the start of every workspace (must start zeroed). */
 #define LSE_WS_COUNTER_BYTES 65536
 

@@ -17,6 +17,7 @@
 #include "../../include/lse_int8.h"
 #include "decode_attn.cuh"
 #include "rope_kv.cuh"
+#include "rms_norm.cuh"
 #include "gemv_i8.cuh"
 #include "pack_w.cuh"
 #include "quantize.cuh"
@@ -900,5 +901,30 @@ extern "C" int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int
     cudaError_t e = cudaLaunchKernelEx(&cfg, rope::rope_kv_kernel, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "rope_kv_write launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// lse_rms_norm: RMSNorm of bf16 rows (rms_norm.cuh).
+// ---------------------------------------------------------------------------------------
+extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
+                            int64_t ldy, void *stream) {
+    if (M < 0 || N <= 0 || ldx < N || ldy < N || !(eps >= 0.f)) return LSE_ERR_INVALID_ARG;
+    if (M == 0) return LSE_OK;
+    if (!x || !weight || !y) return LSE_ERR_INVALID_ARG;
+    if (M > INT32_MAX || N > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((N & 7) || (ldx & 7) || (ldy & 7) || !aligned16(x) || !aligned16(weight) || !aligned16(y))
+        return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(norm::THREADS), 0, static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, norm::rms_norm_kernel, static_cast<const __nv_bfloat16 *>(x), ldx,
+                                       static_cast<const __nv_bfloat16 *>(weight), static_cast<int>(N), eps,
+                                       static_cast<__nv_bfloat16 *>(y), ldy);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "rms_norm launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }

@@ -35,6 +35,7 @@ __all__ = [
     "GATE_UP_SILU_MAX_M",
     "paged_decode_attention",
     "rope_kv_write",
+    "rms_norm",
     "pool_slot_offsets",
     "workspace_for",
     "device_status",
@@ -264,6 +265,29 @@ def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
                                        q.data_ptr(), s.data_ptr(), stream.cuda_stream)
     _lib.check(rc, "lse_int8_quantize")
     return q, s
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """transformers' LlamaRMSNorm on bf16 rows in one kernel: x [..., N] bf16 (last dim
+    contiguous), weight bf16 [N]; fp32 arithmetic, one bf16 rounding."""
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or not (x.is_cuda and weight.is_cuda):
+        raise ValueError("rms_norm: x and weight must be bf16 CUDA tensors")
+    N = x.shape[-1]
+    if weight.shape != (N,) or not weight.is_contiguous():
+        raise ValueError(f"rms_norm: weight must be contiguous [{N}]")
+    x2 = x.reshape(-1, N)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    y2 = out.view(-1, N)
+    if x2.shape[0] == 0:
+        return out
+    _ensure_device(x.device)
+    rc = _lib.load().lse_rms_norm(x2.data_ptr(), x2.shape[0], N, x2.stride(0), weight.data_ptr(), float(eps),
+                                  y2.data_ptr(), y2.stride(0), torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(rc, "lse_rms_norm")
+    return out
 
 
 def pool_slot_offsets(dest_block_id: torch.Tensor, dest_within: torch.Tensor, k_pool: torch.Tensor) -> torch.Tensor:

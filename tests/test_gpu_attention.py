@@ -148,3 +148,14 @@ def test_rope_kv_write_matches_torch(M, H, H_kv, D, cs_dtype):
     untouched = torch.ones(nb, bs, dtype=torch.bool, device="cuda")
     untouched[dest_block, dest_within] = False
     assert torch.all(k_pool[untouched] == 0) and torch.all(v_pool[untouched] == 0)
+
+
+@pytest.mark.parametrize("M,N", [(1, 4096), (64, 4096), (5, 8192), (3, 136)])
+def test_rms_norm_matches_torch(M, N):
+    g = torch.Generator().manual_seed(M + N)
+    x = (torch.randn(M, N, generator=g) * 3).to(torch.bfloat16).cuda()
+    w = (torch.rand(N, generator=g) + 0.5).to(torch.bfloat16).cuda()
+    y = ops.rms_norm(x, w, 1e-5)
+    xf = x.double()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.double()
+    torch.testing.assert_close(y.double(), ref, rtol=8e-3, atol=1e-3)
