@@ -30,7 +30,12 @@ def main(argv=None):
     ap.add_argument("--algo", choices=list(ALGOS), default="auto")
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--rowmajor", action="store_true", help="row-major W instead of the packed layout")
+    ap.add_argument("--attention", type=int, default=0, metavar="E",
+                    help="profile the paged decode attention instead: E sequences of 1025 positions, "
+                         "Llama-3-8B attention shape, three layers' pools in rotation")
     args = ap.parse_args(argv)
+    if args.attention:
+        return attention_case(args.attention, args.launches)
     K, N = (LLAMA3_8B_SHAPES if args.model == "8b" else LLAMA3_70B_SHAPES)[args.shape]
     copies = max(2, -(-3 * 128 * 2**20 // (N * K)))  # > 3x L2 of weights in rotation
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -67,6 +72,41 @@ def main(argv=None):
     print(f"M={args.M} {args.model}:{args.shape} K={K} N={N} algo={args.algo} {'row-major' if args.rowmajor else 'packed'}: {ms * 1e3:.2f} us/launch "
           f"({linear_bytes(args.M, K, N) / ms / 1e6:.0f} GB/s, {linear_flops(args.M, K, N) / ms / 1e9:.1f} TFLOP/s, "
           f"CUDA-graph launches)")
+    assert ops.device_status() == 0
+
+
+def attention_case(E: int, launches: int) -> None:
+    """`launches` paged decode-attention calls (32 query / 8 KV heads, head_dim 128, block_size
+    16, 1025 positions, shuffled block table) over three layers' pools, in one CUDA graph."""
+    H, H_kv, D, bs, ctx = 32, 8, 128, 16, 1025
+    g = torch.Generator(device="cuda").manual_seed(0)
+    nbps = -(-ctx // bs)
+    nb = E * nbps + 1
+    bt = torch.randperm(nb, device="cuda", generator=g)[: E * nbps].view(E, nbps).to(torch.int32)
+    cl = torch.full((E,), ctx, dtype=torch.int32, device="cuda")
+    pools = [(torch.randn(nb, bs, H_kv, D, device="cuda", generator=g).to(torch.bfloat16),
+              torch.randn(nb, bs, H_kv, D, device="cuda", generator=g).to(torch.bfloat16)) for _ in range(3)]
+    q = torch.randn(E, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.paged_decode_attention(q, *pools[0], bt, cl, ctx, out=o)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(launches):
+            ops.paged_decode_attention(q, *pools[i % 3], bt, cl, ctx, out=o)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / launches
+    byts = E * ctx * H_kv * D * 2 * 2
+    print(f"paged decode attention E={E} ctx={ctx}: {ms * 1e3:.2f} us/launch ({byts / ms / 1e6:.0f} GB/s of K/V)")
     assert ops.device_status() == 0
 
 
