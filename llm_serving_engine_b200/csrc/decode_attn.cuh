@@ -17,10 +17,11 @@
 //     scores S = Q K^T are warp MMAs with the query heads as rows, the online softmax runs
 //     on the S accumulators, which are then the row operand of O += P V (V transposed by
 //     ldmatrix.trans);
-//   * the four warps' (max, sum, acc) merge in shared memory; with several splits each CTA
-//     writes its partial to the workspace and the CTA that arrives last on the (sequence,
-//     KV head) counter merges them in split order and writes o (deterministic; it re-arms
-//     the counter).  No CTA waits for another.
+//   * the four warps' (max, sum, acc) merge in shared memory; positions are split over
+//     several CTAs only for small batches (the host plan), in which case each CTA writes its
+//     partial to the workspace and the CTA that arrives last on the (sequence, KV head)
+//     counter merges them in split order and writes o (deterministic; it re-arms the
+//     counter).  No CTA waits for another.
 // A block id outside [0, num_blocks) makes that position masked (never read) and records
 // LSE_ERR_INVALID_ARG in the device status word.
 #pragma once

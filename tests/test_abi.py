@@ -104,3 +104,48 @@ def test_library_has_no_libcuda_link_dependency():
     deps = subprocess.run(["ldd", build.LIB_PATH], capture_output=True, text=True).stdout
     assert "libcuda.so" not in deps and "libcudart" not in deps, deps
     ctypes.CDLL(build.LIB_PATH)
+
+
+def test_attention_rope_norm_host_validation():
+    """The decode-attention, RoPE/K-V and RMSNorm entries refuse bad arguments on the host,
+    before any device call (no GPU here)."""
+    lib = _lib.load()
+    P = 256  # any 256-aligned non-null address: never dereferenced on these paths
+    # H not a multiple of H_kv; head_dim 96; block table narrower than max_context / block_size
+    assert lib.lse_paged_decode_attention(P, 2, 12, 128, 1536, 128, P, P, 10, 16, 8, P, 4, P, 64, 0.1, P, 1536, 128,
+                                          None, 0, None) == _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_paged_decode_attention(P, 2, 8, 96, 768, 96, P, P, 10, 16, 8, P, 4, P, 64, 0.1, P, 768, 96,
+                                          None, 0, None) == _lib.LSE_ERR_UNSUPPORTED
+    assert lib.lse_paged_decode_attention(P, 2, 8, 128, 1024, 128, P, P, 10, 16, 8, P, 3, P, 64, 0.1, P, 1024, 128,
+                                          None, 0, None) == _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_paged_decode_attention(P + 1, 2, 8, 128, 1024, 128, P, P, 10, 16, 8, P, 4, P, 64, 0.1, P, 1024,
+                                          128, None, 0, None) == _lib.LSE_ERR_ALIGNMENT
+    assert lib.lse_paged_decode_attention(P, 0, 8, 128, 1024, 128, P, P, 10, 16, 8, P, 4, P, 64, 0.1, P, 1024, 128,
+                                          None, 0, None) == _lib.LSE_OK  # no sequences: nothing to do
+    # odd head_dim; cos/sin dtype code outside {F32, BF16}
+    assert lib.lse_rope_kv_write(P, 4, 1000, 8, 2, 63, P, P, 63, _lib.DT_F32, P, P, P, P, 63, None) == \
+        _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_rope_kv_write(P, 4, 1536, 8, 2, 128, P, P, 128, _lib.DT_F16, P, P, P, P, 128, None) == \
+        _lib.LSE_ERR_INVALID_ARG
+    # RMSNorm: N % 8, ld < N, negative eps
+    assert lib.lse_rms_norm(P, 4, 12, 16, P, 1e-5, P, 16, None) == _lib.LSE_ERR_ALIGNMENT
+    assert lib.lse_rms_norm(P, 4, 64, 32, P, 1e-5, P, 64, None) == _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_rms_norm(P, 4, 64, 64, P, -1.0, P, 64, None) == _lib.LSE_ERR_INVALID_ARG
+
+
+def test_python_ops_refuse_cpu_tensors():
+    """No CPU fallback: the torch-facing ops raise on CPU tensors."""
+    import torch
+
+    from llm_serving_engine_b200 import ops
+
+    q = torch.zeros(2, 8, 64, dtype=torch.bfloat16)
+    pool = torch.zeros(4, 16, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA only"):
+        ops.paged_decode_attention(q, pool, pool, torch.zeros(2, 2, dtype=torch.int32),
+                                   torch.ones(2, dtype=torch.int32), 16)
+    with pytest.raises(ValueError):
+        ops.rms_norm(torch.zeros(2, 64), torch.ones(64), 1e-5)
+    with pytest.raises((RuntimeError, ValueError)):
+        ops.rope_kv_write(torch.zeros(2, 12 * 64, dtype=torch.bfloat16), 8, 2, 64, torch.zeros(2, 64),
+                          torch.zeros(2, 64), pool, pool, torch.zeros(2, dtype=torch.int64))
