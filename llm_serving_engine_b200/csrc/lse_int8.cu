@@ -300,12 +300,13 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
 //     CTAs per SM (M <= 8; above that, four row blocks per CTA, so that each activation load,
 //     which costs eight L1 wavefronts, serves 64 weight rows);
 //   * many row blocks (N/16 >= 2 x SMs: QKV): CTAs of 8 warps on two row blocks, so every
-//     activation load serves 32 weight rows;
+//     activation load serves 32 weight rows, eight chunks per row block in registers (a warp's
+//     K slice is then two register groups deep at K = 4096: 2-4% faster than four);
 //   * few row blocks (O, down): CTAs of 16 warps, one row block (two for M > 8, where the
 //     activation loads, not the weight stream, would otherwise saturate L1);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
-// LSE_SKINNY_VARIANT=<0..14> pins one configuration for tuning runs (9, 10: the cp.async
+// LSE_SKINNY_VARIANT=<0..17> pins one configuration for tuning runs (9, 10: the cp.async
 // shared-memory weight ring, measured no faster than registers on B200).
 int skinny_variant() {
     static const int v = [] {
@@ -323,7 +324,7 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
                              int num_sms, cudaStream_t st) {
     if (variant < 0) {
         const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
-        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 11) : (rb_per_sm >= 2 ? 1 : 0);
+        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 11) : (rb_per_sm >= 2 ? 15 : 0);
     }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
@@ -351,6 +352,11 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
             case 12: return launch_skinny<MT, 4, 4, 2, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 13: return launch_skinny<MT, 4, 4, 2, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 14: return launch_skinny<MT, 8, 4, 1, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            // eight chunks per row block in registers: a short K slice (O, QKV at K = 4096) is
+            // one or two register groups deep instead of two to four
+            case 15: return launch_skinny<MT, 8, 2, 8, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 16: return launch_skinny<MT, 16, 1, 8, BF, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 17: return launch_skinny<MT, 8, 1, 8, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             default:
                 if constexpr (MT == 1) return launch_skinny<1, 16, 1, 4, false, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
                 else return launch_skinny<2, 16, 2, 4, true, 1, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
