@@ -449,6 +449,33 @@ def decode_attention(dev, warm, ops, hbm_peak):
     return out
 
 
+def bf16_cublas_points(layers: int, dev, warm, xs):
+    """Same-box comparison: torch F.linear (cuBLAS) with bf16 weights of the same shapes at
+    every decode-sweep point, `layers` distinct weights per graph (the reference's
+    quantize="none" projections).  Per point: us per launch and bf16 weight GB/s."""
+    g = torch.Generator(device=dev).manual_seed(29)
+    wts = {name: [torch.randn(N, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+           for name, (K, N) in LLAMA3_8B_SHAPES.items()}
+    out = []
+    for M in DECODE_M:
+        for name in SHAPE_ORDER:
+            K, N = LLAMA3_8B_SHAPES[name]
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+            def one(x=xs[(M, name)], y=y, ws=wts[name]):
+                for w in ws:
+                    torch.matmul(x, w.t(), out=y)
+            gr = capture(one, warm)
+            time_graph(gr, 2)
+            us = time_graph(gr, 10) / layers * 1e3
+            out.append({"M": M, "shape": name, "us": round(us, 3),
+                        "GBps": round((2 * N * K + 2 * M * K + 2 * M * N) / us / 1e3, 1)})
+            del gr
+    del wts
+    torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------------------
 def cpu_reference_sample(seconds: float):
     """The reference's CPU path (float32 nn.Linear on the dequantized weight, all host
@@ -655,6 +682,7 @@ def main():
     fused_mlp = fused_gate_up(weights, dev, warm, ops, hbm_peak)
     fused_res = fused_residual(weights, dev, warm, ops)
     attn = decode_attention(dev, warm, ops, hbm_peak)
+    cublas = bf16_cublas_points(layers, dev, warm, xs)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
@@ -709,6 +737,9 @@ def main():
         line["fused_gate_up_silu"] = fused_mlp
         line["fused_residual"] = fused_res
         line["decode_attention"] = attn
+        line["bf16_cublas_points"] = cublas
+        line["int8_speedup_vs_bf16_cublas"] = {f"M{p['M']}_{p['shape']}": round(c["us"] / p["us"], 3)
+                                               for p, c in zip(points, cublas)}
         if tp70b:
             line["config5_70b_column_split"] = tp70b
         if decode4:

@@ -53,7 +53,7 @@ struct Params {
     const int *context_len;   // [E]
     __nv_bfloat16 *o;         // [E, H, D], d contiguous
     int64_t o_stride_e, o_stride_h;
-    int E, H_kv, block_size, num_blocks, chunk, splits;
+    int E, H_kv, block_size, num_blocks, chunk, splits, max_ctx;
     float scale_log2;         // softmax scale * log2(e)
     float *part;              // [E, H_kv, splits, G, D + 2] fp32 partials (splits > 1)
     int *counters;            // [E * H_kv] arrival counters, zero between launches
@@ -112,24 +112,21 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // q and the pool come from earlier kernels
 
-    int ctx = p.context_len[e];
-    if (ctx > p.splits * p.chunk) {  // beyond the max_context the launch was sized for
-        if (split == 0 && threadIdx.x == 0) report_status(LSE_ERR_INVALID_ARG);
-        ctx = p.splits * p.chunk;
-    }
-    const int begin = split * p.chunk;
-    const int end = min(ctx, begin + p.chunk);
-
-    // This CTA's slice of the block table, staged once (-1: outside the pool).
+    // The context length, this CTA's slice of the block table (every entry of positions below
+    // max_context: independent of the context length, so both loads are in flight together)
+    // and q (below) are read at once; block ids are range-checked where they are used.
     __shared__ int s_blk[MAX_TABLE];
+    const int begin = split * p.chunk;
     const int first_bi = begin / p.block_size;
-    const int n_bi = end > begin ? (end - 1) / p.block_size - first_bi + 1 : 0;
-    for (int i = threadIdx.x; i < n_bi; i += THREADS) {
-        const int blk = p.block_table[e * p.bt_stride + first_bi + i];
-        const bool ok = blk >= 0 && blk < p.num_blocks;
-        if (!ok) report_status(LSE_ERR_INVALID_ARG);
-        s_blk[i] = ok ? blk : -1;
+    const int span = min(p.max_ctx, begin + p.chunk);  // positions this CTA may cover
+    const int n_bi = span > begin ? (span - 1) / p.block_size - first_bi + 1 : 0;
+    for (int i = threadIdx.x; i < n_bi; i += THREADS) s_blk[i] = p.block_table[e * p.bt_stride + first_bi + i];
+    int ctx = p.context_len[e];
+    if (ctx > p.max_ctx) {  // beyond the max_context the launch was sized for
+        if (split == 0 && threadIdx.x == 0) report_status(LSE_ERR_INVALID_ARG);
+        ctx = p.max_ctx;
     }
+    const int end = min(ctx, begin + p.chunk);
 
     // Q as the row operand, rows = query heads (rows >= G and 8..15 are zero): per K16 step
     // j, a0 = Q[r0][16j + 2q4 .. +1], a2 = Q[r0][16j + 8 + 2q4 .. +1].
@@ -154,7 +151,8 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
             const int pos = g0 + lane;
             const int bi = pos / p.block_size;
             const int blk = s_blk[bi - first_bi];
-            if (blk >= 0) my_slot = blk * p.block_size + (pos - bi * p.block_size);
+            if (blk >= 0 && blk < p.num_blocks) my_slot = blk * p.block_size + (pos - bi * p.block_size);
+            else report_status(LSE_ERR_INVALID_ARG);  // masked: the position is not read
         }
         const uint32_t kdst = wbase + st * STAGE_B, vdst = kdst + TILE_B;
         constexpr int RPI = 32 / CH;  // rows per instruction

@@ -836,6 +836,7 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
     p.num_blocks = static_cast<int>(num_blocks);
     p.chunk = pl.chunk;
     p.splits = pl.splits;
+    p.max_ctx = static_cast<int>(max_context);
     p.scale_log2 = scale * 1.4426950408889634f;  // log2(e): softmax in base 2
     p.counters = static_cast<int *>(workspace);
     p.part = need ? reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + attn_counter_bytes(E, H_kv)) : nullptr;
