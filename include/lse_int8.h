@@ -164,11 +164,10 @@ int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ld
  *            lse_device_status, as is a block id outside [0, num_blocks))
  *   o        bf16, element (e, h, d) at o[e * o_stride_e + h * o_stride_h + d]
  *   workspace  >= lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, block_size)
- *            bytes
- *            (0 allowed when that is 0), 16-byte aligned, zeroed once before its first use
- *            and then kept for this launch shape (E, H, H_kv, D, max_context) on one stream:
- *            the split-K arrival counters at its start are laid out per shape and left at
- *            zero by every call
+ *            bytes (0 allowed when that is 0), 16-byte aligned, zeroed once before its first
+ *            use; the split-K arrival counters at its start have the same place for every
+ *            launch shape and every call leaves them at zero, so one buffer per stream
+ *            (grown when a shape needs more) serves all shapes
  * D = 64 or 128 and G in {1, 2, 4, 8} (LSE_ERR_UNSUPPORTED otherwise).  fp32 softmax and
  * accumulation, one bf16 rounding of o.  A sequence with context_len 0 gets zeros.
  */

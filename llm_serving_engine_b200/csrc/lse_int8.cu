@@ -719,6 +719,13 @@ struct AttnPlan {
     int splits, chunk;
 };
 
+// Workspace of a split launch: a fixed region of arrival counters (one per (sequence, KV
+// head) pair; splits happen only for fewer pairs than this), then the fp32 partials.  The
+// counters sit at the same place for every launch shape, so one zero-initialised buffer
+// serves every shape on a stream.
+constexpr int64_t kAttnMaxSplitPairs = 1024;
+constexpr size_t kAttnCounterBytes = kAttnMaxSplitPairs * sizeof(int);
+
 // Split the positions of a (sequence, KV head) pair only when there are too few pairs to give
 // most SMs a CTA.  A CTA pays several microseconds before its stream is full (context length
 // and block-table loads, pipeline fill) and again at the end (warp merge, partials): measured
@@ -728,7 +735,8 @@ AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_s
     const int64_t pairs = std::max<int64_t>(1, E * H_kv);
     const int64_t cap = std::max<int64_t>(1, (max_context + 255) / 256);  // chunks of >= 256 positions
     int64_t splits = 1;
-    if (2 * pairs < static_cast<int64_t>(num_sms)) splits = std::min<int64_t>((num_sms + pairs - 1) / pairs, cap);
+    if (2 * pairs < static_cast<int64_t>(num_sms) && pairs <= kAttnMaxSplitPairs)
+        splits = std::min<int64_t>((num_sms + pairs - 1) / pairs, cap);
     // a CTA stages at most attn::MAX_TABLE block-table entries (chunk / block_size + 1)
     const int64_t max_chunk = (attn::MAX_TABLE - 1) * block_size / 32 * 32;
     splits = std::max<int64_t>(splits, (max_context + max_chunk - 1) / max_chunk);
@@ -738,12 +746,10 @@ AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_s
     return {static_cast<int>(splits), static_cast<int>(chunk)};
 }
 
-size_t attn_counter_bytes(int64_t E, int64_t H_kv) { return static_cast<size_t>((E * H_kv * 4 + 255) / 256 * 256); }
-
 size_t attn_workspace_bytes(const AttnPlan &pl, int64_t E, int64_t H, int64_t H_kv, int64_t D) {
     if (pl.splits <= 1) return 0;
     const int64_t G = H / H_kv;
-    return attn_counter_bytes(E, H_kv) + static_cast<size_t>(E * H_kv) * pl.splits * G * (D + 2) * sizeof(float);
+    return kAttnCounterBytes + static_cast<size_t>(E * H_kv) * pl.splits * G * (D + 2) * sizeof(float);
 }
 
 template <int D, int G>
@@ -839,7 +845,7 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
     p.max_ctx = static_cast<int>(max_context);
     p.scale_log2 = scale * 1.4426950408889634f;  // log2(e): softmax in base 2
     p.counters = static_cast<int *>(workspace);
-    p.part = need ? reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + attn_counter_bytes(E, H_kv)) : nullptr;
+    p.part = need ? reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kAttnCounterBytes) : nullptr;
     cudaError_t e;
     if (D == 128) {
         switch (G) {

@@ -338,10 +338,11 @@ def rope_kv_write(qkv: torch.Tensor, n_heads: int, n_kv_heads: int, head_dim: in
     return q_out
 
 
-# Split-K scratch of the decode attention, one zero-initialised buffer per (device, stream,
-# launch shape): the arrival counters at its start are laid out per shape, so a buffer is
-# never shared between shapes.  Created outside captures only.
+# Split-K scratch of the decode attention: one zero-initialised, grow-only buffer per (device,
+# stream); its arrival counters sit at a fixed place for every launch shape and every call
+# leaves them at zero.  Created (or grown) outside captures only.
 _attn_ws: dict[tuple, torch.Tensor] = {}
+_attn_ws_retired: list[torch.Tensor] = []  # outgrown buffers stay alive: captured graphs may use them
 
 
 def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
@@ -381,12 +382,14 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     lib = _lib.load()
     stream = torch.cuda.current_stream(q.device)
     need = int(lib.lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, bs))
-    key = (q.device.index, stream.cuda_stream, E, H, H_kv, D, int(max_context), bs)
+    key = (q.device.index, stream.cuda_stream)
     ws = _attn_ws.get(key)
-    if need and ws is None:
+    if need and (ws is None or ws.numel() < need):
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("paged_decode_attention: workspace must grow outside a CUDA graph capture; "
                                "run one eager call with the same shapes on the capture stream first")
+        if ws is not None:
+            _attn_ws_retired.append(ws)
         ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
         _attn_ws[key] = ws
     scale = 1.0 / float(D) ** 0.5 if scale is None else float(scale)

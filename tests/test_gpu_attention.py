@@ -159,3 +159,19 @@ def test_rms_norm_matches_torch(M, N):
     xf = x.double()
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.double()
     torch.testing.assert_close(y.double(), ref, rtol=8e-3, atol=1e-3)
+
+
+def test_one_workspace_serves_changing_shapes():
+    """Small batches split positions over CTAs and use the workspace's arrival counters; calls
+    of different shapes on one stream share one buffer, interleaved, and stay exact."""
+    cases = [_case(E, 8, 2, 64, 16, [700] * E, seed=40 + E) for E in (1, 3, 2)]
+    refs = []
+    for q, kp, vp, bt, cl, mc in cases:
+        refs.append(ref_paged_decode_attention(q.float().numpy(), kp.float().numpy(), vp.float().numpy(),
+                                               bt.numpy(), cl.numpy()))
+    for _ in range(2):
+        for (q, kp, vp, bt, cl, mc), ref in zip(cases, refs):
+            o = _run(q, kp, vp, bt, cl, mc)
+            torch.cuda.synchronize()
+            check_parity(o.reshape(-1, o.shape[-1]), ref.reshape(-1, ref.shape[-1]), "interleaved shapes")
+    assert ops.device_status() == 0
