@@ -385,13 +385,16 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     key = (q.device.index, stream.cuda_stream)
     ws = _attn_ws.get(key)
     if need and (ws is None or ws.numel() < need):
-        if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("paged_decode_attention: workspace must grow outside a CUDA graph capture; "
-                               "run one eager call with the same shapes on the capture stream first")
-        if ws is not None:
-            _attn_ws_retired.append(ws)
-        ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
-        _attn_ws[key] = ws
+        with _ws_lock:
+            ws = _attn_ws.get(key)
+            if ws is None or ws.numel() < need:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError("paged_decode_attention: workspace must grow outside a CUDA graph capture; "
+                                       "run one eager call with the same shapes on the capture stream first")
+                if ws is not None:
+                    _attn_ws_retired.append(ws)
+                ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
+                _attn_ws[key] = ws
     scale = 1.0 / float(D) ** 0.5 if scale is None else float(scale)
     rc = lib.lse_paged_decode_attention(
         q.data_ptr(), E, H, D, q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), nb, bs, H_kv,
