@@ -336,6 +336,24 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
         del g
     out["int8_speedup"] = round(out["int8"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
     out["int8_lm_head_speedup"] = round(out["int8_lm_head"]["tokens_per_s"] / out["none"]["tokens_per_s"], 3)
+    q8.set_lm_head_int8(False)
+    # the same model at small batches (the decode kernel's regime): int8 vs bf16 projections
+    small = {}
+    for b in (1, 16):
+        bf = DecodeModel(LLAMA3_8B, b, ctx, dev, seed=11, quantize=False, weights=base.weights)
+        i8 = DecodeModel(LLAMA3_8B, b, ctx, dev, seed=11, quantize=False, weights=base.weights, kv=bf.kv)
+        i8.proj, i8.quantize = q8.proj, True  # the int8 modules built above
+        row = {}
+        for name, m in (("int8", i8), ("none", bf)):
+            g = capture(m.step, warm)
+            time_graph(g, 3)
+            ms = time_graph(g, steps)
+            row[name] = {"tokens_per_s": round(b / (ms / 1e3), 1), "ms_per_step": round(ms, 4)}
+            del g
+        row["int8_speedup"] = round(row["int8"]["tokens_per_s"] / row["none"]["tokens_per_s"], 3)
+        small[f"batch{b}"] = row
+        del bf, i8
+    out["small_batch"] = small
     del base, q8, q8_sdpa
     torch.cuda.empty_cache()
     return out
