@@ -124,3 +124,47 @@ def test_row_assignment():
     with pytest.raises(ValueError):
         shard_rows(10, 4, 0)
     assert np.array_equal(np.concatenate([shard_rows(12, 4, r).numpy() for r in range(4)]), np.arange(12))
+
+
+# ---- a rank that fails: the others end with an error, not a hang ----------------------
+def _failing_rank_worker(rank: int, world: int, port: int, out) -> None:
+    import datetime
+    import time
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    try:
+        q, s = _weights(1, 48, 64)
+        mod = ColumnParallelInt8Linear.from_quantized(q, s, local_factory=oracle_local)
+        if rank == world - 1:
+            out.put((rank, "left before the collective"))
+            return  # this rank fails between steps: it never joins the gather
+        t0 = time.time()
+        try:
+            mod(_x(2, 5, 64))
+            out.put((rank, "completed"))
+        except Exception as e:  # noqa: BLE001 - any backend error is the expected outcome
+            out.put((rank, f"error after {time.time() - t0:.1f} s: {type(e).__name__}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rank_leaving_before_the_gather_errors_the_others(world):
+    """Failure on the host, as on a GPU pool: one rank leaves between steps; the others' next
+    collective ends with an error within the process group's short timeout instead of hanging."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(out.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    assert results[world - 1] == "left before the collective"
+    for r in range(world - 1):
+        assert results[r].startswith("error after"), results
