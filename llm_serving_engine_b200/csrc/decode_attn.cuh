@@ -39,6 +39,7 @@ constexpr int WARPS = 4;
 constexpr int THREADS = WARPS * 32;
 constexpr int MAX_TABLE = 1024;  // block-table entries one CTA stages (chunk / block_size + 1)
 constexpr int STAGES = 3;        // cp.async iterations in flight per warp
+constexpr int MAX_SPLITS = 64;   // position splits per (sequence, KV head) the merge stages
 
 // Dynamic shared memory of one CTA: per warp STAGES x (16 K rows + 16 V rows) of D bf16.
 template <int D>
@@ -346,23 +347,50 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     if (!last) return;
     __threadfence();
     const float *all = p.part + static_cast<int64_t>(pair) * p.splits * (G * (D + 2));
+    // Every split's (max, sum) per head in one cooperative pass, then each head's weights
+    // exp2(m_s - M): the accumulator loads below are then independent of one another.
+    __shared__ float s_w[MAX_SPLITS][G];
+    __shared__ float s_ml[MAX_SPLITS][G][2];
+    __shared__ float s_L[G];
+    for (int i = threadIdx.x; i < p.splits * G; i += THREADS) {
+        const int sp = i / G, h = i % G;
+        const float *q = all + sp * (G * (D + 2)) + h * (D + 2);
+        s_ml[sp][h][0] = __ldcg(q);
+        s_ml[sp][h][1] = __ldcg(q + 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int h = threadIdx.x;
+        float M = NEG_INF;
+        for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, s_ml[sp][h][0]);
+        float L = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+            const float ms = s_ml[sp][h][0];
+            const float f = (M == NEG_INF || ms == NEG_INF) ? 0.f : exp2f(ms - M);
+            s_w[sp][h] = f;
+            L += s_ml[sp][h][1] * f;
+        }
+        s_L[h] = L;
+    }
+    __syncthreads();
 #pragma unroll
     for (int it = 0; it < ITEMS; ++it) {
         const int idx = threadIdx.x + it * THREADS;
         if (idx >= G * D) continue;
         const int h = idx / D, d = idx % D;
-        float M = NEG_INF;
-        for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(all + sp * (G * (D + 2)) + h * (D + 2)));
-        float L = 0.f, A = 0.f;
-        if (M != NEG_INF)
-            for (int sp = 0; sp < p.splits; ++sp) {
-                const float *q = all + sp * (G * (D + 2)) + h * (D + 2);
-                const float ms = __ldcg(q);
-                if (ms == NEG_INF) continue;
-                const float f = exp2f(ms - M);
-                L += __ldcg(q + 1) * f;
-                A += __ldcg(q + 2 + d) * f;
-            }
+        const float *q = all + h * (D + 2) + 2 + d;
+        float A = 0.f;
+        int sp = 0;
+        for (; sp + 4 <= p.splits; sp += 4) {  // four independent loads in flight
+            const float a0 = __ldcg(q + (sp + 0) * (G * (D + 2))), a1 = __ldcg(q + (sp + 1) * (G * (D + 2)));
+            const float a2 = __ldcg(q + (sp + 2) * (G * (D + 2))), a3 = __ldcg(q + (sp + 3) * (G * (D + 2)));
+            A = fmaf(a0, s_w[sp][h], A);
+            A = fmaf(a1, s_w[sp + 1][h], A);
+            A = fmaf(a2, s_w[sp + 2][h], A);
+            A = fmaf(a3, s_w[sp + 3][h], A);
+        }
+        for (; sp < p.splits; ++sp) A = fmaf(__ldcg(q + sp * (G * (D + 2))), s_w[sp][h], A);
+        const float L = s_L[h];
         const float out = L > 0.f ? A / L : 0.f;
         p.o[e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d] = __float2bfloat16_rn(out);
     }

@@ -822,6 +822,7 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
         return LSE_OK;
     }
     const AttnPlan pl = plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms);
+    if (pl.splits > attn::MAX_SPLITS) return LSE_ERR_UNSUPPORTED;  // a very long context at block_size < 16
     const size_t need = attn_workspace_bytes(pl, E, H, H_kv, D);
     if (need && (!workspace || workspace_bytes < need || !aligned16(workspace))) return LSE_ERR_WORKSPACE;
     attn::Params p{};
