@@ -1,12 +1,12 @@
-// Skinny int8 weight-only GEMM for decode (M <= 16 tokens), on the fragment-major packed
-// weights of pack_w.cuh.
+// Skinny int8 weight-only GEMM for decode (M <= 32 tokens; the auto policy uses it up to 16),
+// on the fragment-major packed weights of pack_w.cuh.
 //
 //   y[m, n] = s[n] * sum_k x[m, k] * w[n, k]
 //
 // Decode is bound by the weight stream (2 flop per weight byte per token).  The kernel is
 // shaped so that nothing but HBM bounds it, and so that consecutive projections overlap:
-//   * one CTA of KW warps owns R blocks of 16 output channels over all of K; warp w takes
-//     every KW-th chunk (32 columns) of each block;
+//   * one CTA of KW warps owns R blocks of 16 output channels over all of K; warp w takes a
+//     contiguous slice of each block's 32-column chunks;
 //   * every lane loads its 16 bytes of a 512-byte chunk straight into registers with one
 //     128-bit streaming load (L1 no-allocate, L2 evict-first): those bytes ARE two 16x16 A
 //     fragments of a 16x8x16 warp MMA (pack_w.cuh), so there is no shared-memory staging,
@@ -24,6 +24,8 @@
 //   * the CTA signals programmatic launch completion on entry: it holds only a small
 //     reduction buffer in shared memory, so the next kernel's CTAs become resident as soon
 //     as registers free up and start their own weight streams under this kernel's tail.
+//   * optional epilogues: the residual add (y = res + s * acc) and, for the MLP, SiLU(gate) *
+//     up on gate/up rows interleaved in 8-row blocks.
 // No workspace, no cross-CTA traffic, no spin-waits.
 #pragma once
 
