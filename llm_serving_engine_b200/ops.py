@@ -280,6 +280,8 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tenso
         x2 = x2.contiguous()
     if out is None:
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    elif out.dtype != torch.bfloat16 or out.shape != x.shape or not out.is_contiguous():
+        raise ValueError("rms_norm: out must be a contiguous bf16 tensor of x's shape")
     y2 = out.view(-1, N)
     if x2.shape[0] == 0:
         return out
