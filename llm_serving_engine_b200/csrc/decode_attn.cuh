@@ -56,7 +56,8 @@ struct Params {
     int64_t o_stride_e, o_stride_h;
     int E, H_kv, block_size, num_blocks, chunk, splits, max_ctx;
     float scale_log2;         // softmax scale * log2(e)
-    float *part;              // [E, H_kv, splits, G, D + 2] fp32 partials (splits > 1)
+    float *part;              // splits > 1: fp32 partials, [E, H_kv, splits, G, D] accumulators
+                              // then [E, H_kv, splits, G, 2] (max, sum)
     int *counters;            // [E * H_kv] arrival counters, zero between launches
 };
 
@@ -323,16 +324,18 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     }
 
     // ---- several splits: publish this partial; the last CTA of the pair merges ----
-    float *mine = p.part + (static_cast<int64_t>(pair) * p.splits + split) * (G * (D + 2));
+    const int64_t acc_region = static_cast<int64_t>(p.E) * p.H_kv * p.splits * (G * D);
+    const int64_t slot = static_cast<int64_t>(pair) * p.splits + split;
+    float *acc_mine = p.part + slot * (G * D);            // [G][D], item idx = h * D + d
+    float *ml_mine = p.part + acc_region + slot * (G * 2);  // [G][2]
 #pragma unroll
     for (int it = 0; it < ITEMS; ++it) {
         const int idx = threadIdx.x + it * THREADS;
         if (idx >= G * D) continue;
-        const int h = idx / D, d = idx % D;
-        mine[h * (D + 2) + 2 + d] = res_a[it];
-        if (d == 0) {
-            mine[h * (D + 2)] = res_m[it];
-            mine[h * (D + 2) + 1] = res_l[it];
+        acc_mine[idx] = res_a[it];
+        if (idx % D == 0) {
+            ml_mine[(idx / D) * 2] = res_m[it];
+            ml_mine[(idx / D) * 2 + 1] = res_l[it];
         }
     }
     __threadfence();
@@ -346,17 +349,16 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const float *all = p.part + static_cast<int64_t>(pair) * p.splits * (G * (D + 2));
+    const float *acc_all = p.part + static_cast<int64_t>(pair) * p.splits * (G * D);
+    const float *ml_all = p.part + acc_region + static_cast<int64_t>(pair) * p.splits * (G * 2);
     // Every split's (max, sum) per head in one cooperative pass, then each head's weights
-    // exp2(m_s - M): the accumulator loads below are then independent of one another.
+    // exp2(m_s - M).
     __shared__ float s_w[MAX_SPLITS][G];
     __shared__ float s_ml[MAX_SPLITS][G][2];
     __shared__ float s_L[G];
     for (int i = threadIdx.x; i < p.splits * G; i += THREADS) {
-        const int sp = i / G, h = i % G;
-        const float *q = all + sp * (G * (D + 2)) + h * (D + 2);
-        s_ml[sp][h][0] = __ldcg(q);
-        s_ml[sp][h][1] = __ldcg(q + 1);
+        s_ml[i / G][i % G][0] = __ldcg(ml_all + 2 * i);
+        s_ml[i / G][i % G][1] = __ldcg(ml_all + 2 * i + 1);
     }
     __syncthreads();
     if (threadIdx.x < G) {
@@ -373,26 +375,54 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
         s_L[h] = L;
     }
     __syncthreads();
+    // Accumulators: thread t owns dims 4f..4f+3 (f = t, t + THREADS, ...) of the G x D
+    // output and loads them from SB splits at once (one 16-byte load each, all in flight
+    // together), then folds them in split order (deterministic).
+    constexpr int F4 = G * D / 4;
+    constexpr int I4 = (F4 + THREADS - 1) / THREADS;
+    constexpr int SB = I4 >= 2 ? 8 : 16;
+    float4 A[I4];
 #pragma unroll
-    for (int it = 0; it < ITEMS; ++it) {
-        const int idx = threadIdx.x + it * THREADS;
-        if (idx >= G * D) continue;
-        const int h = idx / D, d = idx % D;
-        const float *q = all + h * (D + 2) + 2 + d;
-        float A = 0.f;
-        int sp = 0;
-        for (; sp + 4 <= p.splits; sp += 4) {  // four independent loads in flight
-            const float a0 = __ldcg(q + (sp + 0) * (G * (D + 2))), a1 = __ldcg(q + (sp + 1) * (G * (D + 2)));
-            const float a2 = __ldcg(q + (sp + 2) * (G * (D + 2))), a3 = __ldcg(q + (sp + 3) * (G * (D + 2)));
-            A = fmaf(a0, s_w[sp][h], A);
-            A = fmaf(a1, s_w[sp + 1][h], A);
-            A = fmaf(a2, s_w[sp + 2][h], A);
-            A = fmaf(a3, s_w[sp + 3][h], A);
+    for (int i = 0; i < I4; ++i) A[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp0 = 0; sp0 < p.splits; sp0 += SB) {
+        float4 v[I4][SB];
+#pragma unroll
+        for (int i = 0; i < I4; ++i) {
+            const int f = threadIdx.x + i * THREADS;
+#pragma unroll
+            for (int u = 0; u < SB; ++u) {
+                v[i][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (f < F4 && sp0 + u < p.splits)
+                    v[i][u] = __ldcg(reinterpret_cast<const float4 *>(acc_all + static_cast<int64_t>(sp0 + u) * (G * D)) + f);
+            }
         }
-        for (; sp < p.splits; ++sp) A = fmaf(__ldcg(q + sp * (G * (D + 2))), s_w[sp][h], A);
+#pragma unroll
+        for (int i = 0; i < I4; ++i) {
+            const int f = threadIdx.x + i * THREADS;
+            const int h = f < F4 ? (4 * f) / D : 0;
+#pragma unroll
+            for (int u = 0; u < SB; ++u) {
+                if (sp0 + u < p.splits) {
+                    const float w = s_w[sp0 + u][h];
+                    A[i].x = fmaf(v[i][u].x, w, A[i].x);
+                    A[i].y = fmaf(v[i][u].y, w, A[i].y);
+                    A[i].z = fmaf(v[i][u].z, w, A[i].z);
+                    A[i].w = fmaf(v[i][u].w, w, A[i].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < I4; ++i) {
+        const int f = threadIdx.x + i * THREADS;
+        if (f >= F4) continue;
+        const int h = (4 * f) / D, d = (4 * f) % D;
         const float L = s_L[h];
-        const float out = L > 0.f ? A / L : 0.f;
-        p.o[e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d] = __float2bfloat16_rn(out);
+        __nv_bfloat16 *op = p.o + e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d;
+        op[0] = __float2bfloat16_rn(L > 0.f ? A[i].x / L : 0.f);
+        op[1] = __float2bfloat16_rn(L > 0.f ? A[i].y / L : 0.f);
+        op[2] = __float2bfloat16_rn(L > 0.f ? A[i].z / L : 0.f);
+        op[3] = __float2bfloat16_rn(L > 0.f ? A[i].w / L : 0.f);
     }
 }
 

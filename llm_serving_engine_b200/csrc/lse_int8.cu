@@ -726,17 +726,42 @@ struct AttnPlan {
 constexpr int64_t kAttnMaxSplitPairs = 1024;
 constexpr size_t kAttnCounterBytes = kAttnMaxSplitPairs * sizeof(int);
 
-// Split the positions of a (sequence, KV head) pair only when there are too few pairs to give
-// most SMs a CTA.  A CTA pays several microseconds before its stream is full (context length
-// and block-table loads, pipeline fill) and again at the end (warp merge, partials): measured
-// on B200 at 1025 positions, 64 sequences took 48 us unsplit, 67 us in 2 splits and 75 us in 3;
-// 16 sequences (128 pairs, 0.86 CTA per SM) 19.5 us unsplit, 32 us in 5 splits.
+// Split the positions of a (sequence, KV head) pair only when there are too few pairs to fill
+// the GPU, and only into as many splits as keep every CTA of the launch resident at once
+// (two per SM: 184 registers x 128 threads each).  A CTA pays a few microseconds before its
+// stream is full (context length and block-table loads, pipeline fill) and again at the end
+// (warp merge, partials); a second wave of CTAs pays them twice.  Measured on B200 at 1025
+// positions (32 layers' pools per CUDA graph): 1 sequence 8.9 us in 5 splits of >= 256
+// positions, 8.0 us in 9 of >= 128, 8.9 us in 17; 4 sequences (32 pairs) 10.7 us in 5 splits,
+// 9.8 us in 9; 8 sequences 12.8 us in 3 splits (192 CTAs), 12.5 us in 4 (256 CTAs), 16.6 us
+// in 5 (320 CTAs, two waves); 16 sequences 19.3 us unsplit, 17.4 us in 2 splits (256 CTAs),
+// 22.9 us in 3 (384 CTAs); 32 sequences 25.6 us unsplit.
+//
+// Tuning overrides for sweeps, read once per process: LSE_ATTN_MIN_CHUNK (fewest positions
+// per split) and LSE_ATTN_TARGET_CTAS (CTAs resident at once; 0 = two per SM).
+int attn_min_chunk() {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_ATTN_MIN_CHUNK");
+        const int c = e ? std::atoi(e) : 0;
+        return c > 0 ? c : 128;
+    }();
+    return v;
+}
+int attn_target_ctas(int num_sms) {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_ATTN_TARGET_CTAS");
+        return e ? std::max(0, std::atoi(e)) : 0;
+    }();
+    return v > 0 ? v : 2 * num_sms;
+}
+
 AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_size, int num_sms) {
     const int64_t pairs = std::max<int64_t>(1, E * H_kv);
-    const int64_t cap = std::max<int64_t>(1, (max_context + 255) / 256);  // chunks of >= 256 positions
+    const int64_t min_chunk = attn_min_chunk();
+    const int64_t target = attn_target_ctas(num_sms);
+    const int64_t cap = std::max<int64_t>(1, (max_context + min_chunk - 1) / min_chunk);
     int64_t splits = 1;
-    if (2 * pairs < static_cast<int64_t>(num_sms) && pairs <= kAttnMaxSplitPairs)
-        splits = std::min<int64_t>((num_sms + pairs - 1) / pairs, cap);
+    if (2 * pairs <= target && pairs <= kAttnMaxSplitPairs) splits = std::min<int64_t>(target / pairs, cap);
     // a CTA stages at most attn::MAX_TABLE block-table entries (chunk / block_size + 1)
     const int64_t max_chunk = (attn::MAX_TABLE - 1) * block_size / 32 * 32;
     splits = std::max<int64_t>(splits, (max_context + max_chunk - 1) / max_chunk);
