@@ -344,13 +344,16 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
         i8 = DecodeModel(LLAMA3_8B, b, ctx, dev, seed=11, quantize=False, weights=base.weights, kv=bf.kv)
         i8.proj, i8.quantize = q8.proj, True  # the int8 modules built above
         row = {}
-        for name, m in (("int8", i8), ("none", bf)):
+        for name, m in (("int8", i8), ("int8_lm_head", i8), ("none", bf)):
+            i8.set_lm_head_int8(name == "int8_lm_head")
             g = capture(m.step, warm)
             time_graph(g, 3)
             ms = time_graph(g, steps)
             row[name] = {"tokens_per_s": round(b / (ms / 1e3), 1), "ms_per_step": round(ms, 4)}
             del g
+        i8.set_lm_head_int8(False)
         row["int8_speedup"] = round(row["int8"]["tokens_per_s"] / row["none"]["tokens_per_s"], 3)
+        row["int8_lm_head_speedup"] = round(row["int8_lm_head"]["tokens_per_s"] / row["none"]["tokens_per_s"], 3)
         small[f"batch{b}"] = row
         del bf, i8
     out["small_batch"] = small
