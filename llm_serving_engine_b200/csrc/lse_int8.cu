@@ -727,18 +727,23 @@ constexpr int64_t kAttnMaxSplitPairs = 1024;
 constexpr size_t kAttnCounterBytes = kAttnMaxSplitPairs * sizeof(int);
 
 // Split the positions of a (sequence, KV head) pair only when there are too few pairs to fill
-// the GPU, and only into as many splits as keep every CTA of the launch resident at once
-// (two per SM: 184 registers x 128 threads each).  A CTA pays a few microseconds before its
-// stream is full (context length and block-table loads, pipeline fill) and again at the end
-// (warp merge, partials); a second wave of CTAs pays them twice.  Measured on B200 at 1025
-// positions (32 layers' pools per CUDA graph): 1 sequence 8.9 us in 5 splits of >= 256
-// positions, 8.0 us in 9 of >= 128, 8.9 us in 17; 4 sequences (32 pairs) 10.7 us in 5 splits,
-// 9.8 us in 9; 8 sequences 12.8 us in 3 splits (192 CTAs), 12.5 us in 4 (256 CTAs), 16.6 us
-// in 5 (320 CTAs, two waves); 16 sequences 19.3 us unsplit, 17.4 us in 2 splits (256 CTAs),
-// 22.9 us in 3 (384 CTAs); 32 sequences 25.6 us unsplit.
+// the GPU, and only into as many splits as leave the launch at about one and a half CTAs per
+// SM, with at least 128 positions per split.  A CTA pays a few microseconds before its stream
+// is full (context length and block-table loads, pipeline fill) and again at the end (warp
+// merge, partials), so small batches want splits; but residency is two CTAs per SM (184
+// registers x 128 threads, 104 KB of shared memory), a second wave pays the fixed costs twice,
+// and in a decode step the next projection's CTAs start their weight streams under this
+// kernel (programmatic dependent launch) only where an SM has room left.  Measured on B200 at
+// 1025 positions, the kernel alone (32 layers' pools per CUDA graph): 1 sequence 8.9 us in 5
+// splits of >= 256 positions, 8.0 us in 9 of >= 128, 8.9 us in 17; 4 sequences 10.7 us in 5
+// splits, 10.3 us in 7, 9.8 us in 9; 8 sequences 12.8 us in 3 splits, 12.5 us in 4, 16.6 us in
+// 5 (two waves); 16 sequences 19.3 us unsplit, 17.4 us in 2 splits, 22.9 us in 3.  In the
+// Llama-3-8B decode step (llama_decode.py, 1024-token context, CUDA graph): 8 sequences
+// 2.738 ms/step in 3 splits, 2.760 in 4, 2.774 in 2; 16 sequences 3.384 ms unsplit, 3.460 in 2
+// splits.
 //
 // Tuning overrides for sweeps, read once per process: LSE_ATTN_MIN_CHUNK (fewest positions
-// per split) and LSE_ATTN_TARGET_CTAS (CTAs resident at once; 0 = two per SM).
+// per split) and LSE_ATTN_TARGET_CTAS (CTAs a split launch may reach; 0 = 1.5 per SM).
 int attn_min_chunk() {
     static const int v = [] {
         const char *e = std::getenv("LSE_ATTN_MIN_CHUNK");
@@ -752,7 +757,7 @@ int attn_target_ctas(int num_sms) {
         const char *e = std::getenv("LSE_ATTN_TARGET_CTAS");
         return e ? std::max(0, std::atoi(e)) : 0;
     }();
-    return v > 0 ? v : 2 * num_sms;
+    return v > 0 ? v : 3 * num_sms / 2;
 }
 
 AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_size, int num_sms) {
