@@ -363,15 +363,17 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
 
 
 def fused_gate_up(weights, dev, warm, ops, hbm_peak):
-    """The decode MLP's first half, silu(x Wg^T) * (x Wu^T), for M in 1, 4, 16 over every
-    layer's gate_up weight: one fused kernel (lse_int8_gate_up_silu_packed, the gate and up
-    rows interleaved in 16-row blocks) vs the int8 gate_up projection followed by torch's
-    SiLU * mul.  The uniform random weights stand for an interleaved [gate; up] as they are."""
+    """The MLP's first half, silu(x Wg^T) * (x Wu^T), over every layer's gate_up weight: one
+    fused launch (lse_int8_gate_up_silu_packed[_ws]: the decode kernel for M <= 16, the
+    tcgen05 kernel with SiLU * mul in its epilogue above; gate and up rows interleaved in
+    8-row blocks) vs the int8 gate_up projection followed by torch's SiLU * mul, at decode
+    (1, 4, 16, 64) and prefill (512, 2048) token counts.  The uniform random weights stand
+    for an interleaved [gate; up] as they are."""
     K, N2 = LLAMA3_8B_SHAPES["gate_up"]
     inter = N2 // 2
     gx = torch.Generator(device=dev).manual_seed(17)
     out = {"workload": f"Llama-3-8B gate_up K={K}, I={inter}, {len(weights)} layers' weights per graph", "points": []}
-    for M in (1, 4, 16):
+    for M in (1, 4, 16, 64, 512, 2048):
         x = torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16)
         h = torch.empty(M, inter, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(M, N2, device=dev, dtype=torch.bfloat16)
@@ -396,6 +398,7 @@ def fused_gate_up(weights, dev, warm, ops, hbm_peak):
         b = linear_bytes(M, K, N2) - M * N2 * 2 + M * inter * 2
         pt["fused_GBps"] = round(b / pt["fused_us"] / 1e3, 1)
         pt["fused_frac_of_hbm"] = round(b / pt["fused_us"] / 1e3 / hbm_peak, 4)
+        pt["fused_TFLOPs"] = round(2 * M * K * N2 / pt["fused_us"] / 1e6, 1)
         pt["speedup"] = round(pt["unfused_us"] / pt["fused_us"], 3)
         out["points"].append(pt)
     return out

@@ -148,6 +148,18 @@ int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ld
                                  void *y, int64_t ldy, void *stream);
 
 /*
+ * The same for any M, with a workspace of at least lse_int8_linear_workspace(M, K, 2 * I)
+ * bytes (zero-initialised once, as for lse_int8_linear_packed; unused for M <= 16): M <= 16
+ * runs the decode kernel above, larger M the tcgen05 kernel with SiLU * mul in its epilogue,
+ * so that the [M, 2I] gate/up output never reaches memory.  Same weights, scales, y and
+ * error codes as lse_int8_gate_up_silu_packed, plus LSE_ERR_WORKSPACE.
+ */
+int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                    const int8_t *w_packed, const float *scale, int64_t I,
+                                    void *y, int64_t ldy, void *workspace, size_t workspace_bytes,
+                                    void *stream);
+
+/*
  * Paged decode attention, one query token per sequence (the decode-step call of the
  * reference's paged_attention_forward, src/llm_serving_engine/kernels/flash_attention.py:
  * 287-332, with q_len = 1 and query_offset = context_len - 1):

@@ -38,7 +38,7 @@ DT_F32 = 2
 WS_COUNTER_BYTES = 65536
 NOALLOC_SCRATCH_BYTES = 12582912  # fixed scratch of lse_int8_linear_packed_noalloc, per device
 NOALLOC_MAX_M = 64
-GATE_UP_SILU_MAX_M = 16  # lse_int8_gate_up_silu_packed's token range
+GATE_UP_SILU_MAX_M = 16  # lse_int8_gate_up_silu_packed's token range (the decode kernel's)
 ABI_VERSION = 1
 
 # Every symbol include/lse_int8.h declares, with its ctypes signature.
@@ -53,6 +53,7 @@ SIGNATURES = {
                                         _I32),
     "lse_int8_linear_packed_noalloc": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "lse_int8_gate_up_silu_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
+    "lse_int8_gate_up_silu_packed_ws": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _P], _I32),
     "lse_rms_norm": ([_P, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P], _I32),
     "lse_rope_kv_write": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P, _P, _I64, _P], _I32),
     "lse_paged_decode_attention_workspace": ([_I64, _I64, _I64, _I64, _I64, _I64], _SZ),

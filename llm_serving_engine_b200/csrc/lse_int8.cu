@@ -54,9 +54,9 @@ DeviceState g_dev[kMaxDevices];
 std::once_flag g_encode_once;
 EncodeTiledFn g_encode = nullptr;
 
-template <int NT>
+template <int NT, bool SILU = false>
 cudaError_t set_tc_attrs() {
-    return cudaFuncSetAttribute(tc::tc_gemm_i8_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(tc::tc_gemm_i8_kernel<NT, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 tc::Cfg<NT>::SMEM_BYTES);
 }
 
@@ -72,6 +72,8 @@ int init_device(int device) {
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         if (e == cudaSuccess) e = set_tc_attrs<64>();
         if (e == cudaSuccess) e = set_tc_attrs<128>();
+        if (e == cudaSuccess) e = set_tc_attrs<64, true>();
+        if (e == cudaSuccess) e = set_tc_attrs<128, true>();
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
         std::call_once(g_encode_once, [] {
             void *fn = nullptr;
@@ -184,7 +186,7 @@ int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
     return LSE_OK;
 }
 
-template <int NT>
+template <int NT, bool SILU = false>
 int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
               const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
               cudaStream_t st) {
@@ -222,7 +224,7 @@ int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     launch_config(cfg, attr, dim3(pl.grid), dim3(tc::NUM_THREADS), tc::Cfg<NT>::SMEM_BYTES, st);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_i8_kernel<NT>, tw, tx, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_i8_kernel<NT, SILU>, tw, tx, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "tc_gemm_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -707,6 +709,42 @@ extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K,
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// lse_int8_gate_up_silu_packed_ws: the same for any M, with a workspace: M <= 16 on the
+// decode kernel (workspace unused), larger M on the tensor-core kernel with SiLU * mul in its
+// epilogue (tc_gemm_i8.cuh, SILU = true).
+// ---------------------------------------------------------------------------------------
+extern "C" int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                               const int8_t *w_packed, const float *scale, int64_t I, void *y,
+                                               int64_t ldy, void *workspace, size_t workspace_bytes, void *stream) {
+    if (M >= 0 && M <= 16) return lse_int8_gate_up_silu_packed(x, M, K, ldx, w_packed, scale, I, y, ldy, stream);
+    if (M < 0 || I < 0 || K < 0) return LSE_ERR_INVALID_ARG;
+    if (I == 0) return LSE_OK;
+    if (!x || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
+    if (ldx < K || ldy < I) return LSE_ERR_INVALID_ARG;
+    if (I % 8) return LSE_ERR_UNSUPPORTED;
+    if (M > INT32_MAX || 2 * I > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (K == 0) {  // silu(0) * 0
+        const cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(I) * 2,
+                                                static_cast<size_t>(M), st);
+        if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
+        return LSE_OK;
+    }
+    const int64_t N = 2 * I;
+    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
+    if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
+        return LSE_ERR_WORKSPACE;
+    if (pl.nt == 64)
+        return launch_tc<64, true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
+    return launch_tc<128, true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -16,6 +16,11 @@
 //   * The fp32 accumulator lives in TMEM (double-buffered when it fits) and four epilogue
 //     warps read it with tcgen05.ld, apply s[n] (and add the optional residual) and store
 //     bf16 y.
+//   * SILU = true is the MLP's gate_up projection with SiLU * mul fused: the weight rows
+//     interleave 8-row blocks of gate and up (row block b = gate rows 8b..8b+7, then the
+//     matching up rows, `scale` interleaved the same way), so a 16-row block's gate row sits
+//     8 TMEM lanes (8 lanes of the same warp) from its up row; y is [M, N / 2] with
+//     y[m, 8b + r] = silu(s_g * gate) * (s_u * up) (fp32, one bf16 rounding).
 //
 // Warp roles (512 threads): warp 0 TMA producer, warp 1 TMEM allocator + single-thread MMA
 // issuer, warp 2 L2 prefetcher for the weight stream, warps 4-7 epilogue (TMEM lane quarter = warp % 4), warps 8-15 converters (two
@@ -206,7 +211,7 @@ __device__ __forceinline__ uint64_t policy_w_for(const Params &p) {
 }
 
 // ---- the kernel -------------------------------------------------------------------------
-template <int NT>
+template <int NT, bool SILU = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_x, const Params p) {
@@ -526,7 +531,17 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
 #pragma unroll
                     for (int j = 0; j < CH; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
                 }
-                if (whole) {
+                if (whole && SILU) {
+                    // gate lanes ((lane & 8) == 0) take the up value of their row from lane + 8
+                    const int col = (n >> 4) * 8 + (n & 7);
+#pragma unroll
+                    for (int j = 0; j < CH; ++j) {
+                        const float a = __uint_as_float(v[j]) * sc;
+                        const float u = __shfl_xor_sync(0xffffffffu, a, 8);
+                        if (!(lane & 8) && n_ok && c0 + j < mval)
+                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + col] = __float2bfloat16_rn(a / (1.f + expf(-a)) * u);
+                    }
+                } else if (whole) {
 #pragma unroll
                     for (int j = 0; j < CH; ++j) {
                         if (n_ok && c0 + j < mval) {
@@ -630,17 +645,33 @@ tc_gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_w,
             for (int i = 0; i < IPT; ++i) {
                 const int item = threadIdx.x + i * NUM_THREADS;
                 const int j = item / QUADS, rq = (item % QUADS) * 4;
-                if (j >= mval) continue;
                 const int n = n_tile * BN + rq;
-                __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
-                const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+                if constexpr (SILU) {
+                    // quad rq + 8 (the up rows of gate quad rq) is item + 2: lane + 2 of this warp
+                    static_assert(QUADS == 32 && NUM_THREADS % 32 == 0, "quad exchange stays in the warp");
+                    const float u4[4] = {__shfl_xor_sync(0xffffffffu, acc[i].x, 2), __shfl_xor_sync(0xffffffffu, acc[i].y, 2),
+                                         __shfl_xor_sync(0xffffffffu, acc[i].z, 2), __shfl_xor_sync(0xffffffffu, acc[i].w, 2)};
+                    if (j >= mval || (rq & 8)) continue;
+                    const float g4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+                    __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (n + e < p.N) {
-                        float o = a4[e] * __ldg(p.scale + n + e);
-                        if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
-                        yr[e] = __float2bfloat16_rn(o);
-                    }
+                    for (int e = 0; e < 4; ++e)
+                        if (n + e < p.N) {
+                            const float g = g4[e] * __ldg(p.scale + n + e), u = u4[e] * __ldg(p.scale + n + 8 + e);
+                            yr[e] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
+                        }
+                } else {
+                    if (j >= mval) continue;
+                    __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+                    const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (n + e < p.N) {
+                            float o = a4[e] * __ldg(p.scale + n + e);
+                            if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
+                            yr[e] = __float2bfloat16_rn(o);
+                        }
+                }
             }
         }
     }

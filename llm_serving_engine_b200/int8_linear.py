@@ -220,7 +220,7 @@ class Int8LlamaMLP(nn.Module):
         I = self.intermediate_size
         lead = x.shape[:-1]
         x2 = _to_bf16(x).reshape(-1, x.shape[-1])
-        if x2.shape[0] <= ops.GATE_UP_SILU_MAX_M and self._silu():
+        if self._silu():
             h = ops.int8_gate_up_silu_packed(x2, self.gate_up.weight_packed, self.gate_up.scale, I,
                                              self.gate_up.in_features)
         else:

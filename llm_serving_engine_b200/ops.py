@@ -215,9 +215,10 @@ def interleave_gate_up_rows(intermediate: int, device=None) -> torch.Tensor:
 
 def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: torch.Tensor, intermediate: int,
                              K: int, out: torch.Tensor | None = None) -> torch.Tensor:
-    """`silu(x @ (Wg * sg).T) * (x @ (Wu * su).T)` for M <= 16 tokens in one kernel.  `w_packed`
-    is the packed layout of the gate/up rows in `interleave_gate_up_rows` order, `scale` the
-    scales in the same order; returns bf16 [..., intermediate]."""
+    """`silu(x @ (Wg * sg).T) * (x @ (Wu * su).T)` in one kernel: the decode kernel for up to
+    GATE_UP_SILU_MAX_M tokens, the tensor-core kernel with SiLU * mul in its epilogue above.
+    `w_packed` is the packed layout of the gate/up rows in `interleave_gate_up_rows` order,
+    `scale` the scales in the same order; returns bf16 [..., intermediate]."""
     _check_x(x, K, w_packed, scale)
     I = intermediate
     if w_packed.dtype != torch.int8 or w_packed.numel() != packed_weight_bytes(2 * I, K) or not w_packed.is_contiguous():
@@ -229,8 +230,6 @@ def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: tor
     if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
         x2 = x2.contiguous()
     M = x2.shape[0]
-    if M > GATE_UP_SILU_MAX_M:
-        raise ValueError(f"int8_gate_up_silu_packed: M={M} > {GATE_UP_SILU_MAX_M}")
     if out is None:
         out = torch.empty((*lead, I), dtype=torch.bfloat16, device=x.device)
     elif out.dtype != torch.bfloat16 or out.shape != (*lead, I) or not out.is_contiguous():
@@ -239,9 +238,17 @@ def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: tor
         return out
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
-    rc = _lib.load().lse_int8_gate_up_silu_packed(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
-                                                  scale.data_ptr(), I, out.data_ptr(), I, stream.cuda_stream)
-    _lib.check(rc, "lse_int8_gate_up_silu_packed")
+    lib = _lib.load()
+    if M <= GATE_UP_SILU_MAX_M:
+        rc = lib.lse_int8_gate_up_silu_packed(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
+                                              scale.data_ptr(), I, out.data_ptr(), I, stream.cuda_stream)
+        _lib.check(rc, "lse_int8_gate_up_silu_packed")
+        return out
+    ws = workspace_for(x.device, stream)
+    rc = lib.lse_int8_gate_up_silu_packed_ws(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
+                                             scale.data_ptr(), I, out.data_ptr(), I, ws.data_ptr(), ws.numel(),
+                                             stream.cuda_stream)
+    _lib.check(rc, "lse_int8_gate_up_silu_packed_ws")
     return out
 
 

@@ -301,10 +301,62 @@ def test_gate_up_silu_fused_limits():
     assert torch.all(y[:4] == 0)
 
 
+# ---- the same fused on the tensor-core path (M > 16, SiLU * mul in the tcgen05 epilogue) ----
+@pytest.mark.parametrize("M,K,I", [(17, 256, 512), (40, 512, 200), (64, 4096, 14336), (65, 272, 1032),
+                                   (200, 1024, 1024), (512, 4096, 14336), (2048, 512, 2048)])
+def test_gate_up_silu_fused_tc_parity(M, K, I):
+    """Whole tiles (M = 2048: 296 data-parallel tiles), stream-K tiles finished by the last
+    arriving CTA (M = 64: every tile), ragged rows (I = 200, 1032) and ragged tokens."""
+    g = torch.Generator().manual_seed(M + K + I)
+    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16)
+    qg = torch.randint(-127, 128, (I, K), generator=g, dtype=torch.int8)
+    qu = torch.randint(-127, 128, (I, K), generator=g, dtype=torch.int8)
+    sg = torch.empty(I).uniform_(1e-4, 5e-4, generator=g)
+    su = torch.empty(I).uniform_(1e-4, 5e-4, generator=g)
+    perm = ops.interleave_gate_up_rows(I)
+    q = torch.cat([qg, qu]).index_select(0, perm)
+    s = torch.cat([sg, su]).index_select(0, perm)
+    packed = ops.pack_weight(q.cuda())
+    xd = x.cuda()
+    y = ops.int8_gate_up_silu_packed(xd, packed, s.cuda(), I, K)
+    y2 = ops.int8_gate_up_silu_packed(xd, packed, s.cuda(), I, K)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)  # fixed reduction order
+    rows = np.arange(M) if M <= 256 else np.unique(np.random.default_rng(1).choice(M, 256, replace=False))
+    cols = np.arange(I) if I <= 2048 else np.unique(np.random.default_rng(0).choice(I, 2048, replace=False))
+    ref = _silu_mul_ref(x.float().numpy()[rows], qg.numpy()[cols], sg.numpy()[cols], qu.numpy()[cols], su.numpy()[cols])
+    got = y[torch.as_tensor(rows, device="cuda")][:, torch.as_tensor(cols, device="cuda")]
+    check_parity(got, ref, f"gate_up silu (tcgen05) M={M} K={K} I={I}")
+    # the unfused path on the same weights: projection, then SiLU * mul of the paired rows
+    gu = ops.int8_linear_packed(xd, packed, s.cuda(), 2 * I, K).view(M, I // 8, 2, 8).float()
+    unf = (torch.nn.functional.silu(gu[:, :, 0]) * gu[:, :, 1]).reshape(M, I)
+    assert (y.float() - unf).abs().max().item() <= 2e-2 * unf.abs().max().item()
+    assert ops.device_status() == 0
+
+
+def test_gate_up_silu_ws_limits():
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    x = torch.zeros(40, 64, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(ops.packed_weight_bytes(64, 64), dtype=torch.int8, device="cuda")
+    s = torch.ones(64, device="cuda")
+    y = torch.empty(40, 32, dtype=torch.bfloat16, device="cuda")
+    ws = ops.workspace_for(x.device)
+    assert lib.lse_int8_gate_up_silu_packed_ws(x.data_ptr(), 40, 64, 64, w.data_ptr(), s.data_ptr(), 32, y.data_ptr(),
+                                               32, None, 0, st) == _lib.LSE_ERR_WORKSPACE
+    assert lib.lse_int8_gate_up_silu_packed_ws(x.data_ptr(), 40, 64, 64, w.data_ptr(), s.data_ptr(), 20, y.data_ptr(),
+                                               32, ws.data_ptr(), ws.numel(), st) == _lib.LSE_ERR_UNSUPPORTED  # I % 8
+    y.fill_(1.0)
+    assert lib.lse_int8_gate_up_silu_packed_ws(x.data_ptr(), 40, 0, 64, w.data_ptr(), s.data_ptr(), 32, y.data_ptr(),
+                                               32, ws.data_ptr(), ws.numel(), st) == _lib.LSE_OK
+    torch.cuda.synchronize()
+    assert torch.all(y == 0)  # K == 0: silu(0) * 0
+
+
 @pytest.mark.parametrize("M", [3, 16, 40])
 def test_mlp_module_fused_and_unfused_paths(M):
-    """Int8LlamaMLP takes the fused kernel for M <= 16 and the tensor-core path above; both
-    against the fp64 MLP oracle."""
+    """Int8LlamaMLP runs gate_up + SiLU * mul fused for every M (the decode kernel up to 16
+    tokens, the tensor-core kernel above), against the fp64 MLP oracle."""
     from llm_serving_engine_b200.int8_linear import Int8LlamaMLP
     from oracle.ref_linear import ref_mlp
     H, I = 512, 1024
