@@ -142,6 +142,14 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // 16/32-token tiles).
 int token_tile(int64_t M) { return M <= 64 ? 64 : 128; }
 
+int tc_split_align() {
+    static const int v = [] {
+        const char *e = std::getenv("LSE_TC_SPLIT_ALIGN");
+        return e ? (e[0] == '1' ? 1 : 0) : -1;
+    }();
+    return v;
+}
+
 // Tensor-core kernel schedule: full waves data-parallel, the last one-to-two waves stream-K.
 struct TcPlan {
     int nt, m_tiles, n_tiles, tiles, kb, dp_tiles, grid;
@@ -159,6 +167,26 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
     if (t.tiles % G == 0) t.dp_tiles = t.tiles;
     else if (t.tiles < G) t.dp_tiles = 0;
     else t.dp_tiles = (t.tiles / G - 1) * G;
+    // At most half a wave of tiles (decode shapes): split every tile's K range over the same
+    // number s of CTAs (grid tiles * s, s = num_sms / tiles), so that each CTA works on one
+    // tile and each tile's last arriver sums s partials.  Spreading the units evenly over all
+    // SMs instead lets segments straddle tiles: some CTAs then publish two partials and sum
+    // two tiles, one after the other, and they set the launch's tail (a globaltimer trace of
+    // O at M = 64: 7.8 us from the last MMA issue to the last reduction, 6.4 us aligned).  The
+    // aligned grid leaves SMs idle, so it is taken only while it costs at most two more
+    // 128-K stages per CTA.  Measured (24 launches per CUDA graph, even -> aligned): Llama-3-8B
+    // at M = 64 O 15.45 -> 13.77 us (8 stages per CTA instead of 7), QKV 16.62 -> 15.62 (11
+    // either way), down 24.90 -> 24.83 (28 instead of 25); at M = 32 O 14.03 -> 12.68, QKV
+    // 15.30 -> 14.61, down 23.51 -> 23.76; Llama-3-70B at M = 32 O 24.69 -> 25.97 (32 instead
+    // of 28), down 61.36 -> 68.55 (112 instead of 97).
+    // LSE_TC_SPLIT_ALIGN=0 / 1 forces the even spread / the aligned grid (tuning runs).
+    if (t.tiles <= G / 2) {
+        const int s = G / t.tiles;
+        const long long even = (static_cast<long long>(t.tiles) * t.kb + G - 1) / G;
+        const long long aligned = (t.kb + s - 1) / s;
+        const int force = tc_split_align();
+        if (force == 1 || (force < 0 && aligned <= even + 2)) G = t.tiles * s;
+    }
     t.sk_units = static_cast<long long>(t.tiles - t.dp_tiles) * t.kb;
     if (t.dp_tiles == 0) G = static_cast<int>(std::min<long long>(G, t.sk_units));
     t.grid = G;
