@@ -133,6 +133,25 @@ def test_attention_rope_norm_host_validation():
     assert lib.lse_rms_norm(P, 4, 64, 64, P, -1.0, P, 64, None) == _lib.LSE_ERR_INVALID_ARG
 
 
+def test_gate_up_silu_host_validation():
+    """Both fused gate_up + SiLU*mul entries refuse bad arguments on the host (no GPU here)."""
+    lib = _lib.load()
+    P = 256
+    for M in (4, 40):  # the decode-kernel entry's range, and the tensor-core range of the _ws entry
+        ws = lib.lse_int8_gate_up_silu_packed_ws
+        assert ws(P, M, 64, 64, P, P, 20, P, 32, P, 1 << 26, None) == _lib.LSE_ERR_UNSUPPORTED  # I % 8
+        assert ws(P, M, 64, 64, P, P, 32, P, 16, P, 1 << 26, None) == _lib.LSE_ERR_INVALID_ARG  # ldy < I
+        assert ws(P, M, 64, 32, P, P, 32, P, 32, P, 1 << 26, None) == _lib.LSE_ERR_INVALID_ARG  # ldx < K
+        assert ws(P + 8, M, 64, 64, P, P, 32, P, 32, P, 1 << 26, None) == _lib.LSE_ERR_ALIGNMENT
+        assert ws(P, M, 64, 64, P, P, 32, P + 1, 32, P, 1 << 26, None) == _lib.LSE_ERR_ALIGNMENT
+        assert ws(None, M, 64, 64, P, P, 32, P, 32, P, 1 << 26, None) == _lib.LSE_ERR_INVALID_ARG
+        assert ws(P, M, 64, 64, P, P, 0, P, 32, P, 1 << 26, None) == _lib.LSE_OK  # I == 0: nothing to do
+    assert lib.lse_int8_gate_up_silu_packed_ws(P, -1, 64, 64, P, P, 32, P, 32, P, 1 << 26, None) == \
+        _lib.LSE_ERR_INVALID_ARG
+    # the decode-kernel entry alone stops at 16 tokens
+    assert lib.lse_int8_gate_up_silu_packed(P, 17, 64, 64, P, P, 32, P, 32, None) == _lib.LSE_ERR_UNSUPPORTED
+
+
 def test_python_ops_refuse_cpu_tensors():
     """No CPU fallback: the torch-facing ops raise on CPU tensors."""
     import torch
