@@ -10,9 +10,12 @@ a single-GPU call of N/g rows.
 
 * `ColumnParallelInt8Linear`: one projection, shard-local kernel, optional all-gather.
 * `TensorParallelInt8MLP`: `down(silu(gate(x)) * up(x))` with both projections N-split.
-  Rank r holds the gate rows and the up rows of intermediate block r (interleaved), so
-  SiLU * mul stays local; the intermediate block is all-gathered once (down needs all of
-  its K) and down's output block is gathered at the end.
+  Rank r holds the gate rows and the up rows of intermediate block r, so SiLU * mul stays
+  local; the intermediate block is all-gathered once (down needs all of its K) and down's
+  output block is gathered at the end.  With the default (GPU) local linear and SiLU, the
+  rank's gate and up rows are stored interleaved in 8-row blocks and gate_up + SiLU * mul is
+  one fused launch (`ops.int8_gate_up_silu_packed`); otherwise the rank's gate block
+  precedes its up block and SiLU * mul runs after the projection.
 
 The per-rank compute is `local_factory(q_rows, s_rows)`: by default an `Int8Linear` on this
 rank's GPU (the sm_100a kernels; there is no CPU path).  Tests substitute a factory to run
@@ -28,12 +31,13 @@ import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import ops
 from .int8_linear import Int8Linear
 
 LocalLinear = Callable[[torch.Tensor], torch.Tensor]
 LocalFactory = Callable[[torch.Tensor, torch.Tensor], LocalLinear]
 
-__all__ = ["ColumnParallelInt8Linear", "TensorParallelInt8MLP", "shard_rows", "interleaved_rows",
+__all__ = ["ColumnParallelInt8Linear", "TensorParallelInt8MLP", "shard_rows", "interleaved_rows", "fused_rows",
            "gather_columns"]
 
 
@@ -62,6 +66,21 @@ def interleaved_rows(intermediate: int, world: int, rank: int) -> torch.Tensor:
     columns land on the same rank."""
     blk = shard_rows(intermediate, world, rank)
     return torch.cat([blk, blk + intermediate])
+
+
+def fused_rows(intermediate: int, world: int, rank: int) -> torch.Tensor:
+    """The same rows as `interleaved_rows`, in the order the fused gate_up + SiLU * mul kernel
+    reads: 8 gate rows of the rank's block, then the matching 8 up rows, and so on."""
+    blk = shard_rows(intermediate, world, rank)
+    if blk.numel() % 8:
+        raise ValueError(f"fused gate/up rows: {blk.numel()} intermediate rows per rank is not a multiple of 8")
+    b = blk.view(-1, 8)
+    return torch.stack([b, b + intermediate], dim=1).reshape(-1)
+
+
+def _is_silu(act) -> bool:
+    # torch's SiLU, or transformers' SiLUActivation (ACT2FN["silu"])
+    return act is F.silu or type(act).__name__ in ("SiLU", "SiLUActivation")
 
 
 def gather_columns(y: torch.Tensor, group=None) -> torch.Tensor:
@@ -123,13 +142,15 @@ class TensorParallelInt8MLP(nn.Module):
     """`down(act(gate(x)) * up(x))` with gate_up and down split over output rows."""
 
     def __init__(self, gate_up: ColumnParallelInt8Linear, down: ColumnParallelInt8Linear, intermediate: int,
-                 group=None, act=F.silu):
+                 group=None, act=F.silu, fused: bool = False):
         super().__init__()
         self.gate_up = gate_up
         self.down_proj = down
         self.intermediate_size = intermediate
         self.group = group
         self.act = act
+        # fused: gate_up.local is an Int8Linear over `fused_rows` (8-row interleave)
+        self.fused = fused
 
     @classmethod
     def from_quantized(cls, q_gate: torch.Tensor, s_gate: torch.Tensor, q_up: torch.Tensor, s_up: torch.Tensor,
@@ -141,16 +162,26 @@ class TensorParallelInt8MLP(nn.Module):
             raise ValueError("TensorParallelInt8MLP: gate/up must be [I, H] and down [H, I]")
         q_gu = torch.cat([q_gate, q_up], dim=0)
         s_gu = torch.cat([s_gate, s_up], dim=0)
-        gate_up = ColumnParallelInt8Linear.from_quantized(
-            q_gu, s_gu, group, gather_output=False, rows=interleaved_rows(intermediate, world, rank),
-            local_factory=local_factory)
+        if intermediate % world:
+            raise ValueError(f"TensorParallelInt8MLP: intermediate size {intermediate} is not a multiple of {world}")
+        fused = local_factory is _default_local and _is_silu(act) and (intermediate // world) % 8 == 0
+        rows = fused_rows(intermediate, world, rank) if fused else interleaved_rows(intermediate, world, rank)
+        gate_up = ColumnParallelInt8Linear.from_quantized(q_gu, s_gu, group, gather_output=False, rows=rows,
+                                                          local_factory=local_factory)
         down = ColumnParallelInt8Linear.from_quantized(q_down, s_down, group, gather_output=True,
                                                        local_factory=local_factory)
-        return cls(gate_up, down, intermediate, group, act)
+        return cls(gate_up, down, intermediate, group, act, fused=fused)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         world, _ = _world(self.group)
-        gu = self.gate_up(x)  # [..., 2 * I / world]: this rank's gate block, then its up block
-        gate, up = gu.split(self.intermediate_size // world, dim=-1)
-        h = gather_columns(self.act(gate) * up, self.group)  # [..., I]
-        return self.down_proj(h)
+        if self.fused:
+            lin = self.gate_up.local
+            h_local = ops.int8_gate_up_silu_packed(x.to(torch.bfloat16), lin.weight_packed, lin.scale,
+                                                   self.intermediate_size // world, lin.in_features)
+        else:
+            gu = self.gate_up(x)  # [..., 2 * I / world]: this rank's gate block, then its up block
+            gate, up = gu.split(self.intermediate_size // world, dim=-1)
+            h_local = self.act(gate) * up
+        h = gather_columns(h_local, self.group)  # [..., I]
+        y = self.down_proj(h)
+        return y.to(x.dtype) if self.fused and y.dtype != x.dtype else y

@@ -353,6 +353,33 @@ def test_gate_up_silu_ws_limits():
     assert torch.all(y == 0)  # K == 0: silu(0) * 0
 
 
+@pytest.mark.parametrize("M", [4, 40])
+def test_tensor_parallel_mlp_fused_path_one_rank(M):
+    """TensorParallelInt8MLP without a process group (one rank): gate_up + SiLU * mul fused on
+    the rank's 8-row interleaved rows, against the fp64 MLP oracle and against the unfused
+    projections on the same weights (normwise: the two round the intermediate differently)."""
+    import torch.nn.functional as F
+    from llm_serving_engine_b200.int8_linear import Int8Linear
+    from llm_serving_engine_b200.parallel import TensorParallelInt8MLP
+    from oracle.ref_linear import ref_mlp
+    H, I = 512, 1024
+    g = torch.Generator().manual_seed(M)
+    wg, wu, wd = (torch.randn(*shape, generator=g) * 0.02 for shape in [(I, H), (I, H), (H, I)])
+    qs = [ops.quantize_per_channel(t.cuda()) for t in (wg, wu, wd)]
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16).cuda()
+    mlp = TensorParallelInt8MLP.from_quantized(qs[0][0], qs[0][1], qs[1][0], qs[1][1], qs[2][0], qs[2][1])
+    assert mlp.fused
+    y = mlp(x).float().cpu().numpy()
+    gu = Int8Linear.from_quantized(torch.cat([qs[0][0], qs[1][0]]), torch.cat([qs[0][1], qs[1][1]]))(x)
+    unfused = Int8Linear.from_quantized(*qs[2])(F.silu(gu[:, :I]) * gu[:, I:]).float().cpu().numpy()
+    q_np = [(q.cpu().numpy(), s.cpu().numpy()) for q, s in qs]
+    ref = ref_mlp(x.float().cpu().numpy(), *q_np[0], *q_np[1], *q_np[2])
+    # the bf16 rounding of the intermediate between the two projections adds ~1e-2
+    assert np.max(np.abs(y - ref)) / np.max(np.abs(ref)) < 2e-2
+    assert np.max(np.abs(y - unfused)) / np.max(np.abs(unfused)) < 1e-2
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("M", [3, 16, 40])
 def test_mlp_module_fused_and_unfused_paths(M):
     """Int8LlamaMLP runs gate_up + SiLU * mul fused for every M (the decode kernel up to 16

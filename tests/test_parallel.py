@@ -18,8 +18,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 import torch.nn.functional as F
 
-from llm_serving_engine_b200.parallel import (ColumnParallelInt8Linear, TensorParallelInt8MLP, gather_columns,
-                                              interleaved_rows, shard_rows)
+from llm_serving_engine_b200.parallel import (ColumnParallelInt8Linear, TensorParallelInt8MLP, fused_rows,
+                                              gather_columns, interleaved_rows, shard_rows)
 from oracle.ref_linear import ref_int8_linear, ref_quantize
 
 
@@ -72,6 +72,7 @@ def _mlp_case(rank: int, world: int) -> None:
     h = F.silu(gu[:, :I]) * gu[:, I:]
     ref = oracle_local(qd, sd)(h)
     mlp = TensorParallelInt8MLP.from_quantized(qg, sg, qu, su, qd, sd, local_factory=oracle_local)
+    assert not mlp.fused  # a substituted local linear keeps gate block | up block and SiLU * mul after it
     assert torch.equal(mlp(x), ref)
 
 
@@ -168,3 +169,18 @@ def test_rank_leaving_before_the_gather_errors_the_others(world):
     assert results[world - 1] == "left before the collective"
     for r in range(world - 1):
         assert results[r].startswith("error after"), results
+
+
+def test_fused_rows_interleave_the_rank_block_in_8_row_blocks():
+    """Rank r's gate and up rows in the fused kernel's order: 8 gate rows, then the matching
+    8 up rows; the same set of rows as the unfused order."""
+    I, world = 32, 2
+    for rank in range(world):
+        f = fused_rows(I, world, rank)
+        base = rank * I // world
+        expect = [base + j for j in range(8)] + [I + base + j for j in range(8)] + \
+                 [base + 8 + j for j in range(8)] + [I + base + 8 + j for j in range(8)]
+        assert f.tolist() == expect
+        assert sorted(f.tolist()) == sorted(interleaved_rows(I, world, rank).tolist())
+    with pytest.raises(ValueError):
+        fused_rows(24, 2, 0)  # 12 rows per rank
