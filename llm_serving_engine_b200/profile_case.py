@@ -2,6 +2,7 @@
 captures in profiles/ are taken on.
 
     python -m llm_serving_engine_b200.profile_case --M 16 --shape gate_up --algo tcgen05 --launches 4
+    python -m llm_serving_engine_b200.profile_case --M 64 --gate-up-silu --launches 6
 
 Weights (in the packed layout the module stores) are rotated over enough distinct copies that each launch reads its weight from
 HBM, not from L2 (126 MB); the device footprint stays at a few GB.  Prints the CUDA-event
@@ -30,12 +31,16 @@ def main(argv=None):
     ap.add_argument("--algo", choices=list(ALGOS), default="auto")
     ap.add_argument("--launches", type=int, default=4)
     ap.add_argument("--rowmajor", action="store_true", help="row-major W instead of the packed layout")
+    ap.add_argument("--gate-up-silu", action="store_true",
+                    help="the fused gate_up + SiLU*mul (ops.int8_gate_up_silu_packed) on the gate_up shape")
     ap.add_argument("--attention", type=int, default=0, metavar="E",
                     help="profile the paged decode attention instead: E sequences of 1025 positions, "
                          "Llama-3-8B attention shape, three layers' pools in rotation")
     args = ap.parse_args(argv)
     if args.attention:
         return attention_case(args.attention, args.launches)
+    if args.gate_up_silu:
+        args.shape = "gate_up"
     K, N = (LLAMA3_8B_SHAPES if args.model == "8b" else LLAMA3_70B_SHAPES)[args.shape]
     copies = max(2, -(-3 * 128 * 2**20 // (N * K)))  # > 3x L2 of weights in rotation
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -44,13 +49,16 @@ def main(argv=None):
         ws = [ops.pack_weight(w) for w in ws]
 
     def call(w):
-        if args.rowmajor:
+        if args.gate_up_silu:
+            ops.int8_gate_up_silu_packed(x, w, s, N // 2, K, out=h)
+        elif args.rowmajor:
             ops.int8_linear(x, w, s, out=y, algo=algo)
         else:
             ops.int8_linear_packed(x, w, s, N, K, out=y, algo=algo)
     s = torch.empty(N, device="cuda").uniform_(1e-4, 5e-4, generator=g)
     x = torch.randn(args.M, K, generator=g, device="cuda").to(torch.bfloat16)
     y = torch.empty(args.M, N, device="cuda", dtype=torch.bfloat16)
+    h = torch.empty(args.M, N // 2, device="cuda", dtype=torch.bfloat16)
     algo = ALGOS[args.algo]
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -69,7 +77,8 @@ def main(argv=None):
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.launches
-    print(f"M={args.M} {args.model}:{args.shape} K={K} N={N} algo={args.algo} {'row-major' if args.rowmajor else 'packed'}: {ms * 1e3:.2f} us/launch "
+    what = "fused gate_up+SiLU*mul" if args.gate_up_silu else f"algo={args.algo} {'row-major' if args.rowmajor else 'packed'}"
+    print(f"M={args.M} {args.model}:{args.shape} K={K} N={N} {what}: {ms * 1e3:.2f} us/launch "
           f"({linear_bytes(args.M, K, N) / ms / 1e6:.0f} GB/s, {linear_flops(args.M, K, N) / ms / 1e9:.1f} TFLOP/s, "
           f"CUDA-graph launches)")
     assert ops.device_status() == 0
