@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the sm_100a int8 weight-only linear (one JSON line on rank 0).
 
-Metric (BASELINE.json): int8 linear HBM GB/s (M<=64) & TFLOP/s (prefill) vs roofline;
+Metric: int8 linear HBM GB/s (M<=64) & TFLOP/s (prefill) vs roofline;
 decode tok/s.
 
 Workload (`config.workload`): config 2, the decode sweep: M in {1, 4, 16, 64} x the four

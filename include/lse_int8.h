@@ -280,6 +280,13 @@ int lse_device_status(int device, int reset);
  * launch, so a call never depends on an earlier one having finished cleanly.  The first
  * call on a device does the set-up (lse_init's work plus looking up the array's device
  * address) and should come before any stream capture.
+ *
+ * "Allocates nothing" is per call: the 12 MiB array itself is device memory, reserved when
+ * this library's module loads on the device.  With CUDA's lazy module loading (the default)
+ * that happens at lse_init or at the first entry-point call on that device.  A host that
+ * sizes a memory pool from the free memory it sees (the engine's KV pool) must therefore call
+ * lse_init(device) before sizing it; otherwise the module load can find no memory and the
+ * call returns LSE_ERR_CUDA.
  */
 #define LSE_NOALLOC_SCRATCH_BYTES 12582912
 #define LSE_NOALLOC_MAX_M 64

@@ -101,24 +101,31 @@ int current_device(int *dev) {
     return init_device(*dev);
 }
 
+// Tuning knobs.  The shipped library uses the constant given at each call site; a build with
+// -DLSE_TUNING (parameter sweeps only, never the shipped library) lets an environment
+// variable of the same name override it.
+int tuning_knob(const char *name, int value) {
+#ifdef LSE_TUNING
+    const char *e = std::getenv(name);
+    if (e) value = std::atoi(e);
+#else
+    (void)name;
+#endif
+    return value;
+}
+
 // Programmatic dependent launch: both kernels start their weight streams before waiting on
 // the previous kernel in the stream (griddepcontrol.wait), which hides launch latency and
-// pipeline fill between back-to-back projections.  LSE_DISABLE_PDL=1 turns it off.
+// pipeline fill between back-to-back projections.
 bool pdl_enabled() {
-    static const bool on = [] {
-        const char *v = std::getenv("LSE_DISABLE_PDL");
-        return !(v && v[0] == '1');
-    }();
+    static const bool on = tuning_knob("LSE_DISABLE_PDL", 0) != 1;
     return on;
 }
 
 // How many 16 KB weight tiles the kernel's prefetch warp keeps in flight to L2 ahead of the
-// data that has landed in shared memory (LSE_PF_STAGES overrides; 0 disables).
+// data that has landed in shared memory (0 disables).
 int prefetch_stages() {
-    static const int v = [] {
-        const char *e = std::getenv("LSE_PF_STAGES");
-        return e ? std::atoi(e) : 12;
-    }();
+    static const int v = tuning_knob("LSE_PF_STAGES", 12);
     return v;
 }
 
@@ -142,11 +149,9 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // 16/32-token tiles).
 int token_tile(int64_t M) { return M <= 64 ? 64 : 128; }
 
+// -1: the plan's rule below; 0 / 1 force the even spread / the aligned grid (sweeps only).
 int tc_split_align() {
-    static const int v = [] {
-        const char *e = std::getenv("LSE_TC_SPLIT_ALIGN");
-        return e ? (e[0] == '1' ? 1 : 0) : -1;
-    }();
+    static const int v = tuning_knob("LSE_TC_SPLIT_ALIGN", -1);
     return v;
 }
 
@@ -179,7 +184,6 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
     // either way), down 24.90 -> 24.83 (28 instead of 25); at M = 32 O 14.03 -> 12.68, QKV
     // 15.30 -> 14.61, down 23.51 -> 23.76; Llama-3-70B at M = 32 O 24.69 -> 25.97 (32 instead
     // of 28), down 61.36 -> 68.55 (112 instead of 97).
-    // LSE_TC_SPLIT_ALIGN=0 / 1 forces the even spread / the aligned grid (tuning runs).
     if (t.tiles <= G / 2) {
         const int s = G / t.tiles;
         const long long even = (static_cast<long long>(t.tiles) * t.kb + G - 1) / G;
@@ -287,12 +291,9 @@ int run_gemv(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, 
 // Groups per row block the decode kernel prefetches into L2 ahead of its register loads, for
 // M <= 8 (one group measured best on B200: 5-14% faster at M = 1 and 4; at M = 9..16, where
 // the activation loads weigh more, prefetching measured 3-5% slower and is off)
-// (LSE_SKINNY_PF overrides; 0 disables).
+// (0 disables).
 int skinny_prefetch_groups() {
-    static const int v = [] {
-        const char *e = std::getenv("LSE_SKINNY_PF");
-        return e ? std::max(0, std::atoi(e)) : 1;
-    }();
+    static const int v = std::max(0, tuning_knob("LSE_SKINNY_PF", 1));
     return v;
 }
 
@@ -336,13 +337,10 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
 //     activation loads, not the weight stream, would otherwise saturate L1);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
-// LSE_SKINNY_VARIANT=<0..17> pins one configuration for tuning runs (9, 10: the cp.async
+// -1 selects by shape as above; 0..17 pin one configuration in sweeps (9, 10: the cp.async
 // shared-memory weight ring, measured no faster than registers on B200).
 int skinny_variant() {
-    static const int v = [] {
-        const char *e = std::getenv("LSE_SKINNY_VARIANT");
-        return e ? std::atoi(e) : -1;
-    }();
+    static const int v = tuning_knob("LSE_SKINNY_VARIANT", -1);
     return v;
 }
 
@@ -688,7 +686,9 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
     if (K > 0) {
         const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
         const size_t need = tc_workspace_bytes(pl.nt, pl.grid);
-        if (need > static_cast<size_t>(LSE_NOALLOC_SCRATCH_BYTES)) {  // only on parts with > 160 SMs
+        // 64 KB of counters + 2 * grid * 64 * 128 * 4 bytes of partial tiles (M <= 64, token tile 64):
+        // more than the array only for a grid above (12 MiB - 64 KB) / 64 KB = 191 SMs.
+        if (need > static_cast<size_t>(LSE_NOALLOC_SCRATCH_BYTES)) {
             std::snprintf(t_last_error, sizeof(t_last_error),
                           "lse_int8_linear_packed_noalloc: this shape needs %zu scratch bytes, the fixed array "
                           "holds %d",
@@ -808,21 +808,16 @@ constexpr size_t kAttnCounterBytes = kAttnMaxSplitPairs * sizeof(int);
 // 2.738 ms/step in 3 splits, 2.760 in 4, 2.774 in 2; 16 sequences 3.384 ms unsplit, 3.460 in 2
 // splits.
 //
-// Tuning overrides for sweeps, read once per process: LSE_ATTN_MIN_CHUNK (fewest positions
-// per split) and LSE_ATTN_TARGET_CTAS (CTAs a split launch may reach; 0 = 1.5 per SM).
+// Fewest positions per split, and the CTAs a split launch may reach (0: 1.5 per SM).
 int attn_min_chunk() {
     static const int v = [] {
-        const char *e = std::getenv("LSE_ATTN_MIN_CHUNK");
-        const int c = e ? std::atoi(e) : 0;
+        const int c = tuning_knob("LSE_ATTN_MIN_CHUNK", 128);
         return c > 0 ? c : 128;
     }();
     return v;
 }
 int attn_target_ctas(int num_sms) {
-    static const int v = [] {
-        const char *e = std::getenv("LSE_ATTN_TARGET_CTAS");
-        return e ? std::max(0, std::atoi(e)) : 0;
-    }();
+    static const int v = std::max(0, tuning_knob("LSE_ATTN_TARGET_CTAS", 0));
     return v > 0 ? v : 3 * num_sms / 2;
 }
 

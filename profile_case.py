@@ -1,8 +1,8 @@
 """Launch one int8-linear shape a few times: the small, self-contained workload the ncu
 captures in profiles/ are taken on.
 
-    python -m llm_serving_engine_b200.profile_case --M 16 --shape gate_up --algo tcgen05 --launches 4
-    python -m llm_serving_engine_b200.profile_case --M 64 --gate-up-silu --launches 6
+    python profile_case.py --M 16 --shape gate_up --algo tcgen05 --launches 4
+    python profile_case.py --M 64 --gate-up-silu --launches 6
 
 Weights (in the packed layout the module stores) are rotated over enough distinct copies that each launch reads its weight from
 HBM, not from L2 (126 MB); the device footprint stays at a few GB.  Prints the CUDA-event
@@ -17,8 +17,8 @@ import argparse
 
 import torch
 
-from . import ops
-from .inputs import LLAMA3_8B_SHAPES, LLAMA3_70B_SHAPES, linear_bytes, linear_flops
+from llm_serving_engine_b200 import ops
+from llm_serving_engine_b200.inputs import LLAMA3_8B_SHAPES, LLAMA3_70B_SHAPES, linear_bytes, linear_flops
 
 ALGOS = {"auto": ops.ALGO_AUTO, "gemv": ops.ALGO_GEMV, "tcgen05": ops.ALGO_TCGEN05, "skinny": ops.ALGO_SKINNY}
 

@@ -71,8 +71,10 @@ def test_rejects_m_beyond_limit_before_any_launch():
     assert lib.lse_int8_linear_packed_noalloc(0, 0, 64, 64, 0, 0, 32, 0, 32, None) == _lib.LSE_OK
 
 
-# (M, K, N): every token tile the limit admits (16 / 32 / 64), stream-K only (few tiles),
-# data-parallel waves plus a stream-K tail, ragged N and K.
+# (M, K, N): all of them run the 64-token tile (every M up to the limit does); the cases
+# cover the schedules of the stream-K plan: a tile-aligned split (few tiles), data-parallel
+# waves plus a stream-K tail (gate_up), an even spread with tiles shared between CTAs, and
+# ragged N, M and K.
 CASES = [(1, 256, 384), (17, 1024, 1536), (33, 4096, 1000), (64, 4096, 6144), (64, 4096, 28672), (48, 14336, 4096)]
 
 
