@@ -249,18 +249,27 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
 
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     pts = []
+    all_ok = True
     for name in SHAPE_ORDER:
         K, N = LLAMA3_70B_SHAPES[name]
         n = N // world
         copies = max(1, min(8, -(-3 * 126 * 2**20 // (n * K))))
-        ws = []
-        for _ in range(copies):
+        # the full weight, identical on every rank (common seed): copy 0 of the rotation is this
+        # rank's row block of it, and the whole of it gives the single-GPU output the gathered
+        # output is checked against; the other copies only rotate the weight reads past L2
+        gf = torch.Generator(device=dev).manual_seed(1000 + K + N)
+        w_full = torch.randint(-127, 128, (N, K), generator=gf, device=dev, dtype=torch.int8)
+        s_full = torch.empty(N, device=dev).uniform_(1e-4, 5e-4, generator=gf)
+        full_packed = ops.pack_weight(w_full)
+        ws = [ops.pack_weight(w_full[rank * n:(rank + 1) * n])]
+        del w_full
+        for _ in range(copies - 1):
             w = torch.randint(-127, 128, (n, K), generator=g, device=dev, dtype=torch.int8)
             ws.append(ops.pack_weight(w))
             del w
-        s = torch.empty(n, device=dev).uniform_(1e-4, 5e-4, generator=g)
+        s = s_full[rank * n:(rank + 1) * n].contiguous()
         for M in TP_M:
-            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            x = torch.randn(M, K, generator=gf, device=dev).to(torch.bfloat16)  # same x on every rank
             y = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
 
             def one(x=x, y=y):
@@ -290,19 +299,32 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
             time_graph(g3, 1)
             t_e = time_graph(g3, 3) / 10
             del g3
+            # parity of the split: the gathered [M, N] output against one GPU's call on the whole
+            # weight, on sampled rows, the same check on every rank (north_star tolerance)
+            ops.int8_linear_packed(x, ws[0], s, n, K, out=y)
+            full = gather_columns(y)
+            rows = torch.unique(torch.tensor([0, M // 3, M // 2, M - 1], device=dev))
+            ref = ops.int8_linear_packed(x[rows], full_packed, s_full, N, K).float()
+            err = ((full[rows].float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item()
+            ok = max_over_ranks(0.0 if err <= 1e-2 else 1.0, world) == 0.0
+            all_ok = all_ok and ok
             t_k, t_g, t_e = (max_over_ranks(v, world) for v in (t_k, t_g, t_e))
             pts.append({"M": M, "shape": name, "K": K, "N": N, "rows_per_gpu": n,
                         "kernel_us": round(t_k * 1e3, 2), "gather_us": round(t_g * 1e3, 2),
                         "e2e_us": round(t_e * 1e3, 2),
                         "kernel_GBps_per_gpu": round(linear_bytes(M, K, n) / t_k / 1e6, 1),
                         "kernel_TFLOPs_per_gpu": round(linear_flops(M, K, n) / t_k / 1e9, 1),
-                        "gather_bytes": M * N * 2 if world > 1 else 0})
-            del x, y
-        del ws
+                        "gather_bytes": M * N * 2 if world > 1 else 0,
+                        "parity_vs_one_gpu": {"normwise": float(f"{max_over_ranks(err, world):.3e}"), "ok": ok}})
+            del x, y, full, ref
+        del ws, full_packed
         torch.cuda.empty_cache()
+    if not all_ok:
+        raise RuntimeError(f"config5 column split: gathered output differs from the one-GPU output: {pts}")
     return {"workload": f"config5: Llama-3-70B (K,N) qkv 8192x10240, o 8192x8192, gate_up 8192x57344, "
                         f"down 28672x8192; N split over {world} GPU(s); M in {list(TP_M)}",
             "collective": "NCCL all_gather_into_tensor of the output shards + column reorder" if world > 1 else "none",
+            "parity": "gathered output == one-GPU output within normwise 1e-2 on sampled rows, every point, every rank",
             "points": pts}
 
 

@@ -1,0 +1,87 @@
+"""The reference engine's `quantize="int8"` switch, bound to this package.
+
+The reference selects int8 with `ModelConfig.quantize = "int8"` (`LLM_QUANTIZE=int8`,
+`src/llm_serving_engine/config.py:32,46`) and refuses it as the first statement of
+`ModelRunner.__init__` (`src/llm_serving_engine/model/model_runner.py:45-46`).  A maintainer
+binds the switch by replacing that raise with the post-load swap `enable_int8(self)` (the
+two-line hook shown in the integration notes).  `install()` does the same from outside, for
+a reference that has not been edited: it wraps `ModelRunner.__init__` so that a config with
+`quantize="int8"` loads the model as the reference does (with `quantize="none"`), then swaps
+the projections, and any other config runs the reference's `__init__` untouched.
+
+After the swap nothing else in the engine changes: `forward`, `forward_fused`,
+`DecodeGraphRunner` (`decode_graph.py:87-140`) and `PiecewiseGraphRunner`
+(`piecewise_graph.py:71-183`) call the same module slots.  int8 needs CUDA; on a CPU-only
+machine the switch raises `RuntimeError` at load, the way the reference's custom-kernel
+check refuses a CPU device (`model_runner.py:77-94`); there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import functools
+
+import torch
+
+from . import ops
+from .int8_linear import quantize_llama_
+
+__all__ = ["enable_int8", "install", "uninstall", "installed"]
+
+
+def enable_int8(runner, lm_head: bool = False):
+    """Swap a loaded `ModelRunner`'s projections to int8 in place and prepare its device for
+    graph capture.  `runner.model` is the Llama-family model the runner loaded; every
+    decoder layer's q/k/v (one fused int8 QKV), o_proj and MLP become int8 (`quantize_llama_`),
+    and the lm_head too with `lm_head=True`."""
+    device = torch.device(runner.device)
+    if device.type != "cuda":
+        raise RuntimeError(f"int8 weight-only quantization needs a CUDA device, got {runner.device!r}")
+    quantize_llama_(runner.model, lm_head=lm_head)
+    ops.prepare_graph_capture(device)
+    return runner
+
+
+def _check_cuda(config) -> None:
+    if not torch.cuda.is_available() or not str(config.device).startswith("cuda"):
+        raise RuntimeError(
+            f"int8 weight-only quantization needs a CUDA device (config.device={config.device!r}, "
+            f"cuda available: {torch.cuda.is_available()}); there is no CPU int8 path")
+
+
+def _runner_class():
+    from llm_serving_engine.model.model_runner import ModelRunner
+
+    return ModelRunner
+
+
+def installed() -> bool:
+    return getattr(_runner_class().__init__, "_lse_int8", False)
+
+
+def install(lm_head: bool = False) -> None:
+    """Make `ModelRunner(ModelConfig(quantize="int8"))` load an int8 model (idempotent)."""
+    cls = _runner_class()
+    if installed():
+        return
+    original = cls.__init__
+
+    @functools.wraps(original)
+    def __init__(self, config, *args, **kwargs):
+        if getattr(config, "quantize", "none") != "int8":
+            return original(self, config, *args, **kwargs)
+        _check_cuda(config)
+        original(self, dataclasses.replace(config, quantize="none"), *args, **kwargs)
+        self.config = config
+        enable_int8(self, lm_head=lm_head)
+
+    __init__._lse_int8 = True
+    __init__._lse_original = original
+    cls.__init__ = __init__
+
+
+def uninstall() -> None:
+    """Restore the reference's own `ModelRunner.__init__`."""
+    cls = _runner_class()
+    if installed():
+        cls.__init__ = cls.__init__._lse_original

@@ -11,8 +11,12 @@ Graph capture: the op launches on `torch.cuda.current_stream()`, never synchroni
 never allocates outside the torch caching allocator (the output), so the reference's decode
 and piecewise CUDA-graph captures (`decode_graph.py:87-116`, `piecewise_graph.py:71-109`)
 record it like any other kernel.  The one piece of state is a per-(device, stream) workspace,
-created zeroed on first use; creating it inside a capture is refused, and the engine's
-warm-up iterations on the capture stream create it before the capture starts.
+created zeroed on first use.  Creating it inside a capture is refused (its zeroing would
+run only when the graph replays), so it must exist before a capture starts.  The reference
+warms up on `graph_warmup_stream` but captures on the stream `torch.cuda.graph` makes for
+itself (`torch.cuda.graph.default_capture_stream`, used when no stream is passed, as both
+of the engine's captures do); `prepare_graph_capture(device)`, run at the first op call on
+a device, creates that stream and its workspace.
 """
 
 from __future__ import annotations
@@ -38,6 +42,7 @@ __all__ = [
     "rms_norm",
     "pool_slot_offsets",
     "workspace_for",
+    "prepare_graph_capture",
     "device_status",
     "ALGO_AUTO",
     "ALGO_GEMV",
@@ -64,6 +69,27 @@ def _ensure_device(device: torch.device) -> None:
     if idx not in _inited:
         _lib.check(_lib.load().lse_init(idx), f"lse_init(cuda:{idx})")
         _inited.add(idx)
+        if not torch.cuda.is_current_stream_capturing():
+            prepare_graph_capture(torch.device("cuda", idx))
+
+
+def prepare_graph_capture(device: torch.device | int | None = None) -> None:
+    """Create, outside any capture, the workspace of the stream `torch.cuda.graph` captures
+    on when it is given none (`torch.cuda.graph.default_capture_stream`, made here if no graph
+    has been captured yet), so that the reference's decode and piecewise captures record only
+    kernel launches.  Runs once per device at the first op call; a capture on any other
+    stream needs one eager op call (or `workspace_for(device, stream)`) on that stream first."""
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        device = torch.device("cuda", device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with torch.cuda.device(idx):
+        if torch.cuda.graph.default_capture_stream is None:
+            torch.cuda.graph(torch.cuda.CUDAGraph())  # constructing it creates the class's default capture stream
+        stream = torch.cuda.graph.default_capture_stream
+        if stream.device.index == idx:
+            workspace_for(torch.device("cuda", idx), stream)
 
 
 def workspace_for(device: torch.device, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
@@ -79,7 +105,7 @@ def workspace_for(device: torch.device, stream: torch.cuda.Stream | None = None)
                 if torch.cuda.is_current_stream_capturing():
                     raise RuntimeError(
                         "int8_linear: first call on this stream happened inside a CUDA graph capture; "
-                        "run one eager call on the capture stream first (the engine's warm-up does)")
+                        "run one eager call on the capture stream first, or ops.workspace_for(device, stream)")
                 nbytes = int(_lib.load().lse_int8_linear_workspace(1 << 20, 1, 1))
                 ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
                 _workspaces[key] = ws

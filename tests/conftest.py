@@ -9,6 +9,12 @@ import torch
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
+# The reference engine itself (`pip install --no-deps --target baseline/_ref`, done by
+# __graft_entry__.build() where the reference source is present): the engine tests run its own
+# ModelRunner and graph runners with the int8 modules swapped in.
+REF_SITE = os.path.join(REPO, "baseline", "_ref")
+if os.path.isdir(os.path.join(REF_SITE, "llm_serving_engine")) and REF_SITE not in sys.path:
+    sys.path.append(REF_SITE)
 
 
 def pytest_configure(config: pytest.Config) -> None:

@@ -47,8 +47,15 @@ def abi_linear(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, ws: Workspace,
     return y
 
 
-def oracle_rows(x_cpu: torch.Tensor, w_cpu: torch.Tensor, s_cpu: torch.Tensor, rows) -> np.ndarray:
-    return ref_int8_linear(x_cpu[rows].float().numpy(), w_cpu.numpy(), s_cpu.numpy())
+def oracle_rows(x_cpu: torch.Tensor, w_cpu: torch.Tensor, s_cpu: torch.Tensor, rows, chunk: int = 4096) -> np.ndarray:
+    """The fp64 oracle on the listed rows of x; the weight is widened `chunk` output rows at a
+    time, so a 70B-sized matrix never exists in float64 at once."""
+    xr = x_cpu[rows].float().numpy()
+    w, s = w_cpu.numpy(), s_cpu.numpy()
+    N = w.shape[0]
+    if N <= chunk:
+        return ref_int8_linear(xr, w, s)
+    return np.concatenate([ref_int8_linear(xr, w[i:i + chunk], s[i:i + chunk]) for i in range(0, N, chunk)], axis=-1)
 
 
 def check_parity(y_gpu: torch.Tensor, ref: np.ndarray, what: str = "") -> float:

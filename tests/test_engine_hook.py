@@ -1,0 +1,60 @@
+"""Host-side behaviour of the `quantize="int8"` switch on the reference's ModelRunner (CPU).
+
+The reference refuses int8 with NotImplementedError (`src/llm_serving_engine/model/
+model_runner.py:45-46`, pinned by its `tests/test_model_runner.py:120-122`).  With
+`engine_hook.install()` the same call loads an int8 model on a GPU (tests/test_gpu_engine.py);
+on a machine without CUDA it must refuse loudly instead of falling back to a CPU path, and
+every other config must run the reference's own constructor unchanged.
+"""
+
+from __future__ import annotations
+
+import pytest
+
+from tests.engine_helpers import ModelConfig, ModelRunner, save_tiny_llama
+
+from llm_serving_engine_b200 import engine_hook
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(tmp_path_factory):
+    return save_tiny_llama(tmp_path_factory.mktemp("tiny-int8-llama-cpu"))
+
+
+@pytest.fixture
+def hooked():
+    engine_hook.install()
+    yield
+    engine_hook.uninstall()
+
+
+def test_reference_refuses_int8_without_the_hook(tiny_dir):
+    assert not engine_hook.installed()
+    with pytest.raises(NotImplementedError):
+        ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cpu", quantize="int8", use_custom_kernels=False))
+
+
+def test_hook_refuses_int8_without_cuda(tiny_dir, hooked, monkeypatch):
+    import torch
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(RuntimeError, match="needs a CUDA device"):
+        ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cuda", quantize="int8"))
+
+
+def test_hook_leaves_other_configs_to_the_reference(tiny_dir, hooked):
+    runner = ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cpu", dtype="float32",
+                                     use_custom_kernels=False))
+    assert runner.config.quantize == "none"
+    assert type(runner.model.model.layers[0].self_attn.o_proj).__name__ == "Linear"
+
+
+def test_install_is_idempotent_and_uninstall_restores():
+    original = ModelRunner.__init__
+    engine_hook.install()
+    wrapped = ModelRunner.__init__
+    engine_hook.install()
+    assert ModelRunner.__init__ is wrapped and wrapped is not original
+    engine_hook.uninstall()
+    assert ModelRunner.__init__ is original
+    assert not engine_hook.installed()

@@ -27,6 +27,31 @@ def test_int8_step_matches_dequantized_bf16_step(batch):
     assert np.isfinite(err) and err < 2e-2, err
 
 
+@pytest.mark.parametrize("batch", [16, 64])  # decode kernel / tensor-core kernel, as in config 4's step
+def test_llama3_8b_int8_step_matches_dequantized_twin(batch):
+    """Config 4's model at full size (Llama-3-8B shape, 32 layers, paged attention over a
+    1024-position context): one step's logits with the int8 projections against the same step
+    with bf16 projections on the dequantized int8 weights (normwise), and the same greedy token
+    wherever the twin's best two logits are further apart than the largest logit difference."""
+    from llm_serving_engine_b200.llama_decode import LLAMA3_8B
+
+    q8 = DecodeModel(LLAMA3_8B, batch=batch, context=1024, device="cuda", seed=11, quantize=True)
+    deq = q8.dequantized_weights(torch.bfloat16)
+    ref = DecodeModel(LLAMA3_8B, batch=batch, context=1024, device="cuda", seed=11, quantize=False, weights=deq,
+                      kv=q8.kv)
+    tokens = (torch.arange(batch, device="cuda") * 1999) % LLAMA3_8B.vocab
+    a, b = q8.logits(tokens), ref.logits(tokens)
+    diff = (a - b).abs()
+    err = (diff.max() / b.abs().max()).item()
+    assert np.isfinite(err) and err < 3e-2, err
+    top2 = b.topk(2, dim=-1).values
+    decisive = (top2[:, 0] - top2[:, 1]) > diff.max(dim=-1).values
+    assert int(decisive.sum()) >= batch // 8
+    assert torch.equal(a.argmax(-1)[decisive], b.argmax(-1)[decisive])
+    del q8, ref, deq
+    torch.cuda.empty_cache()
+
+
 def test_graph_replay_equals_eager_step():
     m = DecodeModel(TINY, batch=8, context=32, device="cuda", seed=5, quantize=True)
     m.tokens.copy_(torch.arange(8, device="cuda") * 11)

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from llm_serving_engine_b200 import _lib, ops
-from llm_serving_engine_b200.inputs import LLAMA3_8B_SHAPES, make_inputs
+from llm_serving_engine_b200.inputs import LLAMA3_8B_SHAPES, LLAMA3_70B_SHAPES, make_inputs
 from oracle.ref_linear import ref_int8_linear, ref_quantize
 from tests.gpu_helpers import Workspace, abi_linear, check_parity, oracle_rows
 
@@ -65,6 +65,53 @@ def test_decode_sweep_gemv(ws, shape, M):
 def test_prefill_tcgen05(ws, shape, M):
     K, N = LLAMA3_8B_SHAPES[shape]
     _run_case(M, K, N, _lib.ALGO_TCGEN05, ws, sample=24)
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+def _sample_rows(M: int, sample: int, seed: int) -> np.ndarray:
+    if M <= sample:
+        return np.arange(M)
+    return np.unique(np.concatenate([[0, M - 1], np.random.default_rng(seed).choice(M, sample, replace=False)]))
+
+
+@pytest.mark.parametrize("shape", list(LLAMA3_8B_SHAPES))
+@pytest.mark.parametrize("M", [512, 2048, 8192])
+def test_prefill_packed_auto_config3(ws, shape, M):
+    """Config 3 as the modules and the bench run it: packed weights, automatic kernel choice,
+    M up to 8192 (sampled rows against the oracle)."""
+    K, N = LLAMA3_8B_SHAPES[shape]
+    x, w, s = make_inputs(M, K, N, seed=M + N)
+    packed = ops.pack_weight(w.cuda())
+    y = _packed_call(x.cuda(), packed, s.cuda(), N, K, ws, _lib.ALGO_AUTO)
+    torch.cuda.synchronize()
+    rows = _sample_rows(M, 16, M + K)
+    check_parity(y[torch.as_tensor(rows, device="cuda")], oracle_rows(x, w, s, rows), f"config3 {shape} M={M}")
+    assert ws.counters_clear() and ws.guard_intact()
+
+
+@pytest.fixture(scope="module", params=list(LLAMA3_70B_SHAPES))
+def w70b(request):
+    """One Llama-3-70B projection at full size: (name, K, N, W int8 [N, K] on the CPU, s, packed W on the GPU)."""
+    K, N = LLAMA3_70B_SHAPES[request.param]
+    g = torch.Generator().manual_seed(K + N)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    s = torch.empty(N).uniform_(1e-4, 5e-4, generator=g)
+    packed = ops.pack_weight(w.cuda())
+    yield request.param, K, N, w, s, packed
+    del packed
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("M", [1, 32, 256, 4096])
+def test_config5_70b_full_shapes_packed(ws, w70b, M):
+    """Config 5's four 70B shapes at full size on the packed, automatic path (the one the module
+    and the column split run), at the sweep's M values; sampled rows against the oracle."""
+    name, K, N, w, s, packed = w70b
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(M + 1)).to(torch.bfloat16)
+    y = _packed_call(x.cuda(), packed, s.cuda(), N, K, ws, _lib.ALGO_AUTO)
+    torch.cuda.synchronize()
+    rows = _sample_rows(M, 6, M + N)
+    check_parity(y[torch.as_tensor(rows, device="cuda")], oracle_rows(x, w, s, rows), f"config5 {name} M={M}")
     assert ws.counters_clear() and ws.guard_intact()
 
 
