@@ -158,33 +158,41 @@ class DecodeModel:
     def _head(self, h: torch.Tensor) -> torch.Tensor:
         return self.lm_head_int8(h) if self.lm_head_int8 is not None else F.linear(h, self.lm_head)
 
-    def _hidden(self, tokens: torch.Tensor, in_place: bool) -> torch.Tensor:
-        """Final-norm hidden state of one step.  `in_place` writes the new K/V into the
-        caches (the decode step); otherwise into copies (a side-effect-free check)."""
+    def layer(self, li: int, h: torch.Tensor, in_place: bool = False) -> torch.Tensor:
+        """Decoder layer `li` on the residual stream `h` [B, H]; returns the new stream.
+        `in_place` writes the new K/V into the caches (the decode step); otherwise into copies
+        (a side-effect-free check)."""
         s = self.shape
-        B, hd, pos = self.batch, s.head_dim, self.context
+        B, hd = self.batch, s.head_dim
+        qkv_p, o_p, mlp = self.proj[li]
+        n_in, n_post = self.norms[li]
+        x = _rms_norm(h, n_in, s.eps)
+        qkv = qkv_p(x)
+        kc, vc = self.kv["k"][li], self.kv["v"][li]
+        if not in_place:
+            kc, vc = kc.clone(), vc.clone()
+        # RoPE on q and k, k and v into their slots, q as (heads, B, hd): one kernel
+        qh = ops.rope_kv_write(qkv, s.heads, s.kv_heads, hd, self.cos_full, self.sin_full, kc, vc,
+                               self.kv["kv_off"], self.kv["kv_head_stride"])
+        q = qh.transpose(0, 1)  # [B, heads, hd] view
+        if self.attention == "paged":
+            attn = ops.paged_decode_attention(q, kc, vc, self.kv["block_table"], self.kv["context_len"],
+                                              self.context + 1)
+        else:
+            attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
+        h = o_p(attn.reshape(B, s.heads * hd), residual=h)  # residual + o_proj(attn)
+        x = _rms_norm(h, n_post, s.eps)
+        return mlp(x, residual=h)
+
+    def _hidden(self, tokens: torch.Tensor, in_place: bool, trace: list | None = None) -> torch.Tensor:
+        """Final-norm hidden state of one step (`layer` over every layer); `trace`, when
+        given, receives each layer's input stream."""
         h = self.embed[tokens]  # [B, H]
-        for li in range(s.layers):
-            qkv_p, o_p, mlp = self.proj[li]
-            n_in, n_post = self.norms[li]
-            x = _rms_norm(h, n_in, s.eps)
-            qkv = qkv_p(x)
-            kc, vc = self.kv["k"][li], self.kv["v"][li]
-            if not in_place:
-                kc, vc = kc.clone(), vc.clone()
-            # RoPE on q and k, k and v into their slots, q as (heads, B, hd): one kernel
-            qh = ops.rope_kv_write(qkv, s.heads, s.kv_heads, hd, self.cos_full, self.sin_full, kc, vc,
-                                   self.kv["kv_off"], self.kv["kv_head_stride"])
-            q = qh.transpose(0, 1)  # [B, heads, hd] view
-            if self.attention == "paged":
-                attn = ops.paged_decode_attention(q, kc, vc, self.kv["block_table"], self.kv["context_len"],
-                                                  self.context + 1)
-            else:
-                attn = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=True)
-            h = o_p(attn.reshape(B, s.heads * hd), residual=h)  # residual + o_proj(attn)
-            x = _rms_norm(h, n_post, s.eps)
-            h = mlp(x, residual=h)
-        return _rms_norm(h, self.final_norm, s.eps)
+        for li in range(self.shape.layers):
+            if trace is not None:
+                trace.append(h)
+            h = self.layer(li, h, in_place)
+        return _rms_norm(h, self.final_norm, self.shape.eps)
 
     def dequantized_weights(self, dtype: torch.dtype = torch.bfloat16) -> list:
         """Per layer the dequantized int8 weights in `weights` order ([q;k;v], o, [gate;up],

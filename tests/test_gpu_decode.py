@@ -28,11 +28,13 @@ def test_int8_step_matches_dequantized_bf16_step(batch):
 
 
 @pytest.mark.parametrize("batch", [16, 64])  # decode kernel / tensor-core kernel, as in config 4's step
-def test_llama3_8b_int8_step_matches_dequantized_twin(batch):
+def test_llama3_8b_int8_layers_match_dequantized_twin(batch):
     """Config 4's model at full size (Llama-3-8B shape, 32 layers, paged attention over a
-    1024-position context): one step's logits with the int8 projections against the same step
-    with bf16 projections on the dequantized int8 weights (normwise), and the same greedy token
-    wherever the twin's best two logits are further apart than the largest logit difference."""
+    1024-position context), layer by layer: every layer of the int8 model and of its twin with
+    bf16 projections on the dequantized int8 weights runs on the same input (the int8 model's
+    own residual stream at that layer), and the two residual updates agree within normwise
+    2e-2.  End to end, the logits after 32 random-init layers, where the two models' rounding
+    differences compound, agree within 1e-1."""
     from llm_serving_engine_b200.llama_decode import LLAMA3_8B
 
     q8 = DecodeModel(LLAMA3_8B, batch=batch, context=1024, device="cuda", seed=11, quantize=True)
@@ -40,15 +42,19 @@ def test_llama3_8b_int8_step_matches_dequantized_twin(batch):
     ref = DecodeModel(LLAMA3_8B, batch=batch, context=1024, device="cuda", seed=11, quantize=False, weights=deq,
                       kv=q8.kv)
     tokens = (torch.arange(batch, device="cuda") * 1999) % LLAMA3_8B.vocab
-    a, b = q8.logits(tokens), ref.logits(tokens)
-    diff = (a - b).abs()
-    err = (diff.max() / b.abs().max()).item()
-    assert np.isfinite(err) and err < 3e-2, err
-    top2 = b.topk(2, dim=-1).values
-    decisive = (top2[:, 0] - top2[:, 1]) > diff.max(dim=-1).values
-    assert int(decisive.sum()) >= batch // 8
-    assert torch.equal(a.argmax(-1)[decisive], b.argmax(-1)[decisive])
-    del q8, ref, deq
+    trace: list = []
+    a = q8._head(q8._hidden(tokens, in_place=False, trace=trace)).float()
+    worst = 0.0
+    for li, h in enumerate(trace):
+        da = (q8.layer(li, h) - h).float()
+        db = (ref.layer(li, h) - h).float()
+        err = ((da - db).abs().max() / db.abs().max()).item()
+        assert np.isfinite(err) and err < 2e-2, f"layer {li}: residual update normwise {err:.3e}"
+        worst = max(worst, err)
+    b = ref.logits(tokens)
+    e2e = ((a - b).abs().max() / b.abs().max()).item()
+    assert np.isfinite(e2e) and e2e < 1e-1, f"logits after 32 layers: normwise {e2e:.3e} (worst layer {worst:.3e})"
+    del q8, ref, deq, trace
     torch.cuda.empty_cache()
 
 
