@@ -653,7 +653,7 @@ def main():
     # The auto policy of lse_int8_linear_packed: the warp-MMA skinny kernel for M <= 16, the
     # tcgen05 kernel above.
     points = []
-    per_kernel = {"skinny_i8_kernel": [0.0, 0.0, 0], "tc_gemm_i8_kernel": [0.0, 0.0, 0]}  # bytes, ms, launches
+    per_kernel = {"skinny_i8_kernel": [0.0, 0.0, 0], "tc_i8_kernel": [0.0, 0.0, 0]}  # bytes, ms, launches
     for M in DECODE_M:
         for name in SHAPE_ORDER:
             K, N = LLAMA3_8B_SHAPES[name]
@@ -666,7 +666,7 @@ def main():
             time_graph(g1, 2)
             per_launch_ms = time_graph(g1, 10) / layers
             b = linear_bytes(M, K, N)
-            kern = "skinny_i8_kernel" if M <= 16 else "tc_gemm_i8_kernel"
+            kern = "skinny_i8_kernel" if M <= 16 else "tc_i8_kernel"
             per_kernel[kern][0] += b
             per_kernel[kern][1] += per_launch_ms
             per_kernel[kern][2] += 1

@@ -69,11 +69,20 @@ int lse_init(int device);
  *   w      int8 [N, K] row-major (nn.Linear [out, in] layout), K % 16 == 0, 16-byte aligned
  *   scale  fp32 [N] per-output-channel scale
  *   y      bf16 [M, N], row stride ldy (>= N), 2-byte aligned
- *   workspace  device scratch of at least lse_int8_linear_workspace(M, K, N) bytes,
- *              16-byte aligned; its first LSE_WS_COUNTER_BYTES bytes must be zero before the
- *              first call, and every successful call leaves them zero again.
+ *   workspace  device scratch of at least lse_int8_linear_workspace(M, K, N) bytes (0 and NULL
+ *              are allowed when lse_int8_linear_workspace_for reports 0 for the call), 16-byte
+ *              aligned, contents irrelevant: the call initialises what it uses, so a fresh
+ *              allocation from any allocator (a caching allocator's block, memory captured
+ *              into a CUDA graph's pool) serves.
  * M == 0 or N == 0 is a no-op returning LSE_OK.  K == 0 writes zeros.
  * Calls that share one workspace must be ordered on the GPU (same stream, or events).
+ *
+ * The tensor-core path (LSE_ALGO_TCGEN05) multiplies int8 weights by int8 activation digits:
+ * a first kernel writes each token row as S signed 8-bit digit planes under a power-of-two
+ * row scale (S = 3 up to 64 tokens, 2 above: every element at least 2^(10-8S) times the
+ * row's largest is represented exactly, any element to within 2^-(8S-2) of the largest),
+ * the projection accumulates in exact int32 (tcgen05.mma kind::i8) and applies the scales
+ * in fp32.  A row holding a NaN or an infinity produces a NaN output row.
  */
 int lse_int8_linear(const void *x, int64_t M, int64_t K, int64_t ldx,
                     const int8_t *w, const float *scale, int64_t N,
@@ -89,15 +98,15 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx,
                        int algo, void *stream);
 
 /*
- * Packed weights.  The kernels stream weights fastest from a fragment-major layout: W is
- * zero padded to Np = 128*ceil(N/128) rows and Kp = 128*ceil(K/128) columns; each block of
- * 16 rows is one contiguous run of 16*Kp bytes made of 512-byte chunks (one per 32 columns)
- * in which lane t = 4*r0 + q of a warp owns 16 bytes:
- *   W[rb*16 + rr*8 + r0][kc*32 + h*16 + 4*q + e]  at  (rb*(Kp/32) + kc)*512 + t*16 + h*8 + rr*4 + e
- * (rb row block, kc column chunk, h, rr in {0,1}, r0 < 8, q < 4, e < 4), each byte stored
- * biased (v ^ 0x80, i.e. v + 128).  One 128-bit load per
- * lane then yields warp-MMA operand fragments for the decode kernel, and tensor-memory rows
- * for the prefill kernel, without any shuffling.
+ * Packed weights.  Both kernels stream weights from one packed layout: W is zero padded to
+ * Np = 128*ceil(N/128) rows and Kp = 128*ceil(K/128) columns and cut into groups of 8 rows;
+ * group g is one contiguous run of 8*Kp bytes made of 512-byte atoms, one per 64 columns,
+ * each holding its 8 rows' 64 columns (64 bytes per row) with the 16-byte chunk c of row r
+ * stored at chunk position c ^ ((r >> 1) & 3) (the tensor core's 64-byte swizzle):
+ *   W[8*g + r][64*a + 16*c + e]  at  g*8*Kp + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e
+ * (r < 8, c < 4, e < 16), plain two's-complement bytes.  A 128 x 128 tile is then the tensor
+ * core's K-major operand as it stands (16 runs of 1 KB, one bulk-tensor copy), and one 128-bit
+ * load per lane gives the decode kernel a warp-MMA operand fragment, without any shuffling.
  * The repack happens once, at load (the build's counterpart of the reference loading
  * nn.Linear weights at model_runner.py:50-53); lse_int8_linear_packed then has the same
  * contract as lse_int8_linear_ex with `w_packed` in place of the row-major W.  Its auto
@@ -149,7 +158,7 @@ int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ld
 
 /*
  * The same for any M, with a workspace of at least lse_int8_linear_workspace(M, K, 2 * I)
- * bytes (zero-initialised once, as for lse_int8_linear_packed; unused for M <= 16): M <= 16
+ * bytes (any contents, as for lse_int8_linear_packed; unused for M <= 16): M <= 16
  * runs the decode kernel above, larger M the tcgen05 kernel with SiLU * mul in its epilogue,
  * so that the [M, 2I] gate/up output never reaches memory.  Same weights, scales, y and
  * error codes as lse_int8_gate_up_silu_packed, plus LSE_ERR_WORKSPACE.
@@ -221,12 +230,20 @@ int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int
 int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
                  int64_t ldy, void *stream);
 
-/* Bytes of the counter region at the start of every workspace (must start zeroed). */
+/* Bytes of the counter region at the start of every linear workspace (the tensor-core path
+ * clears the counters it uses before each launch). */
 #define LSE_WS_COUNTER_BYTES 65536
 
-/* Workspace bytes lse_int8_linear needs for this shape (auto algo); always >= the
- * counter region. */
+/* Workspace bytes the tensor-core path needs for this shape (any weight layout): stream-K
+ * counters, partial tiles, the activation digit planes and row scales; always >= the counter
+ * region.  Enough for every algorithm. */
 size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N);
+
+/* Workspace bytes one call with this algorithm choice (lse_algo, after LSE_ALGO_AUTO's choice
+ * by M and layout) and weight layout (packed nonzero: lse_int8_linear_packed and the gate_up
+ * entries; 0: lse_int8_linear / _ex) needs: 0 when the chosen kernel uses none (the decode
+ * kernel, the GEMV), lse_int8_linear_workspace(M, K, N) otherwise. */
+size_t lse_int8_linear_workspace_for(int64_t M, int64_t K, int64_t N, int algo, int packed);
 
 /*
  * Symmetric per-output-channel quantization at load time (the build's replacement for the
@@ -248,8 +265,9 @@ const char *lse_last_cuda_error(void);
 /*
  * Device-side status of `device`: LSE_OK, or LSE_ERR_DEVICE_TIMEOUT when a bounded
  * wait inside a kernel gave up since the last reset.  Synchronizes the device.  When
- * `reset` is nonzero the flag is cleared.  After a timeout the workspace counter region
- * must be zeroed again before the next call.
+ * `reset` is nonzero the flag is cleared.  After a timeout the decode-attention workspace
+ * (lse_paged_decode_attention) must be zeroed again before its next use; the linear
+ * workspaces need nothing.
  */
 int lse_device_status(int device, int reset);
 
@@ -258,8 +276,9 @@ int lse_device_status(int device, int reset);
  * library for callers that cannot allocate a workspace.
  *
  * Same result as lse_int8_linear_packed(..., LSE_ALGO_TCGEN05, ...), without the workspace
- * arguments: the tensor-core kernel's scratch (stream-K arrival counters and partial tiles)
- * is a fixed array of LSE_NOALLOC_SCRATCH_BYTES (12 MiB) per device, a static device
+ * arguments: the tensor-core path's scratch (stream-K arrival counters, partial tiles, the
+ * activation digit planes and row scales) is a fixed array of LSE_NOALLOC_SCRATCH_BYTES
+ * (16 MiB) per device, a static device
  * variable of this library, so the call allocates nothing, neither device nor host memory.
  * Who needs it: a binding that mirrors the engine's nn.Linear call (x, W, s -> y) has no
  * workspace to pass and often no device allocator of its own (a plain C, ctypes or cgo
@@ -271,24 +290,26 @@ int lse_device_status(int device, int reset);
  *   M: 1 .. LSE_NOALLOC_MAX_M (64) tokens -- the largest token tile whose partial tiles fit
  *      the fixed array.  A larger M returns LSE_ERR_WORKSPACE before touching the GPU, with
  *      the limit in lse_last_cuda_error(); use lse_int8_linear_packed with a workspace.
- *      M == 0 or N == 0 is a no-op; K == 0 writes zeros.
+ *      K: the digit planes take 3 * M * K bytes, so at M = 64 K up to about 36,000 fits on
+ *      a 148-SM GPU (every Llama-3 8B and 70B projection); a larger need also returns
+ *      LSE_ERR_WORKSPACE.  M == 0 or N == 0 is a no-op; K == 0 writes zeros.
  *
  * Every call on a device shares the one array, and the array keeps the last call's
  * contents.  Calls that overlap on the GPU (different streams with no ordering between
  * them) race on it and give wrong results: order them on one stream or with events.  Each
- * call clears the arrival counters it uses (an asynchronous memset on `stream`) before its
- * launch, so a call never depends on an earlier one having finished cleanly.  The first
+ * call's first kernel (the activation split) clears the arrival counters the call uses, so a
+ * call never depends on an earlier one having finished cleanly.  The first
  * call on a device does the set-up (lse_init's work plus looking up the array's device
  * address) and should come before any stream capture.
  *
- * "Allocates nothing" is per call: the 12 MiB array itself is device memory, reserved when
+ * "Allocates nothing" is per call: the 16 MiB array itself is device memory, reserved when
  * this library's module loads on the device.  With CUDA's lazy module loading (the default)
  * that happens at lse_init or at the first entry-point call on that device.  A host that
  * sizes a memory pool from the free memory it sees (the engine's KV pool) must therefore call
  * lse_init(device) before sizing it; otherwise the module load can find no memory and the
  * call returns LSE_ERR_CUDA.
  */
-#define LSE_NOALLOC_SCRATCH_BYTES 12582912
+#define LSE_NOALLOC_SCRATCH_BYTES 16777216
 #define LSE_NOALLOC_MAX_M 64
 int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t K, int64_t ldx,
                                    const int8_t *w_packed, const float *scale, int64_t N,

@@ -36,7 +36,7 @@ DT_F16 = 1
 DT_F32 = 2
 
 WS_COUNTER_BYTES = 65536
-NOALLOC_SCRATCH_BYTES = 12582912  # fixed scratch of lse_int8_linear_packed_noalloc, per device
+NOALLOC_SCRATCH_BYTES = 16777216  # fixed scratch of lse_int8_linear_packed_noalloc, per device
 NOALLOC_MAX_M = 64
 GATE_UP_SILU_MAX_M = 16  # lse_int8_gate_up_silu_packed's token range (the decode kernel's)
 ABI_VERSION = 1
@@ -48,6 +48,7 @@ SIGNATURES = {
     "lse_int8_linear": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _P], _I32),
     "lse_int8_linear_ex": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
     "lse_int8_linear_workspace": ([_I64, _I64, _I64], _SZ),
+    "lse_int8_linear_workspace_for": ([_I64, _I64, _I64, _I32, _I32], _SZ),
     "lse_int8_linear_packed": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _I32, _P], _I32),
     "lse_int8_linear_packed_residual": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _P, _SZ, _I32, _P],
                                         _I32),

@@ -1,0 +1,140 @@
+// Activation digit planes for the int8 tensor-core kernel (sm_100a).
+//
+// The tensor-core kernel multiplies int8 weights by int8 activations (tcgen05.mma
+// kind::i8, exact int32 accumulation).  The bf16 activations are written, per token row m,
+// as a fixed-point integer in S signed 8-bit digits under a power-of-two row scale:
+//
+//   r[m] = 2^e[m],  v[m, k] = rint(x[m, k] / r[m]) = sum_p d_p[m, k] * 256^(S-1-p),
+//   d_p in [-128, 127]   (p = 0 the most significant digit plane)
+//
+// so that  y[m, n] = s[n] * r[m] * sum_p 256^(S-1-p) * sum_k w[n, k] d_p[m, k].
+//
+// e[m] is the smallest exponent with max_k |x[m, k]| / 2^e <= V_S = 127 * (256^S - 1) / 255
+// (32639 for S = 2, 8355711 for S = 3), i.e. max |x| / 2^e in [2^(8S-2), 2^(8S-1)).
+// Hence every element with |x| >= max|x| * 2^(10-8S) (2^-6 of the row maximum for S = 2,
+// 2^-14 for S = 3) is represented exactly (its 8 significant bf16 bits sit at or above the
+// quantum), and any element's error is at most half a quantum, below max|x| * 2^-(8S-2).  A row
+// of zeros gets r = 1 and zero digits; a row holding a NaN or an infinity gets r = NaN (the
+// whole output row is NaN, as a matmul over it would be at least partly).
+//
+// Layout: plane p of row m is the int8 run planes[p * plane_stride + m * Kp + k], k < Kp
+// (zeros for K <= k < Kp), K-contiguous: the kernel's tensor map reads a box of
+// [S planes][token tile][128 K bytes] as one K-major B operand of S * NT rows.
+//
+// One CTA per row; CTA 0 also clears the stream-K arrival counters of the projection launch
+// that follows.  Programmatic dependent launch: the CTA releases its dependents on entry (the
+// projection kernel's weight copies start under it) and waits for the kernel that wrote x
+// before touching any memory.
+#pragma once
+
+#include "common.cuh"
+
+namespace lse {
+namespace split {
+
+constexpr int THREADS = 256;
+
+template <int S>
+struct Digits {
+    static_assert(S == 2 || S == 3, "2 or 3 digit planes");
+    static constexpr int kMaxV = S == 2 ? 32639 : 8355711;  // 127 * (256^S - 1) / 255
+    static constexpr int kTopExp = 8 * S - 2;                // max|x| / 2^e in [2^kTopExp, 2^(kTopExp+1))
+};
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Balanced base-256 digits of v (|v| <= kMaxV), most significant first, packed per plane into
+// byte `slot & 3` of d[p].
+template <int S>
+__device__ __forceinline__ void digits_of(int v, uint32_t (&d)[S], int slot) {
+#pragma unroll
+    for (int p = S - 1; p >= 0; --p) {
+        int dig = v;
+        if (p > 0) {
+            dig = ((v + 128) & 255) - 128;
+            v = (v - dig) >> 8;  // exact: v - dig is a multiple of 256
+        }
+        d[p] |= static_cast<uint32_t>(dig & 255) << (8 * (slot & 3));
+    }
+}
+
+template <int S>
+__global__ void __launch_bounds__(THREADS)
+act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *__restrict__ planes,
+                 int64_t plane_stride, float *__restrict__ row_scale, int *__restrict__ counters, int n_counters) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    const int m = blockIdx.x;
+    // The projection kernel that follows counts stream-K arrivals in `counters`: they start at
+    // zero for every launch without any invariant on the workspace's earlier contents.
+    if (m == 0)
+        for (int i = threadIdx.x; i < n_counters; i += THREADS) counters[i] = 0;
+    const __nv_bfloat16 *xr = x + static_cast<int64_t>(m) * ldx;
+    const int nk = K >> 3;  // 8-element chunks (K % 16 == 0, rows 16-byte aligned)
+    float amax = 0.f;
+    bool bad = false;
+    for (int c = threadIdx.x; c < nk; c += THREADS) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = fabsf(bf16_lo(w[i])), b = fabsf(bf16_hi(w[i]));
+            bad |= !(a <= 3.4e38f) || !(b <= 3.4e38f);  // NaN or infinity
+            amax = fmaxf(amax, fmaxf(a, b));
+        }
+    }
+    __shared__ float s_max[THREADS / 32];
+    __shared__ int s_bad[THREADS / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        bad |= __shfl_xor_sync(0xffffffffu, static_cast<int>(bad), o) != 0;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        s_max[warp] = amax;
+        s_bad[warp] = bad;
+    }
+    __syncthreads();
+    amax = 0.f;
+    bad = false;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) {
+        amax = fmaxf(amax, s_max[i]);
+        bad |= s_bad[i] != 0;
+    }
+    int e = 0;
+    if (!bad && amax > 0.f) {
+        e = ilogbf(amax) - Digits<S>::kTopExp;
+        if (ldexpf(amax, -e) > static_cast<float>(Digits<S>::kMaxV)) ++e;  // an all-ones mantissa
+    }
+    // digits: 8 elements per chunk -> S planes x 8 bytes
+    for (int c = threadIdx.x; c < (Kp >> 3); c += THREADS) {
+        uint32_t d0[S] = {}, d1[S] = {};
+        if (c < nk && !bad) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c));
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float f = h ? bf16_hi(w[i]) : bf16_lo(w[i]);
+                    int q = static_cast<int>(rintf(ldexpf(f, -e)));
+                    q = max(-Digits<S>::kMaxV, min(Digits<S>::kMaxV, q));
+                    const int slot = 2 * i + h;
+                    if (slot < 4) digits_of<S>(q, d0, slot);
+                    else digits_of<S>(q, d1, slot);
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < S; ++p)
+            *reinterpret_cast<uint2 *>(planes + p * plane_stride + static_cast<int64_t>(m) * Kp + 8 * c) =
+                make_uint2(d0[p], d1[p]);
+    }
+    if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);
+}
+
+}  // namespace split
+}  // namespace lse

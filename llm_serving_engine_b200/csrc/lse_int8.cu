@@ -22,7 +22,8 @@
 #include "pack_w.cuh"
 #include "quantize.cuh"
 #include "skinny_mma.cuh"
-#include "tc_gemm_i8.cuh"
+#include "act_split.cuh"
+#include "tc_i8.cuh"
 
 namespace lse {
 
@@ -54,10 +55,17 @@ DeviceState g_dev[kMaxDevices];
 std::once_flag g_encode_once;
 EncodeTiledFn g_encode = nullptr;
 
-template <int NT, bool SILU = false>
-cudaError_t set_tc_attrs() {
-    return cudaFuncSetAttribute(tc::tc_gemm_i8_kernel<NT, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                tc::Cfg<NT>::SMEM_BYTES);
+template <int NT, int S, bool SILU, bool WPACK>
+cudaError_t set_tci8_attrs() {
+    return cudaFuncSetAttribute(tci8::tc_i8_kernel<NT, S, SILU, WPACK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                tci8::Cfg<NT, S>::SMEM_BYTES);
+}
+
+template <bool SILU, bool WPACK>
+cudaError_t set_tci8_attrs_all() {
+    cudaError_t e = set_tci8_attrs<64, 3, SILU, WPACK>();
+    if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK>();
+    return e;
 }
 
 int init_device(int device) {
@@ -70,10 +78,9 @@ int init_device(int device) {
         if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) { set_cuda_error(e, "cudaSetDevice"); return; }
         int sms = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        if (e == cudaSuccess) e = set_tc_attrs<64>();
-        if (e == cudaSuccess) e = set_tc_attrs<128>();
-        if (e == cudaSuccess) e = set_tc_attrs<64, true>();
-        if (e == cudaSuccess) e = set_tc_attrs<128, true>();
+        if (e == cudaSuccess) e = set_tci8_attrs_all<false, false>();
+        if (e == cudaSuccess) e = set_tci8_attrs_all<false, true>();
+        if (e == cudaSuccess) e = set_tci8_attrs_all<true, true>();
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
         std::call_once(g_encode_once, [] {
             void *fn = nullptr;
@@ -165,9 +172,9 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
     TcPlan t{};
     t.nt = token_tile(M);
     t.m_tiles = static_cast<int>((M + t.nt - 1) / t.nt);
-    t.n_tiles = static_cast<int>((N + tc::BN - 1) / tc::BN);
+    t.n_tiles = static_cast<int>((N + tci8::BN - 1) / tci8::BN);
     t.tiles = t.m_tiles * t.n_tiles;
-    t.kb = static_cast<int>((K + tc::BK - 1) / tc::BK);
+    t.kb = static_cast<int>((K + tci8::BK - 1) / tci8::BK);
     int G = num_sms;
     if (t.tiles % G == 0) t.dp_tiles = t.tiles;
     else if (t.tiles < G) t.dp_tiles = 0;
@@ -197,9 +204,6 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
     return t;
 }
 
-size_t tc_workspace_bytes(int nt, int grid) {
-    return LSE_WS_COUNTER_BYTES + static_cast<size_t>(2) * grid * nt * tc::BN * sizeof(float);
-}
 
 int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
@@ -218,22 +222,69 @@ int encode_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
     return LSE_OK;
 }
 
-template <int NT, bool SILU = false>
-int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
-              const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
-              cudaStream_t st) {
-    CUtensorMap tw, tx;
-    // Packed W: [Np/16 row blocks][16*Kp bytes] as 8-byte elements, box = one 128 x 128 tile
-    // (8 row blocks x 2 KB), no swizzle.  Row-major W: [N][K] bytes, 128 x 128 box, 128B swizzle.
+int encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+              uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2) {
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::snprintf(t_last_error, sizeof(t_last_error), "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+        return LSE_ERR_CUDA;
+    }
+    return LSE_OK;
+}
+
+// Digit planes of the int8 tensor-core path: 3 (24-bit activations) up to 64 tokens, where the
+// MMA's N = 3 x 64 costs nothing against the weight stream, 2 (16-bit) above.
+int digit_planes(int64_t M) { return M <= 64 ? 3 : 2; }
+
+size_t tci8_partial_bytes(int nt, int grid) { return static_cast<size_t>(2) * grid * nt * tci8::BN * sizeof(float); }
+
+// Workspace of one tensor-core call: stream-K counters, partial tiles, S digit planes of
+// M x Kp bytes and M row scales.
+size_t tci8_workspace_bytes(int nt, int S, int grid, int64_t M, int64_t K) {
+    const size_t planes = static_cast<size_t>(S) * M * packed_cols(K);
+    return LSE_WS_COUNTER_BYTES + tci8_partial_bytes(nt, grid) + planes + (static_cast<size_t>(M) * 4 + 15) / 16 * 16;
+}
+
+template <int NT, int S, bool SILU>
+int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
+                 const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws,
+                 bool packed, cudaStream_t st) {
     const int64_t Kp = packed_cols(K);
-    int rc = packed ? encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, static_cast<uint64_t>(2 * Kp),
-                                static_cast<uint64_t>(packed_rows(N) / 16), static_cast<uint64_t>(16 * Kp), 256, 8,
+    uint8_t *wsb = static_cast<uint8_t *>(ws);
+    int *counters = reinterpret_cast<int *>(wsb);
+    float *partials = reinterpret_cast<float *>(wsb + LSE_WS_COUNTER_BYTES);
+    int8_t *planes = reinterpret_cast<int8_t *>(wsb + LSE_WS_COUNTER_BYTES + tci8_partial_bytes(NT, pl.grid));
+    const int64_t plane_stride = M * Kp;
+    float *rscale = reinterpret_cast<float *>(planes + S * plane_stride);
+    // 1) activations -> digit planes + row scales (also clears this launch's stream-K counters)
+    {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(split::THREADS), 0, st);
+        const int n_counters = static_cast<int>(pl.tiles - pl.dp_tiles);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, split::act_split_kernel<S>, static_cast<const __nv_bfloat16 *>(x), ldx,
+                                           static_cast<int>(K), static_cast<int>(Kp), planes, plane_stride, rscale,
+                                           counters, n_counters);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) { set_cuda_error(e, "act_split launch"); return LSE_ERR_CUDA; }
+    }
+    // 2) the projection
+    CUtensorMap tw, tx;
+    int rc = packed ? encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, static_cast<uint64_t>(Kp),
+                                static_cast<uint64_t>(packed_rows(N) / 8), static_cast<uint64_t>(8 * Kp), 128, 16,
                                 CU_TENSOR_MAP_SWIZZLE_NONE)
-                    : encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, tc::BK, tc::BN);
+                    : encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, tci8::BK, tci8::BN);
     if (rc) return rc;
-    rc = encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, ldx * 2, 64, NT);
+    rc = encode_3d(&tx, planes, static_cast<uint64_t>(Kp), static_cast<uint64_t>(M), S, static_cast<uint64_t>(Kp),
+                   static_cast<uint64_t>(plane_stride), tci8::BK, NT, S);
     if (rc) return rc;
-    tc::Params p{};
+    tci8::Params p{};
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
@@ -242,24 +293,36 @@ int launch_tc(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx
     p.res = static_cast<const __nv_bfloat16 *>(res);
     p.ldr = ldr;
     p.scale = scale;
-    p.counters = static_cast<int *>(ws);
-    p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + LSE_WS_COUNTER_BYTES);
+    p.row_scale = rscale;
+    p.counters = counters;
+    p.partials = partials;
     p.m_tiles = pl.m_tiles;
     p.tiles = pl.tiles;
     p.kb = pl.kb;
     p.dp_tiles = pl.dp_tiles;
     p.grid = pl.grid;
     p.sk_units = pl.sk_units;
-    p.w_packed = packed ? 1 : 0;
     p.w = w;
+    p.kp = Kp;
     p.pf_stages = prefetch_stages();
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, dim3(pl.grid), dim3(tc::NUM_THREADS), tc::Cfg<NT>::SMEM_BYTES, st);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc::tc_gemm_i8_kernel<NT, SILU>, tw, tx, p);
+    launch_config(cfg, attr, dim3(pl.grid), dim3(tci8::NUM_THREADS), tci8::Cfg<NT, S>::SMEM_BYTES, st);
+    cudaError_t e = packed ? cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, true>, tw, tx, p)
+                           : cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, false>, tw, tx, p);
     if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) { set_cuda_error(e, "tc_gemm_i8 launch"); return LSE_ERR_CUDA; }
+    if (e != cudaSuccess) { set_cuda_error(e, "tc_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
+}
+
+// The token tile and digit planes go together: 64-token tiles with 3 planes (M <= 64),
+// 128-token tiles with 2 planes above.
+template <bool SILU>
+int run_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
+              const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
+              cudaStream_t st) {
+    if (pl.nt == 64) return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st);
+    return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st);
 }
 
 template <int MT, int ROWS>
@@ -297,28 +360,15 @@ int skinny_prefetch_groups() {
     return v;
 }
 
-template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false, int P = 0>
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, cudaStream_t st) {
     const int64_t row_blocks = SILU_MUL ? N / 8 : (N + 15) / 16;  // weight row blocks (SILU_MUL: 2N rows)
     dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
-    constexpr int smem = P > 0 ? skinny_ring_bytes<KW, R, U, P>() : 0;
-    auto kernel = skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL, P>;
-    if constexpr (smem > 48 * 1024) {  // opt in to the cp.async ring's shared memory, once per device
-        static std::once_flag once[kMaxDevices];
-        static cudaError_t set_err[kMaxDevices];
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
-        if (e != cudaSuccess) return e;
-        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-        std::call_once(once[dev], [&] {
-            set_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        });
-        if (set_err[dev] != cudaSuccess) return set_err[dev];
-    }
+    auto kernel = skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, grid, dim3(KW * 32), smem, st);
+    launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<const __nv_bfloat16 *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
                               static_cast<__nv_bfloat16 *>(y), ldy, static_cast<const __nv_bfloat16 *>(res), ldr,
@@ -337,8 +387,7 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
 //     activation loads, not the weight stream, would otherwise saturate L1);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
-// -1 selects by shape as above; 0..17 pin one configuration in sweeps (9, 10: the cp.async
-// shared-memory weight ring, measured no faster than registers on B200).
+// -1 selects by shape as above; 0..17 pin one configuration in sweeps.
 int skinny_variant() {
     static const int v = tuning_knob("LSE_SKINNY_VARIANT", -1);
     return v;
@@ -352,7 +401,7 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
                              int num_sms, cudaStream_t st) {
     if (variant < 0) {
         const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
-        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 11) : (rb_per_sm >= 2 ? 15 : 0);
+        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 1) : (rb_per_sm >= 2 ? 1 : 0);
     }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
@@ -372,9 +421,8 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
             case 6: return launch_skinny<MT, 8, 2, 4, BF, 3, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 7: return launch_skinny<MT, 8, 1, 4, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 8: return launch_skinny<MT, 16, 1, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
-            // cp.async shared-memory weight ring (P groups of U chunks in flight per lane)
-            case 9: return launch_skinny<MT, 8, 1, 4, BF, 3, SILU, 4>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
-            case 10: return launch_skinny<MT, 16, 1, 4, BF, 2, SILU, 3>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 9: return launch_skinny<MT, 8, 1, 8, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+            case 10: return launch_skinny<MT, 16, 1, 8, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             // four row blocks per CTA: each activation load serves 64 weight rows
             case 11: return launch_skinny<MT, 8, 4, 2, BF, 2, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
             case 12: return launch_skinny<MT, 4, 4, 2, BF, 4, SILU>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
@@ -442,10 +490,15 @@ const char *lse_last_cuda_error(void) { return t_last_error; }
 int lse_init(int device) { return init_device(device); }
 
 size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N) {
-    (void)K;
     (void)N;
-    if (M <= 0) return LSE_WS_COUNTER_BYTES;
-    return tc_workspace_bytes(token_tile(M), kMaxGridForWorkspace);
+    if (M <= 0 || K < 0) return LSE_WS_COUNTER_BYTES;
+    return tci8_workspace_bytes(token_tile(M), digit_planes(M), kMaxGridForWorkspace, M, K);
+}
+
+size_t lse_int8_linear_workspace_for(int64_t M, int64_t K, int64_t N, int algo, int packed) {
+    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed != 0);
+    if (algo != LSE_ALGO_TCGEN05) return 0;
+    return lse_int8_linear_workspace(M, K, N);
 }
 
 }  // extern "C"
@@ -489,10 +542,10 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
         return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, res, ldr, g_dev[dev].num_sms, st);
 
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
-    if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
+    if (!workspace || !aligned16(workspace) ||
+        workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;
-    if (pl.nt == 64) return launch_tc<64>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
-    return launch_tc<128>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
+    return run_tc_i8<false>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
 }
 }  // namespace
 }  // namespace lse
@@ -538,9 +591,9 @@ int lse_int8_pack_weight(const int8_t *w, int64_t N, int64_t K, int64_t ldw, int
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
-    const int64_t quads = packed_weight_bytes(N, K) / 4;
-    pack_weight_kernel<<<static_cast<unsigned>((quads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        w, N, K, ldw, w_packed, packed_cols(K), quads);
+    const int64_t runs = packed_weight_bytes(N, K) / 16;
+    pack_weight_kernel<<<static_cast<unsigned>((runs + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        w, N, K, ldw, w_packed, packed_cols(K), runs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "pack launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -682,12 +735,12 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
     void *scratch = nullptr;
     rc = noalloc_scratch(dev, &scratch);
     if (rc) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (K > 0) {
+        // 64 KB of counters + 2 * grid * 64 * 128 * 4 bytes of partial tiles (9.7 MB for 148
+        // SMs) + 3 digit planes of M x Kp bytes + M row scales: for M = 64 the array holds K up
+        // to about 36,000 on a 148-SM part.
         const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
-        const size_t need = tc_workspace_bytes(pl.nt, pl.grid);
-        // 64 KB of counters + 2 * grid * 64 * 128 * 4 bytes of partial tiles (M <= 64, token tile 64):
-        // more than the array only for a grid above (12 MiB - 64 KB) / 64 KB = 191 SMs.
+        const size_t need = tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K);
         if (need > static_cast<size_t>(LSE_NOALLOC_SCRATCH_BYTES)) {
             std::snprintf(t_last_error, sizeof(t_last_error),
                           "lse_int8_linear_packed_noalloc: this shape needs %zu scratch bytes, the fixed array "
@@ -695,13 +748,9 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
                           need, LSE_NOALLOC_SCRATCH_BYTES);
             return LSE_ERR_WORKSPACE;
         }
-        // The stream-K arrival counters must start at zero; partial tiles need no clearing.
-        const long long sk_tiles = static_cast<long long>(pl.tiles) - pl.dp_tiles;
-        if (sk_tiles > 0) {
-            const cudaError_t e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(sk_tiles) * sizeof(int), st);
-            if (e != cudaSuccess) { set_cuda_error(e, "cudaMemsetAsync(no-alloc counters)"); return LSE_ERR_CUDA; }
-        }
     }
+    // The split kernel that precedes the projection clears the stream-K counters it uses, so
+    // nothing of an earlier call's contents is relied upon.
     return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, scratch, LSE_NOALLOC_SCRATCH_BYTES,
                        LSE_ALGO_TCGEN05, true, stream);
 }
@@ -742,7 +791,7 @@ extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K,
 // ---------------------------------------------------------------------------------------
 // lse_int8_gate_up_silu_packed_ws: the same for any M, with a workspace: M <= 16 on the
 // decode kernel (workspace unused), larger M on the tensor-core kernel with SiLU * mul in its
-// epilogue (tc_gemm_i8.cuh, SILU = true).
+// epilogue (tc_i8.cuh, SILU = true), after the activation split.
 // ---------------------------------------------------------------------------------------
 extern "C" int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t ldx,
                                                const int8_t *w_packed, const float *scale, int64_t I, void *y,
@@ -768,11 +817,10 @@ extern "C" int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t
     }
     const int64_t N = 2 * I;
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
-    if (!workspace || !aligned16(workspace) || workspace_bytes < tc_workspace_bytes(pl.nt, pl.grid))
+    if (!workspace || !aligned16(workspace) ||
+        workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;
-    if (pl.nt == 64)
-        return launch_tc<64, true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
-    return launch_tc<128, true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
+    return run_tc_i8<true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
 }
 
 // ---------------------------------------------------------------------------------------

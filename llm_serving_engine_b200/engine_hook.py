@@ -23,22 +23,21 @@ import functools
 
 import torch
 
-from . import ops
 from .int8_linear import quantize_llama_
 
 __all__ = ["enable_int8", "install", "uninstall", "installed"]
 
 
 def enable_int8(runner, lm_head: bool = False):
-    """Swap a loaded `ModelRunner`'s projections to int8 in place and prepare its device for
-    graph capture.  `runner.model` is the Llama-family model the runner loaded; every
-    decoder layer's q/k/v (one fused int8 QKV), o_proj and MLP become int8 (`quantize_llama_`),
-    and the lm_head too with `lm_head=True`."""
+    """Swap a loaded `ModelRunner`'s projections to int8 in place.  `runner.model` is the
+    Llama-family model the runner loaded; every decoder layer's q/k/v (one fused int8 QKV),
+    o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`.
+    Nothing else needs preparing: the ops hold no per-stream state, so the engine's graph
+    captures on any stream record them as they are."""
     device = torch.device(runner.device)
     if device.type != "cuda":
         raise RuntimeError(f"int8 weight-only quantization needs a CUDA device, got {runner.device!r}")
     quantize_llama_(runner.model, lm_head=lm_head)
-    ops.prepare_graph_capture(device)
     return runner
 
 

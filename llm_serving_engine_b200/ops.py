@@ -8,15 +8,12 @@ validated on the host and raise `ValueError` / `RuntimeError` before anything la
 way the reference surfaces load-time refusals (`model_runner.py:77-94`).
 
 Graph capture: the op launches on `torch.cuda.current_stream()`, never synchronizes and
-never allocates outside the torch caching allocator (the output), so the reference's decode
-and piecewise CUDA-graph captures (`decode_graph.py:87-116`, `piecewise_graph.py:71-109`)
-record it like any other kernel.  The one piece of state is a per-(device, stream) workspace,
-created zeroed on first use.  Creating it inside a capture is refused (its zeroing would
-run only when the graph replays), so it must exist before a capture starts.  The reference
-warms up on `graph_warmup_stream` but captures on the stream `torch.cuda.graph` makes for
-itself (`torch.cuda.graph.default_capture_stream`, used when no stream is passed, as both
-of the engine's captures do); `prepare_graph_capture(device)`, run at the first op call on
-a device, creates that stream and its workspace.
+never allocates outside the torch caching allocator, so the reference's decode and piecewise
+CUDA-graph captures (`decode_graph.py:87-116`, `piecewise_graph.py:71-109`) record it like
+any other kernel.  The tensor-core path's scratch (stream-K counters and partial tiles, the
+activation digit planes) is taken from the caching allocator on every call, like the
+output: the library initialises what it uses, so the block may be any earlier tensor's, on
+any stream, inside a capture or not, and nothing persists between calls.
 """
 
 from __future__ import annotations
@@ -41,8 +38,7 @@ __all__ = [
     "rope_kv_write",
     "rms_norm",
     "pool_slot_offsets",
-    "workspace_for",
-    "prepare_graph_capture",
+    "linear_workspace",
     "device_status",
     "ALGO_AUTO",
     "ALGO_GEMV",
@@ -57,11 +53,8 @@ ALGO_SKINNY = _lib.ALGO_SKINNY
 
 _DTYPE_CODES = {torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16, torch.float32: _lib.DT_F32}
 
-# One workspace per (device, stream): calls on one stream are ordered, calls on different
-# streams never share scratch.  Sized for the largest token tile, so it never grows.
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
-_ws_lock = threading.Lock()
 _inited: set[int] = set()
+_ws_lock = threading.Lock()
 
 
 def _ensure_device(device: torch.device) -> None:
@@ -69,47 +62,16 @@ def _ensure_device(device: torch.device) -> None:
     if idx not in _inited:
         _lib.check(_lib.load().lse_init(idx), f"lse_init(cuda:{idx})")
         _inited.add(idx)
-        if not torch.cuda.is_current_stream_capturing():
-            prepare_graph_capture(torch.device("cuda", idx))
 
 
-def prepare_graph_capture(device: torch.device | int | None = None) -> None:
-    """Create, outside any capture, the workspace of the stream `torch.cuda.graph` captures
-    on when it is given none (`torch.cuda.graph.default_capture_stream`, made here if no graph
-    has been captured yet), so that the reference's decode and piecewise captures record only
-    kernel launches.  Runs once per device at the first op call; a capture on any other
-    stream needs one eager op call (or `workspace_for(device, stream)`) on that stream first."""
-    if device is None:
-        device = torch.device("cuda", torch.cuda.current_device())
-    elif isinstance(device, int):
-        device = torch.device("cuda", device)
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    with torch.cuda.device(idx):
-        if torch.cuda.graph.default_capture_stream is None:
-            torch.cuda.graph(torch.cuda.CUDAGraph())  # constructing it creates the class's default capture stream
-        stream = torch.cuda.graph.default_capture_stream
-        if stream.device.index == idx:
-            workspace_for(torch.device("cuda", idx), stream)
-
-
-def workspace_for(device: torch.device, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """The zero-initialised scratch buffer calls on (device, stream) share."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    stream = stream if stream is not None else torch.cuda.current_stream(idx)
-    key = (idx, stream.cuda_stream)
-    ws = _workspaces.get(key)
-    if ws is None:
-        with _ws_lock:
-            ws = _workspaces.get(key)
-            if ws is None:
-                if torch.cuda.is_current_stream_capturing():
-                    raise RuntimeError(
-                        "int8_linear: first call on this stream happened inside a CUDA graph capture; "
-                        "run one eager call on the capture stream first, or ops.workspace_for(device, stream)")
-                nbytes = int(_lib.load().lse_int8_linear_workspace(1 << 20, 1, 1))
-                ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
-                _workspaces[key] = ws
-    return ws
+def linear_workspace(M: int, K: int, N: int, device: torch.device, algo: int = _lib.ALGO_AUTO,
+                     packed: bool = True) -> torch.Tensor | None:
+    """Scratch for one call (None when the chosen kernel needs none): a fresh block of the
+    torch caching allocator on the current stream, its contents irrelevant to the library."""
+    nbytes = int(_lib.load().lse_int8_linear_workspace_for(M, K, N, int(algo), 1 if packed else 0))
+    if nbytes == 0:
+        return None
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
 def _check_x(x: torch.Tensor, K: int, *tensors: torch.Tensor) -> None:
@@ -150,19 +112,20 @@ def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, ou
         return y
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
-    ws = workspace_for(x.device, stream)
+    ws = linear_workspace(M, K, N, x.device, algo, packed)
+    ws_ptr, ws_bytes = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     lib = _lib.load()
     if r2 is not None:
         if r2.data_ptr() == y2.data_ptr() and r2.stride(0) != y2.stride(0):
             raise ValueError("int8_linear: residual and out overlap with different strides")
         rc = lib.lse_int8_linear_packed_residual(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N,
                                                  r2.data_ptr(), r2.stride(0), y2.data_ptr(), y2.stride(0),
-                                                 ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
+                                                 ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
         _lib.check(rc, "lse_int8_linear_packed_residual")
         return y
     fn = lib.lse_int8_linear_packed if packed else lib.lse_int8_linear_ex
     rc = fn(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N, y2.data_ptr(), y2.stride(0),
-            ws.data_ptr(), ws.numel(), int(algo), stream.cuda_stream)
+            ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
     _lib.check(rc, "lse_int8_linear_packed" if packed else "lse_int8_linear")
     return y
 
@@ -270,7 +233,7 @@ def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: tor
                                               scale.data_ptr(), I, out.data_ptr(), I, stream.cuda_stream)
         _lib.check(rc, "lse_int8_gate_up_silu_packed")
         return out
-    ws = workspace_for(x.device, stream)
+    ws = linear_workspace(M, K, 2 * I, x.device)
     rc = lib.lse_int8_gate_up_silu_packed_ws(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
                                              scale.data_ptr(), I, out.data_ptr(), I, ws.data_ptr(), ws.numel(),
                                              stream.cuda_stream)
@@ -441,7 +404,8 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
 
 def device_status(device: int | torch.device | None = None, reset: bool = True) -> int:
     """Synchronize and read the device-side status (LSE_OK or LSE_ERR_DEVICE_TIMEOUT).  After a
-    timeout the workspaces of that device are re-zeroed."""
+    timeout the decode-attention workspaces of that device are re-zeroed (the linear
+    workspaces need nothing: each call initialises its own)."""
     if device is None:
         idx = torch.cuda.current_device()
     elif isinstance(device, torch.device):
@@ -450,7 +414,7 @@ def device_status(device: int | torch.device | None = None, reset: bool = True) 
         idx = int(device)
     st = int(_lib.load().lse_device_status(idx, 1 if reset else 0))
     if st == _lib.LSE_ERR_DEVICE_TIMEOUT:
-        for (d, _), ws in _workspaces.items():
+        for (d, _), ws in _attn_ws.items():
             if d == idx:
                 ws.zero_()
     return st

@@ -123,18 +123,22 @@ def ref_mlp(x: np.ndarray, q_gate, s_gate, q_up, s_up, q_down, s_down) -> np.nda
 
 
 def ref_pack_weight(q: np.ndarray) -> np.ndarray:
-    """The build's fragment-major weight layout, restated with numpy (checker for the pack
-    kernel).  W is zero padded to multiples of 128 in both dimensions; for row block rb (16
-    rows) and 32-column chunk kc, the 512-byte chunk at (rb*KC + kc)*512 holds
-    W[rb*16 + rr*8 + r0][kc*32 + h*16 + 4*qq + e] at byte (4*r0 + qq)*16 + h*8 + rr*4 + e."""
+    """The build's packed weight layout, restated with numpy (checker for the pack kernel).
+    W is zero padded to multiples of 128 in both dimensions and cut into groups of 8 rows; group
+    g is a run of 8*Kp bytes of 512-byte atoms, one per 64 columns, each holding its 8 rows' 64
+    columns 64 bytes per row, the 16-byte chunk c of row r stored at chunk position
+    c ^ ((r >> 1) & 3) (plain two's-complement bytes):
+    W[8g + r][64a + 16c + e] at g*8*Kp + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e."""
     N, K = q.shape
     Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
     pad = np.zeros((Np, Kp), dtype=np.int8)
     pad[:N, :K] = q
-    RB, KC = Np // 16, Kp // 32
-    # axes: rb, rr, r0, kc, h, qq, e  ->  rb, kc, r0, qq, h, rr, e
-    v = pad.reshape(RB, 2, 8, KC, 2, 4, 4).transpose(0, 3, 2, 5, 4, 1, 6)
-    return (v.reshape(-1).view(np.uint8) ^ np.uint8(0x80)).view(np.int8).copy()
+    # axes: g, r, a, c, e  ->  g, a, r, c', e  with the stored chunk position c' = c ^ ((r >> 1) & 3)
+    v = pad.reshape(Np // 8, 8, Kp // 64, 4, 16).transpose(0, 2, 1, 3, 4)
+    out = np.empty_like(v)
+    for r in range(8):
+        out[:, :, r, np.arange(4) ^ ((r >> 1) & 3), :] = v[:, :, r, :, :]
+    return out.reshape(-1)
 
 
 def parity_errors(y: np.ndarray, ref: np.ndarray) -> tuple[float, bool, float]:

@@ -11,21 +11,33 @@ from oracle.ref_linear import parity_errors, ref_int8_linear
 
 
 class Workspace:
-    """A zeroed scratch buffer for lse_int8_linear plus a guard band to catch overruns."""
+    """Scratch for the C ABI's linear calls, grown to each call's need, plus a guard band after
+    the needed bytes to catch overruns.  The library requires nothing of its contents; the
+    buffer is filled with garbage (0xA5) so that a call relying on zeroed memory would fail."""
 
     GUARD = 4096
 
     def __init__(self, device="cuda"):
-        self.nbytes = int(_lib.load().lse_int8_linear_workspace(1 << 20, 1, 1))
-        self.buf = torch.zeros(self.nbytes + self.GUARD, dtype=torch.uint8, device=device)
-        self.buf[self.nbytes:] = 0xA5
+        self.device = device
+        self.nbytes = 0
+        self.buf = torch.full((self.GUARD,), 0xA5, dtype=torch.uint8, device=device)
+
+    def ensure(self, M: int, K: int, N: int) -> "Workspace":
+        need = int(_lib.load().lse_int8_linear_workspace(M, K, N))
+        if need > self.nbytes:
+            self.nbytes = need
+            self.buf = torch.full((need + self.GUARD,), 0xA5, dtype=torch.uint8, device=self.device)
+        return self
 
     @property
     def ptr(self) -> int:
         return self.buf.data_ptr()
 
     def counters_clear(self) -> bool:
-        return bool((self.buf[:_lib.WS_COUNTER_BYTES] == 0).all().item())
+        """Every stream-K counter a call used is back at zero (the last arriver re-arms it);
+        counters no call used still hold the fill pattern."""
+        head = self.buf[:_lib.WS_COUNTER_BYTES]
+        return bool(((head == 0) | (head == 0xA5)).all().item())
 
     def guard_intact(self) -> bool:
         return bool((self.buf[self.nbytes:] == 0xA5).all().item())
@@ -38,6 +50,7 @@ def abi_linear(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, ws: Workspace,
     M = x.shape[0]
     N, K = w.shape
     ldx = x.stride(0) if ldx is None else ldx
+    ws.ensure(M, K, N)
     if y is None:
         y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     ldy = y.stride(0) if ldy is None else ldy

@@ -232,6 +232,7 @@ def test_pack_kernel_matches_layout_restatement(N, K):
 
 def _packed_call(x, packed, s, N, K, ws, algo, y=None, ldy=None):
     M = x.shape[0]
+    ws.ensure(M, K, N)
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda") if y is None else y
     ldy = y.stride(0) if ldy is None else ldy
     rc = _lib.load().lse_int8_linear_packed(x.data_ptr(), M, K, x.stride(0), packed.data_ptr(), s.data_ptr(), N,
@@ -388,7 +389,7 @@ def test_gate_up_silu_ws_limits():
     w = torch.zeros(ops.packed_weight_bytes(64, 64), dtype=torch.int8, device="cuda")
     s = torch.ones(64, device="cuda")
     y = torch.empty(40, 32, dtype=torch.bfloat16, device="cuda")
-    ws = ops.workspace_for(x.device)
+    ws = torch.empty(int(lib.lse_int8_linear_workspace(40, 64, 64)), dtype=torch.uint8, device="cuda")
     assert lib.lse_int8_gate_up_silu_packed_ws(x.data_ptr(), 40, 64, 64, w.data_ptr(), s.data_ptr(), 32, y.data_ptr(),
                                                32, None, 0, st) == _lib.LSE_ERR_WORKSPACE
     assert lib.lse_int8_gate_up_silu_packed_ws(x.data_ptr(), 40, 64, 64, w.data_ptr(), s.data_ptr(), 20, y.data_ptr(),
@@ -484,7 +485,7 @@ def test_residual_argument_errors():
     wp = torch.zeros(ops.packed_weight_bytes(64, 64), dtype=torch.int8, device="cuda")
     s = torch.ones(64, device="cuda")
     y = torch.empty(4, 64, dtype=torch.bfloat16, device="cuda")
-    ws = ops.workspace_for(x.device)
+    ws = torch.empty(int(lib.lse_int8_linear_workspace(4, 64, 64)), dtype=torch.uint8, device="cuda")
     args = (x.data_ptr(), 4, 64, 64, wp.data_ptr(), s.data_ptr(), 64)
     tail = (ws.data_ptr(), ws.numel(), ops.ALGO_AUTO, st)
     assert lib.lse_int8_linear_packed_residual(*args, None, 64, y.data_ptr(), 64, *tail) == _lib.LSE_ERR_INVALID_ARG

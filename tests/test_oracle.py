@@ -192,3 +192,24 @@ def test_attention_oracle_matches_torch_sdpa_in_float64():
         ref = F.scaled_dot_product_attention(torch.from_numpy(q[e])[None, :, None], k, v, enable_gqa=True)
         np.testing.assert_allclose(out[e], ref[0, :, 0].numpy(), rtol=1e-12, atol=1e-12)
     assert np.all(ref_paged_decode_attention(q, k_pool, v_pool, bt, np.array([0, 0, 0])) == 0)
+
+
+def test_pack_layout_restatement_places_every_byte():
+    """The packed layout's checker puts W[n, k] at (n // 8) * 8 * Kp + (k // 64) * 512 +
+    (n % 8) * 64 + ((k // 16 % 4) ^ (n % 8 // 2)) * 16 + k % 16, with zero padding to multiples
+    of 128: the 64-byte-swizzled K-major atoms the tensor core reads as its operand and the
+    decode kernel's fragments come from."""
+    from oracle.ref_linear import ref_pack_weight
+
+    rng = np.random.default_rng(5)
+    for N, K in ((8, 16), (130, 200), (256, 384)):
+        w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+        p = ref_pack_weight(w)
+        Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
+        assert p.shape == (Np * Kp,)
+        n, k = np.meshgrid(np.arange(N), np.arange(K), indexing="ij")
+        off = (n // 8) * 8 * Kp + (k // 64) * 512 + (n % 8) * 64 + (((k // 16) % 4) ^ ((n % 8) // 2)) * 16 + k % 16
+        assert np.array_equal(p[off], w)
+        mask = np.ones(Np * Kp, dtype=bool)
+        mask[off.ravel()] = False
+        assert not p[mask].any()

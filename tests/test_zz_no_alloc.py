@@ -33,6 +33,7 @@ def _noalloc(x: torch.Tensor, packed: torch.Tensor, s: torch.Tensor, N: int, K: 
 
 
 def _existing(x, packed, s, N, K, ws: Workspace) -> torch.Tensor:
+    ws.ensure(x.shape[0], K, N)
     y = torch.empty((x.shape[0], N), dtype=torch.bfloat16, device=x.device)
     rc = _lib.load().lse_int8_linear_packed(x.data_ptr(), x.shape[0], K, x.stride(0), packed.data_ptr(), s.data_ptr(),
                                             N, y.data_ptr(), y.stride(0), ws.ptr, ws.nbytes, _lib.ALGO_TCGEN05,
