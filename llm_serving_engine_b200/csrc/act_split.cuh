@@ -21,8 +21,8 @@
 // (zeros for K <= k < Kp), K-contiguous: the kernel's tensor map reads a box of
 // [S planes][token tile][128 K bytes] as one K-major B operand of S * NT rows.
 //
-// One CTA per row; CTA 0 also clears the stream-K arrival counters of the projection launch
-// that follows.  Programmatic dependent launch: the CTA releases its dependents on entry (the
+// One CTA per row, every load of the row in flight at once (up to 16,384 elements); CTA 0 also
+// clears the stream-K arrival counters of the projection launch that follows.  Programmatic dependent launch: the CTA releases its dependents on entry (the
 // projection kernel's weight copies start under it) and waits for the kernel that wrote x
 // before touching any memory.
 #pragma once
@@ -59,6 +59,35 @@ __device__ __forceinline__ void digits_of(int v, uint32_t (&d)[S], int slot) {
     }
 }
 
+// Chunks of 8 elements each thread keeps in registers: a row of up to THREADS * CPT * 8 =
+// 16,384 elements is read once, with every load in flight together; a longer row is read in
+// batches of that size (twice: once for the maximum, once for the digits).
+constexpr int CPT = 8;
+
+template <int S>
+__device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_t plane_stride, int64_t row_off, int c,
+                                             const uint4 &v, int e, bool valid) {
+    uint32_t d0[S] = {}, d1[S] = {};
+    if (valid) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float f = h ? bf16_hi(w[i]) : bf16_lo(w[i]);
+                int q = static_cast<int>(rintf(ldexpf(f, -e)));
+                q = max(-Digits<S>::kMaxV, min(Digits<S>::kMaxV, q));
+                const int slot = 2 * i + h;
+                if (slot < 4) digits_of<S>(q, d0, slot);
+                else digits_of<S>(q, d1, slot);
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < S; ++p)
+        *reinterpret_cast<uint2 *>(planes + p * plane_stride + row_off + 8 * c) = make_uint2(d0[p], d1[p]);
+}
+
 template <int S>
 __global__ void __launch_bounds__(THREADS)
 act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *__restrict__ planes,
@@ -72,16 +101,25 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
         for (int i = threadIdx.x; i < n_counters; i += THREADS) counters[i] = 0;
     const __nv_bfloat16 *xr = x + static_cast<int64_t>(m) * ldx;
     const int nk = K >> 3;  // 8-element chunks (K % 16 == 0, rows 16-byte aligned)
+    constexpr int BATCH = THREADS * CPT;
+    uint4 v[CPT];
     float amax = 0.f;
     bool bad = false;
-    for (int c = threadIdx.x; c < nk; c += THREADS) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c));
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int base = 0; base < nk; base += BATCH) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float a = fabsf(bf16_lo(w[i])), b = fabsf(bf16_hi(w[i]));
-            bad |= !(a <= 3.4e38f) || !(b <= 3.4e38f);  // NaN or infinity
-            amax = fmaxf(amax, fmaxf(a, b));
+        for (int i = 0; i < CPT; ++i) {
+            const int c = base + threadIdx.x + i * THREADS;
+            v[i] = c < nk ? __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float a = fabsf(bf16_lo(w[k])), b = fabsf(bf16_hi(w[k]));
+                bad |= !(a <= 3.4e38f) || !(b <= 3.4e38f);  // NaN or infinity
+                amax = fmaxf(amax, fmaxf(a, b));
+            }
         }
     }
     __shared__ float s_max[THREADS / 32];
@@ -109,29 +147,23 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
         e = ilogbf(amax) - Digits<S>::kTopExp;
         if (ldexpf(amax, -e) > static_cast<float>(Digits<S>::kMaxV)) ++e;  // an all-ones mantissa
     }
-    // digits: 8 elements per chunk -> S planes x 8 bytes
-    for (int c = threadIdx.x; c < (Kp >> 3); c += THREADS) {
-        uint32_t d0[S] = {}, d1[S] = {};
-        if (c < nk && !bad) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c));
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    // digits: 8 elements per chunk -> S planes x 8 bytes; a row that fits one batch is still
+    // in registers
+    const int64_t row_off = static_cast<int64_t>(m) * Kp;
+    const int nkp = Kp >> 3;
+    for (int base = 0; base < nkp; base += BATCH) {
+        if (nk > BATCH) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const float f = h ? bf16_hi(w[i]) : bf16_lo(w[i]);
-                    int q = static_cast<int>(rintf(ldexpf(f, -e)));
-                    q = max(-Digits<S>::kMaxV, min(Digits<S>::kMaxV, q));
-                    const int slot = 2 * i + h;
-                    if (slot < 4) digits_of<S>(q, d0, slot);
-                    else digits_of<S>(q, d1, slot);
-                }
+            for (int i = 0; i < CPT; ++i) {
+                const int c = base + threadIdx.x + i * THREADS;
+                v[i] = c < nk ? __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c)) : make_uint4(0, 0, 0, 0);
             }
         }
 #pragma unroll
-        for (int p = 0; p < S; ++p)
-            *reinterpret_cast<uint2 *>(planes + p * plane_stride + static_cast<int64_t>(m) * Kp + 8 * c) =
-                make_uint2(d0[p], d1[p]);
+        for (int i = 0; i < CPT; ++i) {
+            const int c = base + threadIdx.x + i * THREADS;
+            if (c < nkp) store_digits<S>(planes, plane_stride, row_off, c, v[i], e, c < nk && !bad);
+        }
     }
     if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);
 }

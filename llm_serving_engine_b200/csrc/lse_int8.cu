@@ -276,8 +276,8 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
     }
     // 2) the projection
     CUtensorMap tw, tx;
-    int rc = packed ? encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, static_cast<uint64_t>(Kp),
-                                static_cast<uint64_t>(packed_rows(N) / 8), static_cast<uint64_t>(8 * Kp), 128, 16,
+    int rc = packed ? encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, static_cast<uint64_t>(2 * Kp),
+                                static_cast<uint64_t>(packed_rows(N) / 16), static_cast<uint64_t>(16 * Kp), 256, 8,
                                 CU_TENSOR_MAP_SWIZZLE_NONE)
                     : encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K, N, K, tci8::BK, tci8::BN);
     if (rc) return rc;

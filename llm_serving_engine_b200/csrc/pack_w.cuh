@@ -1,25 +1,30 @@
 // Load-time repack of int8 weights into the layout both kernels stream.
 //
 // W [N, K] (row-major int8) is zero padded to Np = 128*ceil(N/128) rows and
-// Kp = 128*ceil(K/128) columns and cut into groups of 8 rows.  Group g (rows 8g..8g+7) is ONE
-// contiguous run of 8 * Kp bytes made of 512-byte atoms, one per 64 columns; an atom holds
-// its 8 rows' 64 columns, 64 bytes per row, with the 16-byte chunks of row r swapped by the
-// tensor core's 64-byte swizzle (chunk c of row r stored at chunk position c ^ ((r >> 1) & 3)):
+// Kp = 128*ceil(K/128) columns and cut into row blocks of 16 rows.  Row block b (rows
+// 16b..16b+15) is ONE contiguous run of 16 * Kp bytes made of 2 KB blocks, one per 128
+// columns; a 2 KB block holds the block's two 8-row groups (h = 0: rows 16b..16b+7, h = 1:
+// the next 8) one after the other, each as two 512-byte atoms of 64 columns; an atom holds its
+// 8 rows' 64 columns, 64 bytes per row, with the 16-byte chunks of row r swapped by the tensor
+// core's 64-byte swizzle (chunk c of row r stored at chunk position c ^ ((r >> 1) & 3)):
 //
-//   W[8g + r][64a + 16c + e]  at  g * 8 * Kp + a * 512 + r * 64 + ((c ^ ((r >> 1) & 3)) * 16) + e
+//   W[16b + 8h + r][128t + 64a + 16c + e]  at
+//       b * 16 * Kp + t * 2048 + h * 1024 + a * 512 + r * 64 + ((c ^ ((r >> 1) & 3)) * 16) + e
 //
-//   (r < 8, c < 4, e < 16).  Bytes are the plain two's-complement int8 values.
+//   (h, a < 2, r < 8, c < 4, e < 16).  Bytes are the plain two's-complement int8 values.
 //
 // Why this order:
-//   * a 128 x 128 tile (16 groups x 2 atoms, 16 runs of 1 KB) is the tensor core's canonical
-//     K-major operand with the 64-byte swizzle (8-row groups 1 KB apart): the tensor-core kernel
-//     hands it to tcgen05.mma kind::i8 as its A operand straight from shared memory, after one
-//     2-D bulk-tensor copy (8-byte elements, box 128 x 16);
+//   * a 128 x 128 tile (8 row blocks x 2 KB) is the tensor core's canonical K-major operand
+//     with the 64-byte swizzle (8-row groups 1 KB apart, the second 64 columns of a group 512
+//     bytes on): the tensor-core kernel hands it to tcgen05.mma kind::i8 as its A operand
+//     straight from shared memory, after one 2-D bulk-tensor copy (8-byte elements, box
+//     256 x 8: eight runs of 2 KB);
 //   * for the decode kernel, lane 4 * r0 + q of a warp loads row r0's 16 columns 16q..16q+15 of
 //     an atom with one 128-bit load; the swizzle keeps the four lanes of a row on its 64
 //     contiguous bytes and the eight lanes of two rows on one 128-byte line, so a warp load is
-//     512 contiguous bytes in 4 line requests.  The matching load in the next group gets row
-//     r0 + 8's.  Word j of those 16 bytes (columns 16q + 4j .. +3, rows r0 and r0 + 8) is the A
+//     512 contiguous bytes in 4 line requests.  The matching load 1 KB on (the row block's
+//     second group) gets row r0 + 8's, so a warp streams one contiguous run per row block.
+//     Word j of those 16 bytes (columns 16q + 4j .. +3, rows r0 and r0 + 8) is the A
 //     fragment of the j-th 16x8x16 warp MMA of the atom, taking the columns 16q + 4j + e for
 //     the fragment's K pairs (2q, 2q+1) and (2q+8, 2q+9) - a fixed permutation of K inside each
 //     64-column block, applied to the activations too, so the dot product is unchanged.
@@ -39,8 +44,13 @@ __host__ __device__ inline int64_t packed_weight_bytes(int64_t N, int64_t K) { r
 // Byte offset of W[n][k] in the packed buffer (Kp = packed_cols(K)).
 __host__ __device__ inline int64_t packed_offset(int64_t n, int64_t k, int64_t Kp) {
     const int r = static_cast<int>(n & 7), c = static_cast<int>((k >> 4) & 3);
-    return (n >> 3) * 8 * Kp + (k >> 6) * 512 + r * 64 + ((c ^ ((r >> 1) & 3)) << 4) + (k & 15);
+    return (n >> 4) * 16 * Kp + (k >> 7) * 2048 + ((n >> 3) & 1) * 1024 + ((k >> 6) & 1) * 512 + r * 64 +
+           ((c ^ ((r >> 1) & 3)) << 4) + (k & 15);
 }
+
+// Byte offset of 64-column unit u (u = k / 64) inside a row block's run: 2 KB per two units,
+// the odd unit 512 bytes into the pair's block; the block's second group is 1 KB further on.
+__host__ __device__ inline int64_t packed_unit_offset(int64_t u) { return (u >> 1) * 2048 + (u & 1) * 512; }
 
 // One thread per 16-byte row run (16 consecutive columns of one row); consecutive threads take
 // consecutive runs of the same row, so the reads are coalesced.

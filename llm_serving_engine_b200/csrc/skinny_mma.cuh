@@ -8,8 +8,9 @@
 //   * one CTA of KW warps owns R blocks of 16 output channels over all of K; warp w takes a
 //     contiguous slice of each block's 64-column units;
 //   * a unit is two 128-bit streaming loads per lane (L1 no-allocate, L2 evict-first) that
-//     read 512 contiguous bytes each per warp, four 128-byte lines: row r0's 16 columns
-//     16q..16q+15 of the unit and row r0 + 8's (lane 4 * r0 + q).  Word j of the two loads is
+//     read 512 contiguous bytes each per warp, four 128-byte lines, 1 KB apart: row r0's 16
+//     columns 16q..16q+15 of the unit and row r0 + 8's (lane 4 * r0 + q); a warp's slice of
+//     a row block is one contiguous run (pack_w.cuh).  Word j of the two loads is
 //     the A fragment of the unit's j-th 16x8x16 warp MMA (pack_w.cuh), so there is no
 //     shared-memory staging, no copy bookkeeping and no wait on a barrier.  U loads per row
 //     block (U / 2 units) are kept in flight per lane, issued before the previous kernel is
@@ -35,6 +36,7 @@
 
 #include <type_traits>
 
+#include "pack_w.cuh"
 #include "tc_ptx.cuh"
 
 namespace lse {
@@ -107,7 +109,9 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = lane >> 2, q = lane & 3;
     const int ku_real = (K + 63) >> 6;  // 64-column units holding real columns
-    const int per = (ku_real + KW - 1) / KW;
+    // an even number of units per warp: a slice then starts on a 2 KB block, and a unit j of a
+    // group of UB (even) sits at the compile-time offset packed_unit_offset(j) from its group
+    const int per = ((ku_real + KW - 1) / KW + 1) & ~1;
     const int c0 = min(ku_real, warp * per), c1 = min(ku_real, c0 + per);
     const int nch = c1 - c0;
     // Whole groups, and every column < K (only the last unit of the row can be partial).
@@ -116,15 +120,18 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     const int rot = fast ? rg % ng : 0;
 
     const uint64_t pol = ptx::policy_evict_first();
-    // Row block rg*R + r (padded rows past N hold zeros) is two 8-row groups, 8 * Kp bytes
-    // each: row block r at wbase + r * rb_bytes, its second group 8 * Kp further on.  Lane
-    // (r0, q) reads row r0's 16-byte chunk q of each 512-byte atom, stored at chunk position
-    // q ^ ((r0 >> 1) & 3) (pack_w.cuh), so eight consecutive lanes read one 128-byte line.
+    // Row block rg*R + r (padded rows past N hold zeros) is one run of 16 * Kp bytes at
+    // row_base + r * rb_bytes; unit u of it at packed_unit_offset(u), its second 8-row group
+    // 1 KB further on.  Lane (r0, q) reads row r0's 16-byte chunk q of each 512-byte atom,
+    // stored at chunk position q ^ ((r0 >> 1) & 3), so eight consecutive lanes read one
+    // 128-byte line.
     const int64_t rb_bytes = static_cast<int64_t>(Kp) * 16;
-    const int64_t grp_bytes = static_cast<int64_t>(Kp) * 8;
-    const int8_t *const wbase =
-        wp + static_cast<int64_t>(rg) * R * rb_bytes + c0 * 512 + r0 * 64 + ((q ^ ((r0 >> 1) & 3)) << 4);
-    const int8_t *gp = wbase + rot * (UB * 512);
+    constexpr int64_t grp_bytes = 1024;
+    const int8_t *const row_base = wp + static_cast<int64_t>(rg) * R * rb_bytes;
+    const int8_t *const lane_base = row_base + r0 * 64 + ((q ^ ((r0 >> 1) & 3)) << 4);
+    // first unit of slice group gv (groups start on even units when UB is even)
+    auto group_ptr = [&](int gv) { return lane_base + packed_unit_offset(c0 + gv * UB); };
+    const int8_t *gp = group_ptr(rot);
     uint4 wb[UB][R][2];
 #pragma unroll
     for (int j = 0; j < UB; ++j)
@@ -132,20 +139,22 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
         for (int r = 0; r < R; ++r)
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-                wb[j][r][h] = (fast || j < nch) ? ld_weight16(gp + r * rb_bytes + h * grp_bytes + j * 512, pol)
-                                                : make_uint4(0, 0, 0, 0);
-    // L2 prefetch of the group `v` visits ahead (lane 0, one bulk prefetch per 8-row group): the
-    // register loads then hit L2, so the registers hold only UB units while DRAM has pf_groups
-    // more groups per row block in flight.
+                wb[j][r][h] = (fast || j < nch)
+                                  ? ld_weight16((fast ? gp + packed_unit_offset(j) : lane_base + packed_unit_offset(c0 + j)) +
+                                                    r * rb_bytes + h * grp_bytes, pol)
+                                  : make_uint4(0, 0, 0, 0);
+    // L2 prefetch of the group `v` visits ahead (lane 0, one bulk prefetch per row block of the
+    // 2 KB blocks holding the group's units): the register loads then hit L2, so the registers
+    // hold only UB units while DRAM has pf_groups more groups per row block in flight.
     auto prefetch_group = [&](int v) {
         if (lane == 0 && v < ng) {
             int gv = rot + v;
             if (gv >= ng) gv -= ng;
-            const int8_t *base = wp + static_cast<int64_t>(rg) * R * rb_bytes + (c0 + gv * UB) * 512;
+            const int u0 = c0 + gv * UB;
+            const int blocks = ((u0 + UB - 1) >> 1) - (u0 >> 1) + 1;
+            const int8_t *base = row_base + static_cast<int64_t>(u0 >> 1) * 2048;
 #pragma unroll
-            for (int r = 0; r < R; ++r)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) ptx::bulk_prefetch_l2(base + r * rb_bytes + h * grp_bytes, UB * 512);
+            for (int r = 0; r < R; ++r) ptx::bulk_prefetch_l2(base + r * rb_bytes, blocks * 2048);
         }
     };
     if (fast)
@@ -237,7 +246,8 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     w[r][h] = wb[j][r][h];
-                    if constexpr (REFILL) wb[j][r][h] = ld_weight16(np + r * rb_bytes + h * grp_bytes + j * 512, pol);
+                    if constexpr (REFILL)
+                        wb[j][r][h] = ld_weight16(np + packed_unit_offset(j) + r * rb_bytes + h * grp_bytes, pol);
                 }
             compute(w, j, true);
         }
@@ -248,7 +258,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
         for (int g = 0; g < ng; ++g) {
             if (pf_groups > 0) prefetch_group(g + pf_groups + 1);
             const bool wrap = gi + 1 == ng;  // the next group in the rotated order is group 0
-            const int8_t *np = wrap ? wbase : gp + UB * 512;
+            const int8_t *np = group_ptr(wrap ? 0 : gi + 1);
             if (g + 1 < ng) group(np, std::true_type{});
             else group(np, std::false_type{});
             gp = np;
@@ -271,13 +281,14 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                         for (int h = 0; h < 2; ++h) {
                             w[r][h] = wb[j][r][h];
                             if (c + j + UB < nch)
-                                wb[j][r][h] = ld_weight16(gp + r * rb_bytes + h * grp_bytes + (UB + j) * 512, pol);
+                                wb[j][r][h] = ld_weight16(lane_base + packed_unit_offset(c0 + c + UB + j) + r * rb_bytes +
+                                                              h * grp_bytes,
+                                                          pol);
                         }
                     const bool col_ok = (c + j) * 64 + 16 * q < kcols;  // K % 16 == 0: all 16 or none
                     compute(w, j, col_ok);
                 }
             }
-            gp += UB * 512;
 #pragma unroll
             for (int t = 0; t < MT; ++t) xp[t] += UB * 64;
         }

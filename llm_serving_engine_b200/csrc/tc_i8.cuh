@@ -17,7 +17,7 @@
 // copy and the accumulator.
 //   * W: row-major int8 [N, K] with a 128-byte swizzle (box 128 K x 128 rows), or the
 //     packed layout (pack_w.cuh: 512-byte atoms of 8 rows x 64 columns stored with the 64-byte
-//     swizzle, K-contiguous per 8-row group; box 16 groups x 1 KB, copied as it is).
+//     swizzle, 2 KB per 16-row block and 128 columns; box 8 row blocks x 2 KB, copied as it is).
 //   * digit planes: int8 [S][M][Kp], one 3-D box [S][NT][128 K] with a 128-byte swizzle.
 //   * D: int32 in tensor memory, double-buffered; four epilogue warps read it (tcgen05.ld),
 //     combine the planes, apply s[n] * r[m] (and the optional residual or SiLU * mul) and
@@ -224,12 +224,13 @@ __device__ __forceinline__ uint64_t policy_w_for(const Params &p) {
 }
 
 // Weight tile (n0 / BN, kb) -> shared memory.  Packed: the tensor map views the buffer as
-// [Np / 8 groups][Kp eight-byte elements] and the box is 128 x 16 (16 groups x 1 KB).
-// Row-major: [N][K] bytes, box 128 x 128, 128-byte swizzle.
+// [Np / 16 row blocks][2 * Kp eight-byte elements] and the box is 256 x 8 (8 row blocks x
+// 2 KB), landing as 16 groups 1 KB apart.  Row-major: [N][K] bytes, box 128 x 128, 128-byte
+// swizzle.
 template <bool WPACK>
 __device__ __forceinline__ void load_w_tile(const CUtensorMap *tmap_w, uint32_t dst, int n0, int kb, uint32_t bar,
                                             uint64_t pol) {
-    if constexpr (WPACK) ptx::tma_load_2d(dst, tmap_w, bar, kb * 128, n0 / 8, pol);
+    if constexpr (WPACK) ptx::tma_load_2d(dst, tmap_w, bar, kb * 256, n0 / 16, pol);
     else ptx::tma_load_2d(dst, tmap_w, bar, kb * BK, n0, pol);
 }
 
@@ -241,8 +242,8 @@ __device__ __forceinline__ void prefetch_w_tile_l2(const Params &p, int n0, int 
     for (int i = 0; i < 4; ++i) {
         const int line = i * 32 + lane;
         if constexpr (WPACK) {
-            const int g = line >> 3;  // 8-row group within the tile, 8 lines of 128 bytes each
-            ptx::prefetch_line_l2(p.w + (static_cast<int64_t>(n0 / 8 + g) * p.kp + kb * BK) * 8 + (line & 7) * 128);
+            const int b = line >> 4;  // row block within the tile, 16 lines of 128 bytes each
+            ptx::prefetch_line_l2(p.w + static_cast<int64_t>(n0 / 16 + b) * 16 * p.kp + kb * 2048 + (line & 15) * 128);
         } else {
             const int r = n0 + line;
             if (r < p.N) ptx::prefetch_line_l2(p.w + static_cast<int64_t>(r) * p.K + kb * BK);

@@ -124,20 +124,22 @@ def ref_mlp(x: np.ndarray, q_gate, s_gate, q_up, s_up, q_down, s_down) -> np.nda
 
 def ref_pack_weight(q: np.ndarray) -> np.ndarray:
     """The build's packed weight layout, restated with numpy (checker for the pack kernel).
-    W is zero padded to multiples of 128 in both dimensions and cut into groups of 8 rows; group
-    g is a run of 8*Kp bytes of 512-byte atoms, one per 64 columns, each holding its 8 rows' 64
-    columns 64 bytes per row, the 16-byte chunk c of row r stored at chunk position
-    c ^ ((r >> 1) & 3) (plain two's-complement bytes):
-    W[8g + r][64a + 16c + e] at g*8*Kp + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e."""
+    W is zero padded to multiples of 128 in both dimensions and cut into row blocks of 16
+    rows; row block b is a run of 16*Kp bytes of 2 KB blocks, one per 128 columns, each holding
+    the block's two 8-row groups (h) one after the other as two 512-byte atoms of 64 columns
+    (a), an atom holding its 8 rows' 64 columns 64 bytes per row with the 16-byte chunk c of row
+    r stored at chunk position c ^ ((r >> 1) & 3) (plain two's-complement bytes):
+    W[16b + 8h + r][128t + 64a + 16c + e] at
+    b*16*Kp + t*2048 + h*1024 + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e."""
     N, K = q.shape
     Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
     pad = np.zeros((Np, Kp), dtype=np.int8)
     pad[:N, :K] = q
-    # axes: g, r, a, c, e  ->  g, a, r, c', e  with the stored chunk position c' = c ^ ((r >> 1) & 3)
-    v = pad.reshape(Np // 8, 8, Kp // 64, 4, 16).transpose(0, 2, 1, 3, 4)
+    # axes: b, h, r, t, a, c, e  ->  b, t, h, a, r, c', e  (stored chunk position c' = c ^ ((r >> 1) & 3))
+    v = pad.reshape(Np // 16, 2, 8, Kp // 128, 2, 4, 16).transpose(0, 3, 1, 4, 2, 5, 6)
     out = np.empty_like(v)
     for r in range(8):
-        out[:, :, r, np.arange(4) ^ ((r >> 1) & 3), :] = v[:, :, r, :, :]
+        out[:, :, :, :, r, np.arange(4) ^ ((r >> 1) & 3), :] = v[:, :, :, :, r, :, :]
     return out.reshape(-1)
 
 

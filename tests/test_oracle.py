@@ -195,10 +195,10 @@ def test_attention_oracle_matches_torch_sdpa_in_float64():
 
 
 def test_pack_layout_restatement_places_every_byte():
-    """The packed layout's checker puts W[n, k] at (n // 8) * 8 * Kp + (k // 64) * 512 +
-    (n % 8) * 64 + ((k // 16 % 4) ^ (n % 8 // 2)) * 16 + k % 16, with zero padding to multiples
-    of 128: the 64-byte-swizzled K-major atoms the tensor core reads as its operand and the
-    decode kernel's fragments come from."""
+    """The packed layout's checker puts W[n, k] at (n // 16) * 16 * Kp + (k // 128) * 2048 +
+    (n // 8 % 2) * 1024 + (k // 64 % 2) * 512 + (n % 8) * 64 + ((k // 16 % 4) ^ (n % 8 // 2)) * 16
+    + k % 16, with zero padding to multiples of 128: the 64-byte-swizzled K-major atoms the
+    tensor core reads as its operand and the decode kernel's fragments come from."""
     from oracle.ref_linear import ref_pack_weight
 
     rng = np.random.default_rng(5)
@@ -208,7 +208,8 @@ def test_pack_layout_restatement_places_every_byte():
         Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
         assert p.shape == (Np * Kp,)
         n, k = np.meshgrid(np.arange(N), np.arange(K), indexing="ij")
-        off = (n // 8) * 8 * Kp + (k // 64) * 512 + (n % 8) * 64 + (((k // 16) % 4) ^ ((n % 8) // 2)) * 16 + k % 16
+        off = ((n // 16) * 16 * Kp + (k // 128) * 2048 + (n // 8 % 2) * 1024 + (k // 64 % 2) * 512 + (n % 8) * 64
+               + (((k // 16) % 4) ^ ((n % 8) // 2)) * 16 + k % 16)
         assert np.array_equal(p[off], w)
         mask = np.ones(Np * Kp, dtype=bool)
         mask[off.ravel()] = False
