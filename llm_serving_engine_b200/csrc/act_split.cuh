@@ -64,9 +64,14 @@ __device__ __forceinline__ void digits_of(int v, uint32_t (&d)[S], int slot) {
 // batches of that size (twice: once for the maximum, once for the digits).
 constexpr int CPT = 8;
 
+// 2^k as a float for an exponent of the normal range [-126, 127] (exact, from the bits).
+__device__ __forceinline__ float exp2_exact(int k) { return __int_as_float((k + 127) << 23); }
+
+// x / 2^e rounded to the nearest integer (ties to even) as inv_hi * inv_lo = 2^-e, each factor a
+// normal power of two, so both multiplications are exact: the quotient is below 2^(8S-1).
 template <int S>
 __device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_t plane_stride, int64_t row_off, int c,
-                                             const uint4 &v, int e, bool valid) {
+                                             const uint4 &v, float inv_hi, float inv_lo, bool valid) {
     uint32_t d0[S] = {}, d1[S] = {};
     if (valid) {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -75,7 +80,7 @@ __device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const float f = h ? bf16_hi(w[i]) : bf16_lo(w[i]);
-                int q = static_cast<int>(rintf(ldexpf(f, -e)));
+                int q = __float2int_rn((f * inv_hi) * inv_lo);
                 q = max(-Digits<S>::kMaxV, min(Digits<S>::kMaxV, q));
                 const int slot = 2 * i + h;
                 if (slot < 4) digits_of<S>(q, d0, slot);
@@ -147,6 +152,10 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
         e = ilogbf(amax) - Digits<S>::kTopExp;
         if (ldexpf(amax, -e) > static_cast<float>(Digits<S>::kMaxV)) ++e;  // an all-ones mantissa
     }
+    // 2^-e split into two normal powers of two (e ranges over about [-155, 106])
+    const int ne = -e;
+    const int ne_hi = max(-126, min(127, ne));
+    const float inv_hi = exp2_exact(ne_hi), inv_lo = exp2_exact(ne - ne_hi);
     // digits: 8 elements per chunk -> S planes x 8 bytes; a row that fits one batch is still
     // in registers
     const int64_t row_off = static_cast<int64_t>(m) * Kp;
@@ -162,7 +171,7 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
             const int c = base + threadIdx.x + i * THREADS;
-            if (c < nkp) store_digits<S>(planes, plane_stride, row_off, c, v[i], e, c < nk && !bad);
+            if (c < nkp) store_digits<S>(planes, plane_stride, row_off, c, v[i], inv_hi, inv_lo, c < nk && !bad);
         }
     }
     if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);

@@ -55,17 +55,46 @@ DeviceState g_dev[kMaxDevices];
 std::once_flag g_encode_once;
 EncodeTiledFn g_encode = nullptr;
 
-template <int NT, int S, bool SILU, bool WPACK>
+template <int NT, int S, bool SILU, bool WPACK, bool CLUSTER>
 cudaError_t set_tci8_attrs() {
-    return cudaFuncSetAttribute(tci8::tc_i8_kernel<NT, S, SILU, WPACK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                tci8::Cfg<NT, S>::SMEM_BYTES);
+    return cudaFuncSetAttribute(tci8::tc_i8_kernel<NT, S, SILU, WPACK, CLUSTER>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, tci8::Cfg<NT, S>::SMEM_BYTES);
 }
 
 template <bool SILU, bool WPACK>
 cudaError_t set_tci8_attrs_all() {
-    cudaError_t e = set_tci8_attrs<64, 3, SILU, WPACK>();
-    if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK>();
+    cudaError_t e = set_tci8_attrs<64, 3, SILU, WPACK, false>();
+    if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK, false>();
+    if (e == cudaSuccess) e = set_tci8_attrs<64, 3, SILU, WPACK, true>();
+    if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK, true>();
     return e;
+}
+
+// How many thread-block clusters of c CTAs of a token-tile configuration can be resident at
+// once on the current device (the cluster plan needs all of its clusters resident in one
+// wave; how many fit depends on how the SMs are grouped, not only on their number).
+constexpr int kMaxCluster = 8;  // portable cluster size
+int g_max_clusters[kMaxDevices][2][kMaxCluster + 1];
+
+template <int NT, int S>
+int query_max_clusters(int c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c * 16);
+    cfg.blockDim = dim3(tci8::NUM_THREADS);
+    cfg.dynamicSmemBytes = tci8::Cfg<NT, S>::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tci8::tc_i8_kernel<NT, S, false, true, true>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();  // not fatal: the plan then splits through global memory
+        return 0;
+    }
+    return n;
 }
 
 int init_device(int device) {
@@ -81,6 +110,11 @@ int init_device(int device) {
         if (e == cudaSuccess) e = set_tci8_attrs_all<false, false>();
         if (e == cudaSuccess) e = set_tci8_attrs_all<false, true>();
         if (e == cudaSuccess) e = set_tci8_attrs_all<true, true>();
+        if (e == cudaSuccess)
+            for (int c = 2; c <= kMaxCluster; ++c) {
+                g_max_clusters[device][0][c] = query_max_clusters<64, 3>(c);
+                g_max_clusters[device][1][c] = query_max_clusters<128, 2>(c);
+            }
         if (e != cudaSuccess) set_cuda_error(e, "device set-up");
         std::call_once(g_encode_once, [] {
             void *fn = nullptr;
@@ -166,9 +200,10 @@ int tc_split_align() {
 struct TcPlan {
     int nt, m_tiles, n_tiles, tiles, kb, dp_tiles, grid;
     long long sk_units;
+    int cluster;  // >= 2: every tile split over the CTAs of one thread-block cluster
 };
 
-TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
+TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms, int dev) {
     TcPlan t{};
     t.nt = token_tile(M);
     t.m_tiles = static_cast<int>((M + t.nt - 1) / t.nt);
@@ -176,6 +211,23 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms) {
     t.tiles = t.m_tiles * t.n_tiles;
     t.kb = static_cast<int>((K + tci8::BK - 1) / tci8::BK);
     int G = num_sms;
+    // Few tiles (decode): split every tile's K range evenly over the c CTAs of one cluster,
+    // reduced through distributed shared memory, with c as large as the SMs allow while all
+    // tiles x c CTAs stay resident together (and every CTA gets at least one 128-K stage).
+    // Measured on B200 at M = 64 (globaltimer trace of the global-memory split): the weight
+    // stream ran at the HBM rate, and the partial publication plus the last arriver's sum
+    // added 6-9 us after the last MMA.
+    if (t.tiles <= G / 2 && dev >= 0) {
+        int c = std::min(std::min(G / t.tiles, kMaxCluster), t.kb);
+        while (c >= 2 && g_max_clusters[dev][t.nt == 128 ? 1 : 0][c] < t.tiles) --c;
+        if (c >= 2) {
+            t.cluster = c;
+            t.dp_tiles = 0;
+            t.grid = t.tiles * c;
+            t.sk_units = static_cast<long long>(t.tiles) * t.kb;
+            return t;
+        }
+    }
     if (t.tiles % G == 0) t.dp_tiles = t.tiles;
     else if (t.tiles < G) t.dp_tiles = 0;
     else t.dp_tiles = (t.tiles / G - 1) * G;
@@ -267,7 +319,7 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(split::THREADS), 0, st);
-        const int n_counters = static_cast<int>(pl.tiles - pl.dp_tiles);
+        const int n_counters = pl.cluster >= 2 ? 0 : static_cast<int>(pl.tiles - pl.dp_tiles);
         cudaError_t e = cudaLaunchKernelEx(&cfg, split::act_split_kernel<S>, static_cast<const __nv_bfloat16 *>(x), ldx,
                                            static_cast<int>(K), static_cast<int>(Kp), planes, plane_stride, rscale,
                                            counters, n_counters);
@@ -302,14 +354,30 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
     p.dp_tiles = pl.dp_tiles;
     p.grid = pl.grid;
     p.sk_units = pl.sk_units;
+    p.cluster = pl.cluster;
     p.w = w;
     p.kp = Kp;
     p.pf_stages = prefetch_stages();
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, dim3(pl.grid), dim3(tci8::NUM_THREADS), tci8::Cfg<NT, S>::SMEM_BYTES, st);
-    cudaError_t e = packed ? cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, true>, tw, tx, p)
-                           : cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, false>, tw, tx, p);
+    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr1[1];
+    launch_config(cfg, attr1, dim3(pl.grid), dim3(tci8::NUM_THREADS), tci8::Cfg<NT, S>::SMEM_BYTES, st);
+    attr[0] = attr1[0];
+    cfg.attrs = attr;
+    cudaError_t e;
+    if (pl.cluster >= 2) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = static_cast<unsigned>(pl.cluster);
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+        e = packed ? cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, true, true>, tw, tx, p)
+                   : cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, false, true>, tw, tx, p);
+    } else {
+        cfg.numAttrs = 1;
+        e = packed ? cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, true, false>, tw, tx, p)
+                   : cudaLaunchKernelEx(&cfg, tci8::tc_i8_kernel<NT, S, SILU, false, false>, tw, tx, p);
+    }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "tc_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -541,7 +609,7 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
     if (algo == LSE_ALGO_SKINNY)
         return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, res, ldr, g_dev[dev].num_sms, st);
 
-    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
+    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
     if (!workspace || !aligned16(workspace) ||
         workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;
@@ -739,7 +807,7 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
         // 64 KB of counters + 2 * grid * 64 * 128 * 4 bytes of partial tiles (9.7 MB for 148
         // SMs) + 3 digit planes of M x Kp bytes + M row scales: for M = 64 the array holds K up
         // to about 36,000 on a 148-SM part.
-        const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
+        const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
         const size_t need = tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K);
         if (need > static_cast<size_t>(LSE_NOALLOC_SCRATCH_BYTES)) {
             std::snprintf(t_last_error, sizeof(t_last_error),
@@ -816,7 +884,7 @@ extern "C" int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t
         return LSE_OK;
     }
     const int64_t N = 2 * I;
-    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms);
+    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
     if (!workspace || !aligned16(workspace) ||
         workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;

@@ -39,6 +39,15 @@
 // loops are done, sums all partials in segment order (deterministic) with all 256 threads,
 // applies the scales and stores y.  No CTA ever waits for another CTA.
 //
+// CLUSTER = true (few tiles, decode): every tile's K range is split evenly over the p.cluster
+// CTAs of one thread-block cluster, each CTA holding one segment.  Each CTA leaves its fp32
+// partial in its own shared memory (the drained stage buffers); after a cluster barrier CTA r
+// sums token rows [NT r / c, NT (r + 1) / c) of all c partials through distributed shared
+// memory in rank order (deterministic), applies the scales and stores y; a second cluster
+// barrier keeps every partial alive until all have been read.  No global partials, counters or
+// last-arriver tail.  The cluster's CTAs are co-scheduled, and every CTA reaches both barriers
+// on every path (a CTA whose bounded wait gave up skips its data work, not the barriers).
+//
 // Every mbarrier wait is bounded (tc_ptx.cuh: mbar_wait); on a timeout the CTA raises an
 // abort flag, records LSE_ERR_DEVICE_TIMEOUT, drains its own copies and MMAs, frees TMEM
 // and returns.
@@ -104,6 +113,7 @@ struct Params {
     int *counters;             // [stream-K tiles] arrival counters (zeroed by the split kernel)
     int m_tiles, tiles, kb, dp_tiles, grid;
     long long sk_units;
+    int cluster;               // CTAs per tile in a thread-block cluster (CLUSTER kernels)
     const int8_t *w;           // weights (L2 prefetch addresses; the copies use the tensor map)
     int64_t kp;                // packed layout: padded K
     int pf_stages;             // L2 prefetch distance in stages beyond the shared-memory ring
@@ -251,6 +261,41 @@ __device__ __forceinline__ void prefetch_w_tile_l2(const Params &p, int n0, int 
     }
 }
 
+// y of row quad rq..rq+3 and token j of a tile from its fully reduced fp32 sums `acc` (planes
+// combined): y = bf16(acc * s[n] * r[m] (+ residual)), or for SILU the gate quad takes the up
+// quad's sums from lane + 2 (quad rq + 8) and writes silu(g) * u.  Called by whole warps whose
+// lanes hold the 32 quads of one token in order.
+template <bool SILU>
+__device__ __forceinline__ void finish_quad(const Params &p, float4 acc, int j, int rq, int n_tile, int m0, int mval) {
+    const int n = n_tile * BN + rq;
+    const float rs = j < mval ? __ldg(p.row_scale + m0 + j) : 0.f;
+    if constexpr (SILU) {
+        const float u4[4] = {__shfl_xor_sync(0xffffffffu, acc.x, 2), __shfl_xor_sync(0xffffffffu, acc.y, 2),
+                             __shfl_xor_sync(0xffffffffu, acc.z, 2), __shfl_xor_sync(0xffffffffu, acc.w, 2)};
+        if (j >= mval || (rq & 8)) return;
+        const float g4[4] = {acc.x, acc.y, acc.z, acc.w};
+        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (n + e < p.N) {
+                const float g = g4[e] * (__ldg(p.scale + n + e) * rs);
+                const float u = u4[e] * (__ldg(p.scale + n + 8 + e) * rs);
+                yr[e] = __float2bfloat16_rn(silu_fast(g) * u);
+            }
+    } else {
+        if (j >= mval) return;
+        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (n + e < p.N) {
+                float o = a4[e] * (__ldg(p.scale + n + e) * rs);
+                if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
+                yr[e] = __float2bfloat16_rn(o);
+            }
+    }
+}
+
 // Combine the S planes of one accumulator column: sum_p 256^(S-1-p) d_p.
 template <int S>
 __device__ __forceinline__ float combine_planes(const int32_t (&d)[S]) {
@@ -259,7 +304,7 @@ __device__ __forceinline__ float combine_planes(const int32_t (&d)[S]) {
 }
 
 // ---- the kernel -------------------------------------------------------------------------
-template <int NT, int S, bool SILU, bool WPACK>
+template <int NT, int S, bool SILU, bool WPACK, bool CLUSTER = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
              const Params p) {
@@ -456,7 +501,8 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
             const int mval = min(NT, p.M - m0);  // valid token columns of this tile
             const uint32_t d_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * C::ACC_COLS;
             float *part = nullptr;
-            if (!whole) part = p.partials + static_cast<size_t>(partial_slot(p, blockIdx.x, s.tile)) * (NT * BN);
+            if (CLUSTER) part = reinterpret_cast<float *>(smem);  // this CTA's partial, in the drained stages
+            else if (!whole) part = p.partials + static_cast<size_t>(partial_slot(p, blockIdx.x, s.tile)) * (NT * BN);
 #pragma unroll 1
             for (int c0 = 0; c0 < NT; c0 += 32) {
                 if (c0 >= mval) break;
@@ -478,7 +524,15 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
                 }
                 // r[m] of the chunk's tokens, one per lane, shuffled to every lane below
                 const float rs_lane = (c0 + lane < mval) ? __ldg(p.row_scale + m0 + c0 + lane) : 0.f;
-                if (whole && SILU) {
+                if (CLUSTER) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        int32_t d[S];
+#pragma unroll
+                        for (int pl = 0; pl < S; ++pl) d[pl] = dv[pl][j];
+                        part[(c0 + j) * BN + row] = combine_planes<S>(d);
+                    }
+                } else if (whole && SILU) {
                     // gate lanes ((lane & 8) == 0) take the up value of their row from lane + 8
                     const int col = (n >> 4) * 8 + (n & 7);
 #pragma unroll
@@ -520,7 +574,7 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&d_empty[buf]));
             ++dpos;
-            if (!whole) {
+            if (!CLUSTER && !whole) {
                 // Publish this segment's partial, then count arrivals on the tile.
                 const long long ts = s.tile - p.dp_tiles;
                 const int c_first = sk_owner(p, ts * p.kb);
@@ -551,6 +605,35 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
     __syncwarp();
     ptx::tc_fence_before();
     ptx::cta_sync_all();
+
+    // ---------------- cluster reduction (all 256 threads of every CTA) ----------------
+    if constexpr (CLUSTER) {
+        ptx::cluster_sync();  // every CTA's partial is in its shared memory
+        if (!*abort_flag) {
+            const int c = p.cluster;
+            const uint32_t rank = ptx::cluster_ctarank();
+            const int tile = blockIdx.x / c;
+            const int n_tile = tile / p.m_tiles;
+            const int m0 = (tile % p.m_tiles) * NT;
+            const int mval = min(NT, p.M - m0);
+            const int j0 = NT * static_cast<int>(rank) / c, j1 = NT * (static_cast<int>(rank) + 1) / c;
+            const uint32_t mine = ptx::smem_u32(smem) + (lane * 4) * 4;  // quad `lane` of token 0
+            for (int j = j0 + warp; j < j1; j += NUM_THREADS / 32) {  // one token per warp, lane = row quad
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j < mval) {
+                    for (int q = 0; q < c; ++q) {  // rank order: deterministic
+                        const float4 v = ptx::ld_shared_cluster_v4(ptx::map_shared_rank(mine + j * BN * 4, q));
+                        acc.x += v.x;
+                        acc.y += v.y;
+                        acc.z += v.z;
+                        acc.w += v.w;
+                    }
+                }
+                finish_quad<SILU>(p, acc, j, lane * 4, n_tile, m0, mval);
+            }
+        }
+        ptx::cluster_sync();  // no CTA leaves while its partial may still be read
+    }
 
     // ---------------- stream-K reductions (all 256 threads) ----------------
     // A tile whose last segment arrived here: sum every segment's partial in segment order
@@ -599,39 +682,11 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
                         acc[i].w += v[i][u].w;
                     }
             }
+            static_assert(QUADS == 32 && NUM_THREADS % 32 == 0, "a warp holds the 32 quads of one token");
 #pragma unroll
             for (int i = 0; i < IPT; ++i) {
                 const int item = threadIdx.x + i * NUM_THREADS;
-                const int j = item / QUADS, rq = (item % QUADS) * 4;
-                const int n = n_tile * BN + rq;
-                const float rs = j < mval ? __ldg(p.row_scale + m0 + j) : 0.f;
-                if constexpr (SILU) {
-                    // quad rq + 8 (the up rows of gate quad rq) is item + 2: lane + 2 of this warp
-                    static_assert(QUADS == 32 && NUM_THREADS % 32 == 0, "quad exchange stays in the warp");
-                    const float u4[4] = {__shfl_xor_sync(0xffffffffu, acc[i].x, 2), __shfl_xor_sync(0xffffffffu, acc[i].y, 2),
-                                         __shfl_xor_sync(0xffffffffu, acc[i].z, 2), __shfl_xor_sync(0xffffffffu, acc[i].w, 2)};
-                    if (j >= mval || (rq & 8)) continue;
-                    const float g4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
-                    __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (n + e < p.N) {
-                            const float g = g4[e] * (__ldg(p.scale + n + e) * rs);
-                            const float u = u4[e] * (__ldg(p.scale + n + 8 + e) * rs);
-                            yr[e] = __float2bfloat16_rn(silu_fast(g) * u);
-                        }
-                } else {
-                    if (j >= mval) continue;
-                    __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
-                    const float a4[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (n + e < p.N) {
-                            float o = a4[e] * (__ldg(p.scale + n + e) * rs);
-                            if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
-                            yr[e] = __float2bfloat16_rn(o);
-                        }
-                }
+                finish_quad<SILU>(p, acc[i], item / QUADS, (item % QUADS) * 4, n_tile, m0, mval);
             }
         }
     }

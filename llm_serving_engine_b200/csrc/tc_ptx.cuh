@@ -276,5 +276,29 @@ __device__ __forceinline__ void bar_arrive(int id, int nthreads) {
 // even where the compiler has duplicated the call into divergent role branches.
 __device__ __forceinline__ void cta_sync_all() { asm volatile("barrier.sync 0;" ::: "memory"); }
 
+// ---- thread-block clusters ---------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster arrives (release: its earlier shared-memory writes
+// become visible cluster-wide) and waits for all the others (acquire).  Non-.aligned form.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// The address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 }  // namespace ptx
 }  // namespace lse
