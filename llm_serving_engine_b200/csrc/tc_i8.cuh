@@ -71,6 +71,7 @@ constexpr int TMEM_COLS = 512;
 // A throttle wait of the L2 prefetcher that exceeds this gives up prefetching (~20 us).
 constexpr long long kPrefetchWaitCycles = 40000;
 constexpr int kSmemBudget = 220 * 1024;  // stages + control block (227 KB per CTA at most)
+constexpr int kMaxCluster = 8;          // CTAs per cluster in the CLUSTER schedule (portable size)
 
 template <int NT, int S>
 struct Cfg {
@@ -90,9 +91,9 @@ struct Cfg {
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static_assert(STAGES >= 3, "pipeline depth");
     // barrier block after the stages: full, empty (STAGES each), d_full, d_empty (ACC_BUFS),
-    // drain; then tmem address, abort flag and the pending stream-K reductions (count + 2 x
+    // drain, teardown; then tmem address, abort flag and the pending stream-K reductions (count + 2 x
     // {tile, first CTA, last CTA}).
-    static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 2;
     static constexpr int CTRL_BYTES = NUM_BARS * 8 + 48;
     static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + CTRL_BYTES;
     // kind::i8: D s32 (bits 4-5 = 2), A s8 (bits 7-9 = 1), B s8 (bits 10-12 = 1), both
@@ -296,6 +297,38 @@ __device__ __forceinline__ void finish_quad(const Params &p, float4 acc, int j, 
     }
 }
 
+// finish_quad with the row quad's scales already loaded: s4 = s[n..n+3], s4u = s[n+8..n+11]
+// (SILU's up quad) and rs = r[m].
+template <bool SILU>
+__device__ __forceinline__ void finish_quad_scaled(const Params &p, float4 acc, float4 s4, float4 s4u, float rs, int j,
+                                                   int rq, int n_tile, int m0, int mval) {
+    const int n = n_tile * BN + rq;
+    if constexpr (SILU) {
+        const float u4[4] = {__shfl_xor_sync(0xffffffffu, acc.x, 2), __shfl_xor_sync(0xffffffffu, acc.y, 2),
+                             __shfl_xor_sync(0xffffffffu, acc.z, 2), __shfl_xor_sync(0xffffffffu, acc.w, 2)};
+        if (j >= mval || (rq & 8)) return;
+        const float g4[4] = {acc.x, acc.y, acc.z, acc.w};
+        const float sg[4] = {s4.x, s4.y, s4.z, s4.w};
+        const float su[4] = {s4u.x, s4u.y, s4u.z, s4u.w};
+        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (n + e < p.N) yr[e] = __float2bfloat16_rn(silu_fast(g4[e] * (sg[e] * rs)) * (u4[e] * (su[e] * rs)));
+    } else {
+        if (j >= mval) return;
+        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        const float sc[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (n + e < p.N) {
+                float o = a4[e] * (sc[e] * rs);
+                if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
+                yr[e] = __float2bfloat16_rn(o);
+            }
+    }
+}
+
 // Combine the S planes of one accumulator column: sum_p 256^(S-1-p) d_p.
 template <int S>
 __device__ __forceinline__ float combine_planes(const int32_t (&d)[S]) {
@@ -320,9 +353,10 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
     uint64_t *d_full = empty + C::STAGES;
     uint64_t *d_empty = d_full + C::ACC_BUFS;
     uint64_t *drain = d_empty + C::ACC_BUFS;
-    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(drain + 1);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(drain + 1) + 1;
-    volatile int *pending = reinterpret_cast<volatile int *>(drain + 1) + 2;  // [0] count, then triples
+    uint64_t *td_bar = drain + 1;  // teardown: one arrival per warp
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(td_bar + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(td_bar + 1) + 1;
+    volatile int *pending = reinterpret_cast<volatile int *>(td_bar + 1) + 2;  // [0] count, then triples
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -337,6 +371,7 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
             ptx::mbar_init(ptx::smem_u32(&d_empty[i]), NUM_EPI_WARPS);
         }
         ptx::mbar_init(ptx::smem_u32(drain), 1);
+        ptx::mbar_init(ptx::smem_u32(td_bar), NUM_THREADS / 32);
         *abort_flag = 0;
         pending[0] = 0;
         ptx::fence_mbar_init();
@@ -599,37 +634,68 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
     }
 
     // ---------------- teardown ----------------
-    // In warps 0-2 only lane 0 ran a role loop (or none); the teardown barrier is the
-    // non-aligned form that counts every thread, and it waits for the epilogue before TMEM
-    // is freed.
-    __syncwarp();
+    // In warps 0-2 only lane 0 ran a role loop (or none); every role is done (the epilogue has
+    // read TMEM and recorded its pending reductions) once all 8 warps have arrived.
     ptx::tc_fence_before();
-    ptx::cta_sync_all();
+    ptx::cta_sync_roles(ptx::smem_u32(td_bar));
 
     // ---------------- cluster reduction (all 256 threads of every CTA) ----------------
     if constexpr (CLUSTER) {
+        const int c = p.cluster;
+        const uint32_t rank = ptx::cluster_ctarank();
+        const int tile = blockIdx.x / c;
+        const int n_tile = tile / p.m_tiles;
+        const int m0 = (tile % p.m_tiles) * NT;
+        const int mval = min(NT, p.M - m0);
+        const int j0 = NT * static_cast<int>(rank) / c, j1 = NT * (static_cast<int>(rank) + 1) / c;
+        // s[n] of this lane's row quad (and, for SILU, of the up quad 8 rows on), loaded before
+        // the barrier
+        const int nq = n_tile * BN + lane * 4;
+        float4 s4, s4u = make_float4(0.f, 0.f, 0.f, 0.f);
+        s4.x = nq < p.N ? __ldg(p.scale + nq) : 0.f;
+        s4.y = nq + 1 < p.N ? __ldg(p.scale + nq + 1) : 0.f;
+        s4.z = nq + 2 < p.N ? __ldg(p.scale + nq + 2) : 0.f;
+        s4.w = nq + 3 < p.N ? __ldg(p.scale + nq + 3) : 0.f;
+        if constexpr (SILU) {
+            s4u.x = nq + 8 < p.N ? __ldg(p.scale + nq + 8) : 0.f;
+            s4u.y = nq + 9 < p.N ? __ldg(p.scale + nq + 9) : 0.f;
+            s4u.z = nq + 10 < p.N ? __ldg(p.scale + nq + 10) : 0.f;
+            s4u.w = nq + 11 < p.N ? __ldg(p.scale + nq + 11) : 0.f;
+        }
         ptx::cluster_sync();  // every CTA's partial is in its shared memory
         if (!*abort_flag) {
-            const int c = p.cluster;
-            const uint32_t rank = ptx::cluster_ctarank();
-            const int tile = blockIdx.x / c;
-            const int n_tile = tile / p.m_tiles;
-            const int m0 = (tile % p.m_tiles) * NT;
-            const int mval = min(NT, p.M - m0);
-            const int j0 = NT * static_cast<int>(rank) / c, j1 = NT * (static_cast<int>(rank) + 1) / c;
             const uint32_t mine = ptx::smem_u32(smem) + (lane * 4) * 4;  // quad `lane` of token 0
-            for (int j = j0 + warp; j < j1; j += NUM_THREADS / 32) {  // one token per warp, lane = row quad
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (j < mval) {
-                    for (int q = 0; q < c; ++q) {  // rank order: deterministic
-                        const float4 v = ptx::ld_shared_cluster_v4(ptx::map_shared_rank(mine + j * BN * 4, q));
-                        acc.x += v.x;
-                        acc.y += v.y;
-                        acc.z += v.z;
-                        acc.w += v.w;
-                    }
+            // One token per warp and lane = row quad; two tokens per round, every partial of a
+            // round loaded (distributed shared memory) before any is added, in rank order
+            // (deterministic).
+            constexpr int WARPS = NUM_THREADS / 32;
+#pragma unroll 1
+            for (int j = j0 + warp; j < j1; j += 2 * WARPS) {
+                float4 v[2][tci8::kMaxCluster];
+                float rs[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int jj = j + h * WARPS;
+                    const bool ok = jj < j1 && jj < mval;
+                    rs[h] = ok ? __ldg(p.row_scale + m0 + jj) : 0.f;
+#pragma unroll
+                    for (int q = 0; q < tci8::kMaxCluster; ++q)
+                        v[h][q] = (ok && q < c) ? ptx::ld_shared_cluster_v4(ptx::map_shared_rank(mine + jj * BN * 4, q))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                finish_quad<SILU>(p, acc, j, lane * 4, n_tile, m0, mval);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int jj = j + h * WARPS;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int q = 0; q < tci8::kMaxCluster; ++q) {
+                        acc.x += v[h][q].x;
+                        acc.y += v[h][q].y;
+                        acc.z += v[h][q].z;
+                        acc.w += v[h][q].w;
+                    }
+                    if (jj < j1) finish_quad_scaled<SILU>(p, acc, s4, s4u, rs[h], jj, lane * 4, n_tile, m0, mval);
+                }
             }
         }
         ptx::cluster_sync();  // no CTA leaves while its partial may still be read

@@ -272,9 +272,21 @@ __device__ __forceinline__ void bar_sync(int id, int nthreads) {
 __device__ __forceinline__ void bar_arrive(int id, int nthreads) {
     asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-// CTA-wide barrier that counts threads individually (non-.aligned form), so it is correct
-// even where the compiler has duplicated the call into divergent role branches.
+// CTA-wide barrier for converged code (set-up, before the warp roles split).
 __device__ __forceinline__ void cta_sync_all() { asm volatile("barrier.sync 0;" ::: "memory"); }
+
+// CTA-wide barrier after warp-specialised roles, on an mbarrier initialised with one arrival
+// per warp: every warp reconverges, its lane 0 arrives exactly once and every thread waits for
+// the phase (bounded).  A hardware barrier is not used here: where a warp's lanes leave their
+// roles through different copies of the code, each copy's barrier instruction counted as the
+// warp's arrival (measured on B200: the MMA warp passed a barrier.sync 0 while the epilogue
+// warps were still reading TMEM).
+__device__ __forceinline__ void cta_sync_roles(uint32_t bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    mbar_drain(bar, 0);
+    __syncwarp();  // the lanes leave the wait one by one: reconverge for the code that follows
+}
 
 // ---- thread-block clusters ---------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -282,10 +294,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
-// Every thread of every CTA of the cluster arrives (release: its earlier shared-memory writes
-// become visible cluster-wide) and waits for all the others (acquire).  Non-.aligned form.
+// Every thread of every CTA of the cluster arrives and waits for all the others; the
+// cluster-scope fence before a relaxed arrive publishes the thread's earlier shared-memory
+// writes (local and remote), the wait acquires everyone else's.  Called by whole, converged
+// warps (.aligned).  Measured on B200: 0.9 us from the last arrival to release, against 2-3.5 us
+// for the arrive.release form.
 __device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+    __syncwarp();
+    asm volatile("fence.acq_rel.cluster;\n\tbarrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 // The address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank) {
