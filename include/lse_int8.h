@@ -272,6 +272,17 @@ const char *lse_last_cuda_error(void);
 int lse_device_status(int device, int reset);
 
 /*
+ * Wait limit of the tensor-core kernels on `device`, in SM clock cycles: a bounded mbarrier wait
+ * for data (a copy, an MMA, a stage) that has not completed after this many cycles raises the
+ * CTA's abort flag and records LSE_ERR_DEVICE_TIMEOUT (lse_device_status); the CTA then drains
+ * its own copies and MMAs under the default limit, frees its tensor memory and returns, and the
+ * next call starts clean.  cycles <= 0 restores the default (4e9 cycles, ~2 s).  Takes effect
+ * for launches after the call; meant for tests of the timeout path (a limit of 1 cycle makes
+ * every data wait of a tensor-core launch give up).
+ */
+int lse_set_wait_limit(int device, long long cycles);
+
+/*
  * lse_int8_linear_packed_noalloc -- no counterpart in the reference: an addition of this
  * library for callers that cannot allocate a workspace.
  *

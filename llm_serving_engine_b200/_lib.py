@@ -67,6 +67,7 @@ SIGNATURES = {
     "lse_status_string": ([_I32], ctypes.c_char_p),
     "lse_last_cuda_error": ([], ctypes.c_char_p),
     "lse_device_status": ([_I32, _I32], _I32),
+    "lse_set_wait_limit": ([_I32, ctypes.c_longlong], _I32),
     "lse_abi_version": ([], _I32),
 }
 

@@ -26,6 +26,9 @@ __device__ __forceinline__ void report_timeout() {
 // ~2 s at the B200's 1.9 GHz boost clock, ~3 s under the power cap: far above any
 // legitimate wait in these kernels, short enough that a lost arrival ends the launch.
 constexpr long long kWaitLimitCycles = 4000000000LL;
+// The limit of data waits (lse_set_wait_limit); drains of a CTA's own copies and MMAs keep
+// kWaitLimitCycles.
+__device__ long long g_wait_limit = kWaitLimitCycles;
 
 // Streaming 128-bit load of read-once weight bytes: skip L1, keep L2 normal.
 __device__ __forceinline__ int4 ld_stream_v4(const void *p) {

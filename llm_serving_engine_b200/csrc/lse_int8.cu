@@ -444,15 +444,18 @@ cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, cons
                               MT == 1 ? skinny_prefetch_groups() : 0);
 }
 
-// Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes):
+// Decode-kernel configuration by shape (measured on B200, Llama-3 projection shapes; variant
+// sweeps of 32 layers' weights per CUDA graph, the winners below):
 //   * very many row blocks (N/16 >= 4 x SMs: gate_up): CTAs of 8 warps on one row block, four
 //     CTAs per SM (M <= 8; above that, four row blocks per CTA, so that each activation load,
 //     which costs eight L1 wavefronts, serves 64 weight rows);
 //   * many row blocks (N/16 >= 2 x SMs: QKV): CTAs of 8 warps on two row blocks, so every
 //     activation load serves 32 weight rows, eight chunks per row block in registers (a warp's
-//     K slice is then two register groups deep at K = 4096: 2-4% faster than four);
+//     K slice is then one or two register groups deep at K = 4096): M <= 8 at 4519 GB/s against
+//     3884 with four chunks; M = 9..16 three CTAs per SM, one row block (3286 against 3227);
 //   * few row blocks (O, down): CTAs of 16 warps, one row block (two for M > 8, where the
-//     activation loads, not the weight stream, would otherwise saturate L1);
+//     activation loads, not the weight stream, would otherwise saturate L1, and for a long K
+//     at M <= 8: down 5257 GB/s against 4940);
 //   * fp16 MMA for M <= 8 (cheapest widening), bf16 MMA for M > 8 (activations used as they
 //     are).
 // -1 selects by shape as above; 0..17 pin one configuration in sweeps.
@@ -469,7 +472,10 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
                              int num_sms, cudaStream_t st) {
     if (variant < 0) {
         const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
-        variant = rb_per_sm >= 4 ? (MT == 1 ? 7 : 1) : (rb_per_sm >= 2 ? 1 : 0);
+        if (rb_per_sm >= 4) variant = MT == 1 ? 7 : 1;
+        else if (SILU || MT == 4) variant = rb_per_sm >= 2 ? 1 : 0;
+        else if (rb_per_sm >= 2) variant = MT == 1 ? 15 : 17;
+        else variant = (MT == 1 && K >= 8192) ? 4 : 0;
     }
     if constexpr (MT == 4) {
         // 17..32 tokens: bf16 MMA, two row blocks per CTA so each activation load serves 32 rows
@@ -710,6 +716,23 @@ int lse_int8_quantize(const void *w, int dtype, int64_t N, int64_t K, int64_t ld
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "quantize launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+int lse_set_wait_limit(int device, long long cycles) {
+    int rc = init_device(device);
+    if (rc) return rc;
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) { set_cuda_error(e, "cudaGetDevice"); return LSE_ERR_CUDA; }
+    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) {
+        set_cuda_error(e, "cudaSetDevice");
+        return LSE_ERR_CUDA;
+    }
+    const long long v = cycles > 0 ? cycles : kWaitLimitCycles;
+    e = cudaMemcpyToSymbol(g_wait_limit, &v, sizeof(v));
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) { set_cuda_error(e, "lse_set_wait_limit"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }
 

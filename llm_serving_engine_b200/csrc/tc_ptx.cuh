@@ -42,15 +42,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uin
 }
 
 // Bounded wait for the phase with `parity` to complete.  Gives up (returns false) when
-// the CTA-wide abort flag is raised by another role, or after kWaitLimitCycles, in which
+// the CTA-wide abort flag is raised by another role, or after g_wait_limit cycles, in which
 // case it raises the abort flag and records LSE_ERR_DEVICE_TIMEOUT for the host.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity, 0)) return true;
     const long long t0 = clock64_now();
+    const long long limit = __ldg(&g_wait_limit);  // constant during a launch
+    // Under a short (test) limit, poll instead of sleeping, so the limit is seen.
+    const uint32_t suspend_ns = limit < kWaitLimitCycles ? 0u : 1000000u;
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity, suspend_ns)) return true;
         if (*abort_flag) return false;
-        if (clock64_now() - t0 > kWaitLimitCycles) {
+        if (clock64_now() - t0 > limit) {
             *abort_flag = 1;
             report_timeout();
             return false;

@@ -402,16 +402,26 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     return out
 
 
+def set_wait_limit(cycles: int, device: int | torch.device | None = None) -> None:
+    """Wait limit of the tensor-core kernels' data waits in SM cycles (lse_set_wait_limit);
+    cycles <= 0 restores the default (~2 s).  For tests of the timeout path."""
+    idx = _device_index(device)
+    _lib.check(_lib.load().lse_set_wait_limit(idx, int(cycles)), "lse_set_wait_limit")
+
+
+def _device_index(device: int | torch.device | None) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, torch.device):
+        return device.index if device.index is not None else torch.cuda.current_device()
+    return int(device)
+
+
 def device_status(device: int | torch.device | None = None, reset: bool = True) -> int:
     """Synchronize and read the device-side status (LSE_OK or LSE_ERR_DEVICE_TIMEOUT).  After a
     timeout the decode-attention workspaces of that device are re-zeroed (the linear
     workspaces need nothing: each call initialises its own)."""
-    if device is None:
-        idx = torch.cuda.current_device()
-    elif isinstance(device, torch.device):
-        idx = device.index if device.index is not None else torch.cuda.current_device()
-    else:
-        idx = int(device)
+    idx = _device_index(device)
     st = int(_lib.load().lse_device_status(idx, 1 if reset else 0))
     if st == _lib.LSE_ERR_DEVICE_TIMEOUT:
         for (d, _), ws in _attn_ws.items():
