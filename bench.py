@@ -686,8 +686,13 @@ def main():
                             else "fallback 6650 GB/s"),
             "frac_of_8TBps": round(achieved / 8000.0, 4),
             "algorithmic_bytes_per_launch": round(b / n),
+            # DRAM bytes per launch from one ncu capture of a named case (profiles/traffic.json),
+            # beside that case's own algorithmic bytes: their ratio is the re-read factor
             "traffic": tr.get("dram_bytes_per_launch") if tr else None,
             "traffic_case": tr.get("case") if tr else None,
+            "traffic_case_algorithmic_bytes": tr.get("algorithmic_bytes_per_launch") if tr else None,
+            "traffic_ratio": (round(tr["dram_bytes_per_launch"] / tr["algorithmic_bytes_per_launch"], 4)
+                              if tr and tr.get("algorithmic_bytes_per_launch") else None),
         }
     # dominant kernel = the one with the larger share of the step's time
     step_share = {k: v[1] for k, v in per_kernel.items()}

@@ -272,6 +272,35 @@ const char *lse_last_cuda_error(void);
 int lse_device_status(int device, int reset);
 
 /*
+ * lse_paged_attention -- replaces the reference's paged_attention_forward /
+ * paged_attention_2 (src/llm_serving_engine/kernels/flash_attention.py:202-332) for any number
+ * of query tokens per batch entry: prefill chunks and mixed prefill + decode batches, as
+ * ModelRunner.attend_paged (src/llm_serving_engine/model/model_runner.py:357-363) calls it.
+ *
+ *   q        [H, tokens, D] of `dtype` (LSE_BF16 or LSE_F16), element (h, t, d) at
+ *            q[h * q_stride_h + t * q_stride_m + d]; even strides, 16-byte aligned
+ *   k_pool, v_pool  [num_blocks, block_size, H_kv, D] of `dtype`, contiguous, holding this
+ *            call's new tokens already
+ *   block_table int32 [E, >= ceil(context_len / block_size)], row stride bt_stride
+ *   context_len, query_offset, q_start, q_len  int32 [E]: entry e's queries are rows
+ *            q_start[e] .. q_start[e] + q_len[e] - 1 of q, row i at position
+ *            query_offset[e] + i, attending to positions p < context_len[e] with
+ *            p <= query_offset[e] + i
+ *   max_q_len  >= every q_len[e] (sizes the launch)
+ *   o        [H, tokens, D] of `dtype`, element (h, t, d) at o[h * o_stride_h + t * o_stride_m + d];
+ *            rows of no entry are not written
+ * D = 64 or 128, H / H_kv in {1, 2, 4, 8} (LSE_ERR_UNSUPPORTED otherwise).  fp32 scores and
+ * accumulation, P rounded to `dtype` before P V (as the reference), one rounding of o.  A block
+ * id outside [0, num_blocks) is not read and is reported as LSE_ERR_INVALID_ARG by
+ * lse_device_status.  No workspace.
+ */
+int lse_paged_attention(const void *q, int dtype, int64_t H, int64_t D, int64_t q_stride_h, int64_t q_stride_m,
+                        const void *k_pool, const void *v_pool, int64_t num_blocks, int64_t block_size, int64_t H_kv,
+                        const int32_t *block_table, int64_t bt_stride, const int32_t *context_len,
+                        const int32_t *query_offset, const int32_t *q_start, const int32_t *q_len, int64_t E,
+                        int64_t max_q_len, float scale, void *o, int64_t o_stride_h, int64_t o_stride_m, void *stream);
+
+/*
  * Wait limit of the tensor-core kernels on `device`, in SM clock cycles: a bounded mbarrier wait
  * for data (a copy, an MMA, a stage) that has not completed after this many cycles raises the
  * CTA's abort flag and records LSE_ERR_DEVICE_TIMEOUT (lse_device_status); the CTA then drains

@@ -68,6 +68,8 @@ SIGNATURES = {
     "lse_last_cuda_error": ([], ctypes.c_char_p),
     "lse_device_status": ([_I32, _I32], _I32),
     "lse_set_wait_limit": ([_I32, ctypes.c_longlong], _I32),
+    "lse_paged_attention": ([_P, _I32, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P,
+                             _I64, _I64, ctypes.c_float, _P, _I64, _I64, _P], _I32),
     "lse_abi_version": ([], _I32),
 }
 

@@ -16,6 +16,7 @@
 
 #include "../../include/lse_int8.h"
 #include "decode_attn.cuh"
+#include "paged_attn.cuh"
 #include "rope_kv.cuh"
 #include "rms_norm.cuh"
 #include "gemv_i8.cuh"
@@ -718,6 +719,106 @@ int lse_int8_quantize(const void *w, int dtype, int64_t N, int64_t K, int64_t ld
     if (e != cudaSuccess) { set_cuda_error(e, "quantize launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
 }
+
+}  // extern "C"
+
+namespace lse {
+namespace {
+
+template <int D, int G, typename T>
+cudaError_t launch_pattn(const pattn::Params &p, int64_t E, int64_t max_q_len, cudaStream_t st) {
+    constexpr int smem = pattn::smem_bytes<D>();
+    auto kernel = pattn::paged_attn_kernel<D, G, T>;
+    {  // opt in to more than 48 KB of dynamic shared memory, once per device
+        static std::once_flag once[kMaxDevices];
+        static cudaError_t set_err[kMaxDevices];
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        std::call_once(once[dev], [&] {
+            set_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        });
+        if (set_err[dev] != cudaSuccess) return set_err[dev];
+    }
+    constexpr int toks = pattn::ROWS / G;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(static_cast<unsigned>((max_q_len + toks - 1) / toks), static_cast<unsigned>(E),
+                                  static_cast<unsigned>(p.H_kv)),
+                  dim3(pattn::THREADS), smem, st);
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+template <int D, typename T>
+cudaError_t launch_pattn_g(int64_t G, const pattn::Params &p, int64_t E, int64_t max_q_len, cudaStream_t st) {
+    switch (G) {
+        case 1: return launch_pattn<D, 1, T>(p, E, max_q_len, st);
+        case 2: return launch_pattn<D, 2, T>(p, E, max_q_len, st);
+        case 4: return launch_pattn<D, 4, T>(p, E, max_q_len, st);
+        default: return launch_pattn<D, 8, T>(p, E, max_q_len, st);
+    }
+}
+
+}  // namespace
+}  // namespace lse
+
+extern "C" int lse_paged_attention(const void *q, int dtype, int64_t H, int64_t D, int64_t q_stride_h,
+                                   int64_t q_stride_m, const void *k_pool, const void *v_pool, int64_t num_blocks,
+                                   int64_t block_size, int64_t H_kv, const int32_t *block_table, int64_t bt_stride,
+                                   const int32_t *context_len, const int32_t *query_offset, const int32_t *q_start,
+                                   const int32_t *q_len, int64_t E, int64_t max_q_len, float scale, void *o,
+                                   int64_t o_stride_h, int64_t o_stride_m, void *stream) {
+    if (E < 0 || H <= 0 || H_kv <= 0 || D <= 0 || num_blocks <= 0 || block_size <= 0 || max_q_len < 0)
+        return LSE_ERR_INVALID_ARG;
+    if (E == 0 || max_q_len == 0) return LSE_OK;
+    if (!q || !k_pool || !v_pool || !block_table || !context_len || !query_offset || !q_start || !q_len || !o)
+        return LSE_ERR_INVALID_ARG;
+    if (H % H_kv) return LSE_ERR_INVALID_ARG;
+    if (dtype != LSE_BF16 && dtype != LSE_F16) return LSE_ERR_UNSUPPORTED;
+    const int64_t G = H / H_kv;
+    if ((D != 64 && D != 128) || (G != 1 && G != 2 && G != 4 && G != 8)) return LSE_ERR_UNSUPPORTED;
+    if (E > 65535 || H_kv > 65535 || num_blocks * block_size > INT32_MAX / 2 || bt_stride < 0 ||
+        max_q_len > INT32_MAX / 2)
+        return LSE_ERR_UNSUPPORTED;
+    if ((q_stride_h & 1) || (q_stride_m & 1) || (o_stride_h & 1) || (o_stride_m & 1) || !aligned16(q) || !aligned16(o) ||
+        !aligned16(k_pool) || !aligned16(v_pool))
+        return LSE_ERR_ALIGNMENT;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    pattn::Params p{};
+    p.q = q;
+    p.q_sh = q_stride_h;
+    p.q_sm = q_stride_m;
+    p.k_pool = k_pool;
+    p.v_pool = v_pool;
+    p.block_table = block_table;
+    p.bt_stride = bt_stride;
+    p.context_len = context_len;
+    p.query_offset = query_offset;
+    p.q_start = q_start;
+    p.q_len = q_len;
+    p.o = o;
+    p.o_sh = o_stride_h;
+    p.o_sm = o_stride_m;
+    p.H_kv = static_cast<int>(H_kv);
+    p.block_size = static_cast<int>(block_size);
+    p.num_blocks = static_cast<int>(num_blocks);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (dtype == LSE_BF16)
+        e = D == 128 ? launch_pattn_g<128, __nv_bfloat16>(G, p, E, max_q_len, st)
+                     : launch_pattn_g<64, __nv_bfloat16>(G, p, E, max_q_len, st);
+    else
+        e = D == 128 ? launch_pattn_g<128, __half>(G, p, E, max_q_len, st) : launch_pattn_g<64, __half>(G, p, E, max_q_len, st);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "paged_attn launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+
+extern "C" {
 
 int lse_set_wait_limit(int device, long long cycles) {
     int rc = init_device(device);

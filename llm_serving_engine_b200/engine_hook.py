@@ -11,7 +11,11 @@ the projections, and any other config runs the reference's `__init__` untouched.
 
 After the swap nothing else in the engine changes: `forward`, `forward_fused`,
 `DecodeGraphRunner` (`decode_graph.py:87-140`) and `PiecewiseGraphRunner`
-(`piecewise_graph.py:71-183`) call the same module slots.  int8 needs CUDA; on a CPU-only
+(`piecewise_graph.py:71-183`) call the same module slots.  The runner's paged attention
+(`ModelRunner.attend_paged`, `model_runner.py:357-363`, reached from `paged_attention` in the
+eager and decode-graph paths and from the piecewise runner between its segments) is bound to
+this package's kernel on the same arguments (`ops.paged_attention`, the drop-in for the
+reference's Triton `paged_attention_forward`).  int8 needs CUDA; on a CPU-only
 machine the switch raises `RuntimeError` at load, the way the reference's custom-kernel
 check refuses a CPU device (`model_runner.py:77-94`); there is no CPU fallback.
 """
@@ -23,21 +27,39 @@ import functools
 
 import torch
 
+from . import ops
 from .int8_linear import quantize_llama_
 
-__all__ = ["enable_int8", "install", "uninstall", "installed"]
+__all__ = ["enable_int8", "bind_paged_attention", "install", "uninstall", "installed"]
 
 
-def enable_int8(runner, lm_head: bool = False):
+def _attend_paged(runner, q, layer_idx, paging):
+    """`ModelRunner.attend_paged` on this package's kernel: same arguments, same result."""
+    return ops.paged_attention(q, runner._k_pool[layer_idx], runner._v_pool[layer_idx], paging.block_table,
+                               paging.context_len, paging.query_offset, paging.q_start, paging.q_len,
+                               runner._block_size, paging.max_q_len)
+
+
+def bind_paged_attention(runner):
+    """Route the runner's paged attention to `ops.paged_attention` (an instance attribute, so
+    the runner's own `paged_attention` and the graph runners call it)."""
+    runner.attend_paged = functools.partial(_attend_paged, runner)
+    return runner
+
+
+def enable_int8(runner, lm_head: bool = False, attention: bool = True):
     """Swap a loaded `ModelRunner`'s projections to int8 in place.  `runner.model` is the
     Llama-family model the runner loaded; every decoder layer's q/k/v (one fused int8 QKV),
-    o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`.
-    Nothing else needs preparing: the ops hold no per-stream state, so the engine's graph
-    captures on any stream record them as they are."""
+    o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`;
+    with `attention=True` the paged attention runs on this package's kernel too.  Nothing else
+    needs preparing: the ops hold no per-stream state, so the engine's graph captures on any
+    stream record them as they are."""
     device = torch.device(runner.device)
     if device.type != "cuda":
         raise RuntimeError(f"int8 weight-only quantization needs a CUDA device, got {runner.device!r}")
     quantize_llama_(runner.model, lm_head=lm_head)
+    if attention:
+        bind_paged_attention(runner)
     return runner
 
 

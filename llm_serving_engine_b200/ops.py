@@ -402,6 +402,56 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     return out
 
 
+def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
+                    context_len: torch.Tensor, query_offset: torch.Tensor, q_start: torch.Tensor, q_len: torch.Tensor,
+                    block_size: int, max_q_len: int, scale: float | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's `paged_attention_forward` (`kernels/flash_attention.py:287-332`) on the
+    sm_100a kernel, same arguments and result: q (H, tokens, D) bf16 or fp16 with d contiguous;
+    k_pool / v_pool (num_blocks, block_size, H_KV, D) contiguous, same dtype; block_table
+    int32 [E, n]; context_len, query_offset, q_start, q_len int32 [E]; max_q_len >= every
+    q_len.  Returns o like q (a new tensor unless `out` is given): entry e's rows
+    q_start[e] .. + q_len[e] - 1 attend causally (position query_offset[e] + i) to the
+    positions below context_len[e].  Rows of no entry are left unwritten."""
+    tensors = (q, k_pool, v_pool, block_table, context_len, query_offset, q_start, q_len)
+    if not all(t.is_cuda for t in tensors):
+        raise RuntimeError("paged_attention runs on CUDA only (no CPU fallback)")
+    if q.dtype not in (torch.bfloat16, torch.float16) or k_pool.dtype != q.dtype or v_pool.dtype != q.dtype:
+        raise ValueError("paged_attention: q and the pools must share a dtype, bfloat16 or float16")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("paged_attention: q must be (H, tokens, D) with a contiguous last dim")
+    if k_pool.shape != v_pool.shape or k_pool.dim() != 4 or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
+        raise ValueError("paged_attention: pools must be contiguous (num_blocks, block_size, H_KV, D)")
+    H, T, D = q.shape
+    nb, bs, H_kv, Dk = k_pool.shape
+    if Dk != D or bs != block_size:
+        raise ValueError(f"paged_attention: pool (block_size {bs}, head_dim {Dk}) != ({block_size}, {D})")
+    E = q_len.shape[0]
+    for name, t in (("context_len", context_len), ("query_offset", query_offset), ("q_start", q_start),
+                    ("q_len", q_len)):
+        if t.dtype != torch.int32 or t.shape != (E,) or not t.is_contiguous():
+            raise ValueError(f"paged_attention: {name} must be int32 [{E}]")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] != E or block_table.stride(1) != 1:
+        raise ValueError("paged_attention: block_table must be int32 [E, n] with contiguous rows")
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.dtype != q.dtype or out.shape != q.shape or out.stride(-1) != 1:
+        raise ValueError("paged_attention: out must match q's dtype and shape with a contiguous last dim")
+    if E == 0 or T == 0:
+        return out
+    _ensure_device(q.device)
+    stream = torch.cuda.current_stream(q.device)
+    scale = 1.0 / float(D) ** 0.5 if scale is None else float(scale)
+    dt = _lib.DT_BF16 if q.dtype == torch.bfloat16 else _lib.DT_F16
+    rc = _lib.load().lse_paged_attention(
+        q.data_ptr(), dt, H, D, q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), nb, bs, H_kv,
+        block_table.data_ptr(), block_table.stride(0), context_len.data_ptr(), query_offset.data_ptr(),
+        q_start.data_ptr(), q_len.data_ptr(), E, int(max_q_len), scale, out.data_ptr(), out.stride(0), out.stride(1),
+        stream.cuda_stream)
+    _lib.check(rc, "lse_paged_attention")
+    return out
+
+
 def set_wait_limit(cycles: int, device: int | torch.device | None = None) -> None:
     """Wait limit of the tensor-core kernels' data waits in SM cycles (lse_set_wait_limit);
     cycles <= 0 restores the default (~2 s).  For tests of the timeout path."""

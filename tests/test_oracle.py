@@ -194,6 +194,44 @@ def test_attention_oracle_matches_torch_sdpa_in_float64():
     assert np.all(ref_paged_decode_attention(q, k_pool, v_pool, bt, np.array([0, 0, 0])) == 0)
 
 
+def test_multi_token_attention_oracle_matches_torch_sdpa_and_the_decode_oracle():
+    """Pin the multi-token paged-attention oracle (`paged_attention_2`'s general case): entries
+    with chunks of several tokens after a cached prefix equal torch's causal SDPA (float64,
+    GQA) over the contiguous K/V with the queries placed at their positions; single-token
+    entries at query_offset = context_len - 1 equal the decode oracle; rows of no entry stay
+    zero."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle.ref_attention import gather_kv, ref_paged_attention, ref_paged_decode_attention
+
+    g = torch.Generator().manual_seed(1)
+    H, H_kv, D, bs = 8, 2, 16, 4
+    q_len = np.array([5, 1, 3, 1])
+    query_offset = np.array([0, 6, 9, 0])           # a fresh prefill, decodes, a chunk after a prefix
+    context_len = query_offset + q_len
+    q_start = np.concatenate([[0], np.cumsum(q_len)[:-1]]) + 1  # row 0 belongs to no entry
+    T = int(q_start[-1] + q_len[-1]) + 2
+    E, nbps = len(q_len), 4
+    bt = torch.randperm(E * nbps + 2, generator=g)[: E * nbps].view(E, nbps).numpy()
+    k_pool = torch.randn(E * nbps + 2, bs, H_kv, D, generator=g, dtype=torch.float64).numpy()
+    v_pool = torch.randn(E * nbps + 2, bs, H_kv, D, generator=g, dtype=torch.float64).numpy()
+    q = torch.randn(H, T, D, generator=g, dtype=torch.float64).numpy()
+    out = ref_paged_attention(q, k_pool, v_pool, bt, context_len, query_offset, q_start, q_len)
+    for e in range(E):
+        ctx, off, qs, ql = int(context_len[e]), int(query_offset[e]), int(q_start[e]), int(q_len[e])
+        k = torch.from_numpy(gather_kv(k_pool, bt, e, ctx)).permute(1, 0, 2)[None]
+        v = torch.from_numpy(gather_kv(v_pool, bt, e, ctx)).permute(1, 0, 2)[None]
+        qe = torch.from_numpy(q[:, qs:qs + ql])[None]
+        mask = torch.arange(ctx)[None, :] <= (off + torch.arange(ql))[:, None]
+        ref = F.scaled_dot_product_attention(qe, k, v, attn_mask=mask, enable_gqa=True)
+        np.testing.assert_allclose(out[:, qs:qs + ql], ref[0].numpy(), rtol=1e-12, atol=1e-12)
+        if ql == 1:
+            dec = ref_paged_decode_attention(q[:, qs].reshape(1, H, D), k_pool, v_pool, bt[e:e + 1], context_len[e:e + 1])
+            np.testing.assert_allclose(out[:, qs], dec[0], rtol=1e-12, atol=1e-12)
+    assert np.all(out[:, 0] == 0) and np.all(out[:, -2:] == 0)
+
+
 def test_pack_layout_restatement_places_every_byte():
     """The packed layout's checker puts W[n, k] at (n // 16) * 16 * Kp + (k // 128) * 2048 +
     (n // 8 % 2) * 1024 + (k // 64 % 2) * 512 + (n % 8) * 64 + ((k // 16 % 4) ^ (n % 8 // 2)) * 16
