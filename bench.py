@@ -495,6 +495,85 @@ def decode_attention(dev, warm, ops, hbm_peak):
     return out
 
 
+def prefill_attention(dev, warm, ops):
+    """The multi-token paged-attention kernel (prefill chunks) beside the reference's Triton
+    `paged_attention_forward` when its install is importable: Llama-3-8B attention shape,
+    bf16, one chunk of q_len tokens after a cached prefix per entry.  TFLOP/s counts the
+    causal work (4 * D flops per query-key pair seen)."""
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if os.path.isdir(ref_dir) and ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        from llm_serving_engine.kernels.flash_attention import paged_attention_forward as ref_fwd
+    except Exception:  # the reference is not installed: our kernel alone
+        ref_fwd = None
+    H, H_kv, D, bs = 32, 8, 128, 16
+    out = {"workload": f"H={H}, H_kv={H_kv}, D={D}, block_size={bs}, bf16", "points": []}
+    g = torch.Generator(device=dev).manual_seed(29)
+    for E, qlen, prefix in ((1, 2048, 0), (4, 512, 1024), (16, 128, 896)):
+        ctx = prefix + qlen
+        nbps = -(-ctx // bs)
+        nb = E * nbps + 1
+        bt = torch.randperm(nb, device=dev, generator=g)[: E * nbps].view(E, nbps).to(torch.int32)
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+        cl, off = i32([ctx] * E), i32([prefix] * E)
+        qs, ql = i32([e * qlen for e in range(E)]), i32([qlen] * E)
+        kp = torch.randn(nb, bs, H_kv, D, device=dev, generator=g).to(torch.bfloat16)
+        vp = torch.randn(nb, bs, H_kv, D, device=dev, generator=g).to(torch.bfloat16)
+        q = torch.randn(H, E * qlen, D, device=dev, generator=g).to(torch.bfloat16)
+        pairs = E * H * sum(min(ctx, prefix + i + 1) for i in range(qlen))
+        flops = 4.0 * D * pairs
+        pt = {"E": E, "q_len": qlen, "prefix": prefix}
+        for name, fn in (("ours", lambda: ops.paged_attention(q, kp, vp, bt, cl, off, qs, ql, bs, qlen)),
+                         ("reference_triton", (lambda: ref_fwd(q, kp, vp, bt, cl, off, qs, ql, bs, qlen)) if ref_fwd else None)):
+            if fn is None:
+                continue
+            def run(fn=fn):
+                for _ in range(8):
+                    fn()
+            gr = capture(run, warm)
+            time_graph(gr, 2)
+            us = time_graph(gr, 10) / 8 * 1e3
+            pt[f"{name}_us"] = round(us, 2)
+            pt[f"{name}_TFLOPs"] = round(flops / us / 1e6, 1)
+            del gr
+        if "reference_triton_us" in pt:
+            pt["speedup"] = round(pt["reference_triton_us"] / pt["ours_us"], 3)
+        out["points"].append(pt)
+        del kp, vp, q
+        torch.cuda.empty_cache()
+    return out
+
+
+def host_overhead(dev, ops):
+    """Host time per projection call at M = 16 (Llama-3-8B o_proj shape), no synchronization in
+    the loop: the ctypes path (`ops.int8_linear_packed`), the dispatcher operator
+    (`torch.ops.lse.int8_linear`, what the int8 modules call) and torch's bf16 `F.linear`
+    (cuBLAS) for comparison, each with its launch count per call."""
+    K, N, M, calls = 4096, 4096, 16, 2000
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    w = ops.pack_weight(torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8))
+    s = torch.rand(N, device=dev) * 1e-3
+    wb = torch.randn(N, K, device=dev).to(torch.bfloat16)
+    lse = ops.torch_ops()
+    cases = {"ctypes_ops_int8_linear_packed": lambda: ops.int8_linear_packed(x, w, s, N, K),
+             "torch_ops_lse_int8_linear": lambda: lse.int8_linear(x, w, s, N, K),
+             "torch_F_linear_bf16": lambda: torch.nn.functional.linear(x, wb)}
+    out = {"workload": f"M={M}, K={K}, N={N}, {calls} calls, host wall time per call (GPU queue not drained)",
+           "launches_per_call": {"ctypes_ops_int8_linear_packed": 1, "torch_ops_lse_int8_linear": 1,
+                                 "torch_F_linear_bf16": 1}}
+    for name, fn in cases.items():
+        for _ in range(50):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            fn()
+        out[name + "_us"] = round((time.perf_counter() - t0) / calls * 1e6, 2)
+        torch.cuda.synchronize()
+    return out
+
+
 def bf16_cublas_points(layers: int, dev, warm, xs):
     """Same-box comparison: torch F.linear (cuBLAS) with bf16 weights of the same shapes at
     every decode-sweep point, `layers` distinct weights per graph (the reference's
@@ -733,6 +812,8 @@ def main():
     fused_mlp = fused_gate_up(weights, dev, warm, ops, hbm_peak)
     fused_res = fused_residual(weights, dev, warm, ops)
     attn = decode_attention(dev, warm, ops, hbm_peak)
+    pattn = prefill_attention(dev, warm, ops)
+    host = host_overhead(dev, ops)
     cublas = bf16_cublas_points(layers, dev, warm, xs)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
@@ -788,6 +869,8 @@ def main():
         line["fused_gate_up_silu"] = fused_mlp
         line["fused_residual"] = fused_res
         line["decode_attention"] = attn
+        line["prefill_attention"] = pattn
+        line["host_overhead"] = host
         line["bf16_cublas_points"] = cublas
         line["int8_speedup_vs_bf16_cublas"] = {f"M{p['M']}_{p['shape']}": round(c["us"] / p["us"], 3)
                                                for p, c in zip(points, cublas)}

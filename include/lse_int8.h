@@ -169,6 +169,22 @@ int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t
                                     void *stream);
 
 /*
+ * The packed-weight entry points with the activation type as an argument: `dtype` LSE_BF16 or
+ * LSE_F16 (the reference's ModelConfig.dtype default, src/llm_serving_engine/config.py:31) for
+ * x, y and the residual alike; arguments and workspace otherwise as lse_int8_linear_packed
+ * (with the optional `residual`: null, or as lse_int8_linear_packed_residual) and
+ * lse_int8_gate_up_silu_packed_ws.  fp16 activations enter the decode kernel's fp16 MMA as they
+ * are and the tensor-core kernel's digit planes the same way as bf16 (exact for every element
+ * at least 2^(13-8S) times its row maximum); one rounding of y to fp16.
+ */
+int lse_int8_linear_packed_dt(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                              const float *scale, int64_t N, const void *residual, int64_t ldr, void *y, int64_t ldy,
+                              void *workspace, size_t workspace_bytes, int algo, void *stream);
+int lse_int8_gate_up_silu_packed_dt(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                                    const int8_t *w_packed, const float *scale, int64_t I, void *y, int64_t ldy,
+                                    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Paged decode attention, one query token per sequence (the decode-step call of the
  * reference's paged_attention_forward, src/llm_serving_engine/kernels/flash_attention.py:
  * 287-332, with q_len = 1 and query_offset = context_len - 1):
@@ -188,7 +204,9 @@ int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t
  *            bytes (0 allowed when that is 0), 16-byte aligned, zeroed once before its first
  *            use; the split-K arrival counters at its start have the same place for every
  *            launch shape and every call leaves them at zero, so one buffer per stream
- *            (grown when a shape needs more) serves all shapes
+ *            (grown when a shape needs more) serves all shapes.  workspace = NULL with
+ *            workspace_bytes = 0 asks for the unsplit launch (one CTA per sequence and KV head,
+ *            no workspace), available while max_context <= 1023 * block_size
  * D = 64 or 128 and G in {1, 2, 4, 8} (LSE_ERR_UNSUPPORTED otherwise).  fp32 softmax and
  * accumulation, one bf16 rounding of o.  A sequence with context_len 0 gets zeros.
  */

@@ -1,8 +1,8 @@
 // Activation digit planes for the int8 tensor-core kernel (sm_100a).
 //
 // The tensor-core kernel multiplies int8 weights by int8 activations (tcgen05.mma
-// kind::i8, exact int32 accumulation).  The bf16 activations are written, per token row m,
-// as a fixed-point integer in S signed 8-bit digits under a power-of-two row scale:
+// kind::i8, exact int32 accumulation).  The activations (bf16 or fp16, XT) are written, per
+// token row m, as a fixed-point integer in S signed 8-bit digits under a power-of-two row scale:
 //
 //   r[m] = 2^e[m],  v[m, k] = rint(x[m, k] / r[m]) = sum_p d_p[m, k] * 256^(S-1-p),
 //   d_p in [-128, 127]   (p = 0 the most significant digit plane)
@@ -11,9 +11,10 @@
 //
 // e[m] is the smallest exponent with max_k |x[m, k]| / 2^e <= V_S = 127 * (256^S - 1) / 255
 // (32639 for S = 2, 8355711 for S = 3), i.e. max |x| / 2^e in [2^(8S-2), 2^(8S-1)).
-// Hence every element with |x| >= max|x| * 2^(10-8S) (2^-6 of the row maximum for S = 2,
-// 2^-14 for S = 3) is represented exactly (its 8 significant bf16 bits sit at or above the
-// quantum), and any element's error is at most half a quantum, below max|x| * 2^-(8S-2).  A row
+// Hence every bf16 element with |x| >= max|x| * 2^(10-8S) (2^-6 of the row maximum for S = 2,
+// 2^-14 for S = 3) is represented exactly (its 8 significant bits sit at or above the quantum;
+// for fp16's 11 bits the bound is max|x| * 2^(13-8S)), and any element's error is at most half
+// a quantum, below max|x| * 2^-(8S-2).  A row
 // of zeros gets r = 1 and zero digits; a row holding a NaN or an infinity gets r = NaN (the
 // whole output row is NaN, as a matmul over it would be at least partly).
 //
@@ -22,10 +23,12 @@
 // [S planes][token tile][128 K bytes] as one K-major B operand of S * NT rows.
 //
 // One CTA per row, every load of the row in flight at once (up to 16,384 elements); CTA 0 also
-// clears the stream-K arrival counters of the projection launch that follows.  Programmatic dependent launch: the CTA releases its dependents on entry (the
-// projection kernel's weight copies start under it) and waits for the kernel that wrote x
-// before touching any memory.
+// clears the stream-K arrival counters of the projection launch that follows.  Programmatic
+// dependent launch: the CTA releases its dependents on entry (the projection kernel's weight
+// copies start under it) and waits for the kernel that wrote x before touching any memory.
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -41,8 +44,17 @@ struct Digits {
     static constexpr int kTopExp = 8 * S - 2;                // max|x| / 2^e in [2^kTopExp, 2^(kTopExp+1))
 };
 
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// The two activations (bf16 or fp16, XT) packed in a 32-bit word, as fp32 (exact).
+template <typename XT>
+__device__ __forceinline__ float act_lo(uint32_t w) {
+    if constexpr (std::is_same_v<XT, __half>) return __half2float(__ushort_as_half(static_cast<uint16_t>(w & 0xFFFFu)));
+    else return __uint_as_float(w << 16);
+}
+template <typename XT>
+__device__ __forceinline__ float act_hi(uint32_t w) {
+    if constexpr (std::is_same_v<XT, __half>) return __half2float(__ushort_as_half(static_cast<uint16_t>(w >> 16)));
+    else return __uint_as_float(w & 0xFFFF0000u);
+}
 
 // Balanced base-256 digits of v (|v| <= kMaxV), most significant first, packed per plane into
 // byte `slot & 3` of d[p].
@@ -69,7 +81,7 @@ __device__ __forceinline__ float exp2_exact(int k) { return __int_as_float((k + 
 
 // x / 2^e rounded to the nearest integer (ties to even) as inv_hi * inv_lo = 2^-e, each factor a
 // normal power of two, so both multiplications are exact: the quotient is below 2^(8S-1).
-template <int S>
+template <int S, typename XT>
 __device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_t plane_stride, int64_t row_off, int c,
                                              const uint4 &v, float inv_hi, float inv_lo, bool valid) {
     uint32_t d0[S] = {}, d1[S] = {};
@@ -79,7 +91,7 @@ __device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const float f = h ? bf16_hi(w[i]) : bf16_lo(w[i]);
+                const float f = h ? act_hi<XT>(w[i]) : act_lo<XT>(w[i]);
                 int q = __float2int_rn((f * inv_hi) * inv_lo);
                 q = max(-Digits<S>::kMaxV, min(Digits<S>::kMaxV, q));
                 const int slot = 2 * i + h;
@@ -93,9 +105,9 @@ __device__ __forceinline__ void store_digits(int8_t *__restrict__ planes, int64_
         *reinterpret_cast<uint2 *>(planes + p * plane_stride + row_off + 8 * c) = make_uint2(d0[p], d1[p]);
 }
 
-template <int S>
+template <int S, typename XT = __nv_bfloat16>
 __global__ void __launch_bounds__(THREADS)
-act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *__restrict__ planes,
+act_split_kernel(const XT *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *__restrict__ planes,
                  int64_t plane_stride, float *__restrict__ row_scale, int *__restrict__ counters, int n_counters) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
@@ -104,7 +116,7 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
     // zero for every launch without any invariant on the workspace's earlier contents.
     if (m == 0)
         for (int i = threadIdx.x; i < n_counters; i += THREADS) counters[i] = 0;
-    const __nv_bfloat16 *xr = x + static_cast<int64_t>(m) * ldx;
+    const XT *xr = x + static_cast<int64_t>(m) * ldx;
     const int nk = K >> 3;  // 8-element chunks (K % 16 == 0, rows 16-byte aligned)
     constexpr int BATCH = THREADS * CPT;
     uint4 v[CPT];
@@ -121,7 +133,7 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
             const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float a = fabsf(bf16_lo(w[k])), b = fabsf(bf16_hi(w[k]));
+                const float a = fabsf(act_lo<XT>(w[k])), b = fabsf(act_hi<XT>(w[k]));
                 bad |= !(a <= 3.4e38f) || !(b <= 3.4e38f);  // NaN or infinity
                 amax = fmaxf(amax, fmaxf(a, b));
             }
@@ -171,7 +183,7 @@ act_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int K, int Kp
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
             const int c = base + threadIdx.x + i * THREADS;
-            if (c < nkp) store_digits<S>(planes, plane_stride, row_off, c, v[i], inv_hi, inv_lo, c < nk && !bad);
+            if (c < nkp) store_digits<S, XT>(planes, plane_stride, row_off, c, v[i], inv_hi, inv_lo, c < nk && !bad);
         }
     }
     if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);

@@ -307,7 +307,7 @@ size_t tci8_workspace_bytes(int nt, int S, int grid, int64_t M, int64_t K) {
 template <int NT, int S, bool SILU>
 int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
                  const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws,
-                 bool packed, cudaStream_t st) {
+                 bool packed, cudaStream_t st, bool xf16) {
     const int64_t Kp = packed_cols(K);
     uint8_t *wsb = static_cast<uint8_t *>(ws);
     int *counters = reinterpret_cast<int *>(wsb);
@@ -321,9 +321,13 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
         cudaLaunchAttribute attr[1];
         launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(split::THREADS), 0, st);
         const int n_counters = pl.cluster >= 2 ? 0 : static_cast<int>(pl.tiles - pl.dp_tiles);
-        cudaError_t e = cudaLaunchKernelEx(&cfg, split::act_split_kernel<S>, static_cast<const __nv_bfloat16 *>(x), ldx,
-                                           static_cast<int>(K), static_cast<int>(Kp), planes, plane_stride, rscale,
-                                           counters, n_counters);
+        cudaError_t e = xf16 ? cudaLaunchKernelEx(&cfg, split::act_split_kernel<S, __half>, static_cast<const __half *>(x),
+                                                  ldx, static_cast<int>(K), static_cast<int>(Kp), planes, plane_stride,
+                                                  rscale, counters, n_counters)
+                             : cudaLaunchKernelEx(&cfg, split::act_split_kernel<S, __nv_bfloat16>,
+                                                  static_cast<const __nv_bfloat16 *>(x), ldx, static_cast<int>(K),
+                                                  static_cast<int>(Kp), planes, plane_stride, rscale, counters,
+                                                  n_counters);
         if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) { set_cuda_error(e, "act_split launch"); return LSE_ERR_CUDA; }
     }
@@ -341,9 +345,10 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
     p.M = static_cast<int>(M);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
-    p.y = static_cast<__nv_bfloat16 *>(y);
+    p.y = static_cast<uint16_t *>(y);
+    p.y_f16 = xf16 ? 1 : 0;
     p.ldy = ldy;
-    p.res = static_cast<const __nv_bfloat16 *>(res);
+    p.res = static_cast<const uint16_t *>(res);
     p.ldr = ldr;
     p.scale = scale;
     p.row_scale = rscale;
@@ -389,9 +394,9 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
 template <bool SILU>
 int run_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
               const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
-              cudaStream_t st) {
-    if (pl.nt == 64) return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st);
-    return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st);
+              cudaStream_t st, bool xf16 = false) {
+    if (pl.nt == 64) return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
+    return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
 }
 
 template <int MT, int ROWS>
@@ -429,18 +434,18 @@ int skinny_prefetch_groups() {
     return v;
 }
 
-template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false, typename XT = __nv_bfloat16>
 cudaError_t launch_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
                           int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, cudaStream_t st) {
     const int64_t row_blocks = SILU_MUL ? N / 8 : (N + 15) / 16;  // weight row blocks (SILU_MUL: 2N rows)
     dim3 grid(static_cast<unsigned>((row_blocks + R - 1) / R), static_cast<unsigned>((M + 8 * MT - 1) / (8 * MT)));
-    auto kernel = skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL>;
+    auto kernel = skinny_i8_kernel<MT, KW, R, U, BF16, MINB, SILU_MUL, XT>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     launch_config(cfg, attr, grid, dim3(KW * 32), 0, st);
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<const __nv_bfloat16 *>(x), ldx,
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<const XT *>(x), ldx,
                               static_cast<int>(M), static_cast<int>(K), wp, scale, static_cast<int>(N),
-                              static_cast<__nv_bfloat16 *>(y), ldy, static_cast<const __nv_bfloat16 *>(res), ldr,
+                              static_cast<XT *>(y), ldy, static_cast<const XT *>(res), ldr,
                               static_cast<int>(packed_cols(K)),
                               MT == 1 ? skinny_prefetch_groups() : 0);
 }
@@ -515,15 +520,47 @@ cudaError_t launch_skinny_mt(int variant, const void *x, int64_t M, int64_t K, i
     }
 }
 
+// fp16 activations: the fp16 MMA at every token count, in the shapes the bf16 policy above
+// picks for the same weight (the activations enter the MMA as they are).
+template <int MT, bool SILU = false>
+cudaError_t launch_skinny_f16(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale,
+                              int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, int num_sms,
+                              cudaStream_t st) {
+    const int64_t rb_per_sm = (SILU ? N / 8 : (N + 15) / 16) / num_sms;
+    if (rb_per_sm >= 4) {
+        if constexpr (MT == 1) return launch_skinny<1, 8, 1, 4, false, 4, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+        else return launch_skinny<MT, 8, 2, 4, false, 2, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+    }
+    if (rb_per_sm >= 2) {
+        if (SILU || MT == 4) return launch_skinny<MT, 8, 2, 4, false, 2, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+        if constexpr (MT == 1) return launch_skinny<1, 8, 2, 8, false, 2, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+        else return launch_skinny<MT, 8, 1, 8, false, 3, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+    }
+    if constexpr (MT == 1) {
+        if (!SILU && K >= 8192) return launch_skinny<1, 16, 2, 4, false, 1, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+        return launch_skinny<1, 16, 1, 4, false, 2, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+    } else if constexpr (MT == 2) {
+        return launch_skinny<2, 16, 2, 4, false, 1, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+    } else {
+        return launch_skinny<4, 8, 1, 4, false, 2, SILU, __half>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, st);
+    }
+}
+
 constexpr int64_t kSkinnyMaxM = 32;  // the decode kernel's token range (four 8-token tiles)
 
 int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *wp, const float *scale, int64_t N,
-               void *y, int64_t ldy, const void *res, int64_t ldr, int num_sms, cudaStream_t st) {
+               void *y, int64_t ldy, const void *res, int64_t ldr, int num_sms, cudaStream_t st, bool xf16 = false) {
     if (M > kSkinnyMaxM) return LSE_ERR_UNSUPPORTED;
     const int variant = skinny_variant();
-    cudaError_t e = M <= 8    ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
-                    : M <= 16 ? launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
-                              : launch_skinny_mt<4>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st);
+    cudaError_t e;
+    if (xf16)
+        e = M <= 8    ? launch_skinny_f16<1>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+            : M <= 16 ? launch_skinny_f16<2>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+                      : launch_skinny_f16<4>(x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st);
+    else
+        e = M <= 8    ? launch_skinny_mt<1>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+            : M <= 16 ? launch_skinny_mt<2>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st)
+                      : launch_skinny_mt<4>(variant, x, M, K, ldx, wp, scale, N, y, ldy, res, ldr, num_sms, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
@@ -585,7 +622,7 @@ namespace {
 // same thread.
 int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w, const float *scale, int64_t N,
                 void *y, int64_t ldy, void *workspace, size_t workspace_bytes, int algo, bool packed, void *stream,
-                const void *res = nullptr, int64_t ldr = 0) {
+                const void *res = nullptr, int64_t ldr = 0, bool xf16 = false) {
     if (M < 0 || N < 0 || K < 0) return LSE_ERR_INVALID_ARG;
     if (M == 0 || N == 0) return LSE_OK;
     if (!x || !w || !scale || !y) return LSE_ERR_INVALID_ARG;
@@ -612,15 +649,16 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
         return LSE_OK;
     }
     if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed);
+    if (xf16 && !packed) return LSE_ERR_UNSUPPORTED;  // fp16 activations: packed weights only
     if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);  // row-major: no res
     if (algo == LSE_ALGO_SKINNY)
-        return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, res, ldr, g_dev[dev].num_sms, st);
+        return run_skinny(x, M, K, ldx, w, scale, N, y, ldy, res, ldr, g_dev[dev].num_sms, st, xf16);
 
     const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
     if (!workspace || !aligned16(workspace) ||
         workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;
-    return run_tc_i8<false>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st);
+    return run_tc_i8<false>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, workspace, packed, st, xf16);
 }
 }  // namespace
 }  // namespace lse
@@ -948,17 +986,21 @@ extern "C" int lse_int8_linear_packed_noalloc(const void *x, int64_t M, int64_t 
 }
 
 // ---------------------------------------------------------------------------------------
-// lse_int8_gate_up_silu_packed: the MLP's gate and up projections and SiLU * mul in one
-// decode-kernel launch (M <= 16).
+// The MLP's gate and up projections and SiLU * mul in one projection launch: M <= 16 on the
+// decode kernel (workspace unused), larger M on the tensor-core kernel with SiLU * mul in its
+// epilogue (tc_i8.cuh, SILU = true), after the activation split.
 // ---------------------------------------------------------------------------------------
-extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
-                                            const float *scale, int64_t I, void *y, int64_t ldy, void *stream) {
+namespace lse {
+namespace {
+int gate_up_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed, const float *scale,
+                 int64_t I, void *y, int64_t ldy, void *workspace, size_t workspace_bytes, void *stream, bool xf16,
+                 bool decode_only) {
     if (M < 0 || I < 0 || K < 0) return LSE_ERR_INVALID_ARG;
     if (M == 0 || I == 0) return LSE_OK;
     if (!x || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
     if (ldx < K || ldy < I) return LSE_ERR_INVALID_ARG;
     if (I % 8) return LSE_ERR_UNSUPPORTED;
-    if (M > 16 || 2 * I > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((decode_only && M > 16) || M > INT32_MAX || 2 * I > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
     if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
     if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
     int dev = 0;
@@ -971,49 +1013,70 @@ extern "C" int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K,
         if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
         return LSE_OK;
     }
-    const int variant = skinny_variant();
     const int num_sms = g_dev[dev].num_sms;
-    cudaError_t e = M <= 8 ? launch_skinny_mt<1, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st)
-                           : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
-    return LSE_OK;
-}
-
-// ---------------------------------------------------------------------------------------
-// lse_int8_gate_up_silu_packed_ws: the same for any M, with a workspace: M <= 16 on the
-// decode kernel (workspace unused), larger M on the tensor-core kernel with SiLU * mul in its
-// epilogue (tc_i8.cuh, SILU = true), after the activation split.
-// ---------------------------------------------------------------------------------------
-extern "C" int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t ldx,
-                                               const int8_t *w_packed, const float *scale, int64_t I, void *y,
-                                               int64_t ldy, void *workspace, size_t workspace_bytes, void *stream) {
-    if (M >= 0 && M <= 16) return lse_int8_gate_up_silu_packed(x, M, K, ldx, w_packed, scale, I, y, ldy, stream);
-    if (M < 0 || I < 0 || K < 0) return LSE_ERR_INVALID_ARG;
-    if (I == 0) return LSE_OK;
-    if (!x || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
-    if (ldx < K || ldy < I) return LSE_ERR_INVALID_ARG;
-    if (I % 8) return LSE_ERR_UNSUPPORTED;
-    if (M > INT32_MAX || 2 * I > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
-    if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed)) return LSE_ERR_ALIGNMENT;
-    if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
-    int dev = 0;
-    int rc = current_device(&dev);
-    if (rc) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (K == 0) {  // silu(0) * 0
-        const cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(I) * 2,
-                                                static_cast<size_t>(M), st);
-        if (e != cudaSuccess) { set_cuda_error(e, "cudaMemset2DAsync"); return LSE_ERR_CUDA; }
+    if (M <= 16) {
+        const int variant = skinny_variant();
+        cudaError_t e;
+        if (xf16)
+            e = M <= 8 ? launch_skinny_f16<1, true>(x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st)
+                       : launch_skinny_f16<2, true>(x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st);
+        else
+            e = M <= 8 ? launch_skinny_mt<1, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st)
+                       : launch_skinny_mt<2, true>(variant, x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, num_sms, st);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) { set_cuda_error(e, "skinny_i8 gate_up launch"); return LSE_ERR_CUDA; }
         return LSE_OK;
     }
     const int64_t N = 2 * I;
-    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
+    const TcPlan pl = plan_tc(M, K, N, num_sms, dev);
     if (!workspace || !aligned16(workspace) ||
         workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K))
         return LSE_ERR_WORKSPACE;
-    return run_tc_i8<true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st);
+    return run_tc_i8<true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st, xf16);
 }
+
+int activation_type(int dtype, bool *xf16) {
+    if (dtype == LSE_BF16) *xf16 = false;
+    else if (dtype == LSE_F16) *xf16 = true;
+    else return LSE_ERR_UNSUPPORTED;
+    return LSE_OK;
+}
+}  // namespace
+}  // namespace lse
+
+extern "C" {
+
+int lse_int8_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                                 const float *scale, int64_t I, void *y, int64_t ldy, void *stream) {
+    return gate_up_impl(x, M, K, ldx, w_packed, scale, I, y, ldy, nullptr, 0, stream, false, true);
+}
+
+int lse_int8_gate_up_silu_packed_ws(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                                    const float *scale, int64_t I, void *y, int64_t ldy, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+    return gate_up_impl(x, M, K, ldx, w_packed, scale, I, y, ldy, workspace, workspace_bytes, stream, false, false);
+}
+
+int lse_int8_gate_up_silu_packed_dt(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                                    const int8_t *w_packed, const float *scale, int64_t I, void *y, int64_t ldy,
+                                    void *workspace, size_t workspace_bytes, void *stream) {
+    bool xf16 = false;
+    const int rc = activation_type(dtype, &xf16);
+    if (rc) return rc;
+    return gate_up_impl(x, M, K, ldx, w_packed, scale, I, y, ldy, workspace, workspace_bytes, stream, xf16, false);
+}
+
+int lse_int8_linear_packed_dt(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, const int8_t *w_packed,
+                              const float *scale, int64_t N, const void *residual, int64_t ldr, void *y, int64_t ldy,
+                              void *workspace, size_t workspace_bytes, int algo, void *stream) {
+    bool xf16 = false;
+    const int rc = activation_type(dtype, &xf16);
+    if (rc) return rc;
+    return linear_impl(x, M, K, ldx, w_packed, scale, N, y, ldy, workspace, workspace_bytes, algo, true, stream,
+                       residual, residual ? ldr : 0, xf16);
+}
+
+}  // extern "C"
 
 // ---------------------------------------------------------------------------------------
 // lse_paged_decode_attention: decode attention over the paged K/V pool (decode_attn.cuh).
@@ -1061,13 +1124,14 @@ int attn_target_ctas(int num_sms) {
     return v > 0 ? v : 3 * num_sms / 2;
 }
 
-AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_size, int num_sms) {
+AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_size, int num_sms,
+                   bool unsplit = false) {
     const int64_t pairs = std::max<int64_t>(1, E * H_kv);
     const int64_t min_chunk = attn_min_chunk();
     const int64_t target = attn_target_ctas(num_sms);
     const int64_t cap = std::max<int64_t>(1, (max_context + min_chunk - 1) / min_chunk);
     int64_t splits = 1;
-    if (2 * pairs <= target && pairs <= kAttnMaxSplitPairs) splits = std::min<int64_t>(target / pairs, cap);
+    if (!unsplit && 2 * pairs <= target && pairs <= kAttnMaxSplitPairs) splits = std::min<int64_t>(target / pairs, cap);
     // a CTA stages at most attn::MAX_TABLE block-table entries (chunk / block_size + 1)
     const int64_t max_chunk = (attn::MAX_TABLE - 1) * block_size / 32 * 32;
     splits = std::max<int64_t>(splits, (max_context + max_chunk - 1) / max_chunk);
@@ -1152,7 +1216,9 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
         }
         return LSE_OK;
     }
-    const AttnPlan pl = plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms);
+    // No workspace at all: one CTA per (sequence, KV head) wherever the context allows.
+    const AttnPlan pl = plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms,
+                                  workspace == nullptr && workspace_bytes == 0);
     if (pl.splits > attn::MAX_SPLITS) return LSE_ERR_UNSUPPORTED;  // a very long context at block_size < 16
     const size_t need = attn_workspace_bytes(pl, E, H, H_kv, D);
     if (need && (!workspace || workspace_bytes < need || !aligned16(workspace))) return LSE_ERR_WORKSPACE;

@@ -9,12 +9,12 @@
 // in block block_table[e, p / block_size], slot p % block_size), q and o [H, tokens, D] with
 // any head and token strides (d contiguous), element type bf16 or fp16.
 //
-// Shape: grid (token tiles, entries, KV heads).  A CTA takes 64 rows = the G query heads of
-// 64 / G consecutive tokens of one entry, all reading the same KV head, so every K/V tile it
-// stages serves the whole group (the G-fold reuse a per-head program would read again).  Four
+// Shape: grid (token tiles, entries, KV heads).  A CTA takes 128 rows = the G query heads of
+// 128 / G consecutive tokens of one entry, all reading the same KV head, so every K/V tile it
+// stages serves the whole group (the G-fold reuse a per-head program would read again).  Eight
 // warps, 16 rows each:
-//   * K/V tiles of 64 positions are staged in shared memory by cp.async from all 128 threads,
-//     two tiles in flight; rows are 16-byte-chunk swizzled (chunk c of row r at c ^ (r & 7)) so
+//   * K/V tiles of 64 positions are staged in shared memory by cp.async from all 256 threads,
+//     three tiles in flight; rows are 16-byte-chunk swizzled (chunk c of row r at c ^ (r & 7)) so
 //     ldmatrix reads them without bank conflicts;
 //   * S = Q K^T on warp MMAs (m16n8k16, fp32 accumulate) with Q held in registers as the row
 //     operand; causal and context masks on the accumulators; online softmax in base 2 per row;
@@ -33,11 +33,11 @@
 namespace lse {
 namespace pattn {
 
-constexpr int WARPS = 4;
+constexpr int WARPS = 8;
 constexpr int THREADS = WARPS * 32;
 constexpr int ROWS = WARPS * 16;  // (token, head) rows per CTA
 constexpr int KEYS = 64;          // positions per K/V tile
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 
 template <int D>
 constexpr int smem_bytes() { return STAGES * 2 * KEYS * D * 2; }
@@ -54,6 +54,14 @@ struct Params {
     int H_kv, block_size, num_blocks;
     float scale_log2;          // softmax scale * log2(e)
 };
+
+// 2^x (the SFU's approximation: relative error ~2^-22, subnormal results flushed to 0;
+// 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // D (16x8 fp32) += A (16x16, row) * B (16x8, col), A and B of element type T
 template <typename T>
@@ -84,7 +92,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 template <int D, int G, typename T>
-__global__ void __launch_bounds__(THREADS) paged_attn_kernel(const Params p) {
+__global__ void __launch_bounds__(THREADS, 1) paged_attn_kernel(const Params p) {
     static_assert(D == 64 || D == 128, "head_dim");
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head");
     constexpr int TOKS = ROWS / G;     // tokens per CTA
@@ -169,10 +177,13 @@ __global__ void __launch_bounds__(THREADS) paged_attn_kernel(const Params p) {
 
     const int ntiles = (kend + KEYS - 1) / KEYS;
     if (ntiles > 0) issue(0, 0);
+    if (ntiles > 1) issue(KEYS, 1);
     for (int it = 0; it < ntiles; ++it) {
-        const int st = it & 1;
-        if (it + 1 < ntiles) {
-            issue((it + 1) * KEYS, st ^ 1);
+        const int st = it % STAGES;
+        if (it + 2 < ntiles) {
+            issue((it + 2) * KEYS, (it + 2) % STAGES);  // the stage tile it - 1 used: free since its barrier
+            asm volatile("cp.async.wait_group 2;" ::: "memory");
+        } else if (it + 1 < ntiles) {
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -201,35 +212,41 @@ __global__ void __launch_bounds__(THREADS) paged_attn_kernel(const Params p) {
                 }
             }
         }
-        // masks and online softmax (base 2): this lane holds, per score tile n, positions
-        // kb0 + 8n + 2q4 (+1) of row a (s[n][0..1]) and row b (s[n][2..3])
+        // masks and online softmax (base 2, scale folded into one FMA per score): this lane
+        // holds, per score tile n, positions kb0 + 8n + 2q4 (+1) of row a (s[n][0..1]) and row b
+        // (s[n][2..3]).  A tile every row of the CTA sees in full needs no mask.
+        const float c = p.scale_log2;
+        if (kb0 + KEYS > min(ctx, qoff + t0 + 1)) {
+#pragma unroll
+            for (int n = 0; n < SN; ++n)
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int pos = kb0 + 8 * n + 2 * q4 + u;
+                    if (pos >= lim_a) s[n][u] = NEG_INF;
+                    if (pos >= lim_b) s[n][2 + u] = NEG_INF;
+                }
+        }
         float mxa = NEG_INF, mxb = NEG_INF;
 #pragma unroll
-        for (int n = 0; n < SN; ++n)
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int pos = kb0 + 8 * n + 2 * q4 + u;
-                const float sa = pos < lim_a ? s[n][u] * p.scale_log2 : NEG_INF;
-                const float sb = pos < lim_b ? s[n][2 + u] * p.scale_log2 : NEG_INF;
-                s[n][u] = sa;
-                s[n][2 + u] = sb;
-                mxa = fmaxf(mxa, sa);
-                mxb = fmaxf(mxb, sb);
-            }
+        for (int n = 0; n < SN; ++n) {
+            mxa = fmaxf(mxa, fmaxf(s[n][0], s[n][1]));
+            mxb = fmaxf(mxb, fmaxf(s[n][2], s[n][3]));
+        }
         mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
         mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
         mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
         mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-        const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
-        const float alpha_a = mna == NEG_INF ? 1.f : exp2f(m_a - mna);
-        const float alpha_b = mnb == NEG_INF ? 1.f : exp2f(m_b - mnb);
+        const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);  // raw (unscaled) running maxima
+        const float alpha_a = mna == NEG_INF ? 1.f : ex2((m_a - mna) * c);
+        const float alpha_b = mnb == NEG_INF ? 1.f : ex2((m_b - mnb) * c);
+        const float mca = mna == NEG_INF ? 0.f : mna * c, mcb = mnb == NEG_INF ? 0.f : mnb * c;
         float psa = 0.f, psb = 0.f;
 #pragma unroll
         for (int n = 0; n < SN; ++n)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-                s[n][u] = s[n][u] == NEG_INF ? 0.f : exp2f(s[n][u] - mna);
-                s[n][2 + u] = s[n][2 + u] == NEG_INF ? 0.f : exp2f(s[n][2 + u] - mnb);
+                s[n][u] = ex2(fmaf(s[n][u], c, -mca));  // a masked score gives 2^-inf = 0
+                s[n][2 + u] = ex2(fmaf(s[n][2 + u], c, -mcb));
                 psa += s[n][u];
                 psb += s[n][2 + u];
             }

@@ -97,11 +97,16 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int j) {
 // of the same tokens, and the epilogue writes y[m, 8b + r0] = silu(s_g * gate) * (s_u * up)
 // (fp32, one bf16 rounding) for the N = I intermediate columns; `scale` is interleaved the
 // same way.
-template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false>
+//
+// XT is the activation type of x, y and res: bf16, or fp16 (then the MMA is fp16 and the
+// activations enter it as they are).
+template <int MT, int KW, int R, int U, bool BF16, int MINB, bool SILU_MUL = false, typename XT = __nv_bfloat16>
 __global__ void __launch_bounds__(KW * 32, MINB)
-skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
+skinny_i8_kernel(const XT *__restrict__ x, int64_t ldx, int M, int K,
                  const int8_t *__restrict__ wp, const float *__restrict__ scale, int N,
-                 __nv_bfloat16 *y, int64_t ldy, const __nv_bfloat16 *res, int64_t ldr, int Kp, int pf_groups) {
+                 XT *y, int64_t ldy, const XT *res, int64_t ldr, int Kp, int pf_groups) {
+    constexpr bool XF16 = std::is_same_v<XT, __half>;
+    static_assert(!(XF16 && BF16), "fp16 activations take the fp16 MMA");
     constexpr int UB = U >= 2 ? U / 2 : 1;  // 64-column units per row block in registers
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int rg = blockIdx.x;
@@ -165,8 +170,8 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
     // Activation rows this lane feeds as the B fragment of token tile t: token m0 + 8t + r0,
     // columns 16q..16q+15 of each unit.  A token past M reads the last real row instead: its
     // MMA column is independent of the others and is never stored.
-    const __nv_bfloat16 *xbase[MT];
-    const __nv_bfloat16 *xp[MT];
+    const XT *xbase[MT];
+    const XT *xp[MT];
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
         const int m = min(m0 + 8 * t + r0, M - 1);
@@ -195,7 +200,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
                 const uint32_t lo = jj ? xv[t].z : xv[t].x, hi = jj ? xv[t].w : xv[t].y;
-                if constexpr (BF16) {
+                if constexpr (BF16 || XF16) {
                     bx[t][jj][0] = lo;
                     bx[t][jj][1] = hi;
                 } else {
@@ -327,7 +332,7 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
                             vu += red[w][r][t][2 + jj][lane];
                         }
                         const float g = vg * sg, u = vu * su;
-                        y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
+                        y[static_cast<int64_t>(m) * ldy + n] = from_float<XT>(g / (1.f + expf(-g)) * u);
                     }
                 }
             }
@@ -348,8 +353,8 @@ skinny_i8_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, int M, int K,
 #pragma unroll
                     for (int w = 0; w < KW; ++w) v += red[w][r][t][j][lane];
                     v *= sc;
-                    if (res) v += __bfloat162float(res[static_cast<int64_t>(m) * ldr + n]);
-                    y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(v);
+                    if (res) v += to_float(res[static_cast<int64_t>(m) * ldr + n]);
+                    y[static_cast<int64_t>(m) * ldy + n] = from_float<XT>(v);
                 }
             }
         }

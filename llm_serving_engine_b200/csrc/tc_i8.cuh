@@ -104,10 +104,11 @@ struct Cfg {
 
 struct Params {
     int M, N, K;
-    __nv_bfloat16 *y;
+    uint16_t *y;               // bf16, or fp16 when y_f16 (the activation type)
     int64_t ldy;
-    const __nv_bfloat16 *res;  // null, or the residual added before rounding (may alias y)
+    const uint16_t *res;       // null, or the residual added before rounding (may alias y), same type
     int64_t ldr;
+    int y_f16;
     const float *scale;        // s[n]
     const float *row_scale;    // r[m] (act_split)
     float *partials;           // [2 * grid][NT][BN] fp32 partial tiles
@@ -161,6 +162,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
 // few fp32 ulp, far below the one bf16 rounding of the result); for a below about -88 the
 // exponential overflows and the quotient is -0, the limit of silu.
 __device__ __forceinline__ float silu_fast(float a) { return __fdividef(a, 1.f + __expf(-a)); }
+
+// The activation type of y and the residual is bf16 or fp16 (p.y_f16, uniform in a launch).
+__device__ __forceinline__ uint16_t out_bits(const Params &p, float v) {
+    return p.y_f16 ? __half_as_ushort(__float2half_rn(v)) : __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ float res_value(const Params &p, int64_t i) {
+    const uint16_t b = p.res[i];
+    return p.y_f16 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+}
 
 // ---- schedule (identical in every role and on the host) -----------------------------------
 __device__ __forceinline__ long long sk_begin(const Params &p, int c) { return p.sk_units * c / p.grid; }
@@ -275,24 +285,24 @@ __device__ __forceinline__ void finish_quad(const Params &p, float4 acc, int j, 
                              __shfl_xor_sync(0xffffffffu, acc.z, 2), __shfl_xor_sync(0xffffffffu, acc.w, 2)};
         if (j >= mval || (rq & 8)) return;
         const float g4[4] = {acc.x, acc.y, acc.z, acc.w};
-        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
+        uint16_t *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
 #pragma unroll
         for (int e = 0; e < 4; ++e)
             if (n + e < p.N) {
                 const float g = g4[e] * (__ldg(p.scale + n + e) * rs);
                 const float u = u4[e] * (__ldg(p.scale + n + 8 + e) * rs);
-                yr[e] = __float2bfloat16_rn(silu_fast(g) * u);
+                yr[e] = out_bits(p, silu_fast(g) * u);
             }
     } else {
         if (j >= mval) return;
-        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+        uint16_t *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
             if (n + e < p.N) {
                 float o = a4[e] * (__ldg(p.scale + n + e) * rs);
-                if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
-                yr[e] = __float2bfloat16_rn(o);
+                if (p.res) o += res_value(p, static_cast<int64_t>(m0 + j) * p.ldr + n + e);
+                yr[e] = out_bits(p, o);
             }
     }
 }
@@ -310,21 +320,21 @@ __device__ __forceinline__ void finish_quad_scaled(const Params &p, float4 acc, 
         const float g4[4] = {acc.x, acc.y, acc.z, acc.w};
         const float sg[4] = {s4.x, s4.y, s4.z, s4.w};
         const float su[4] = {s4u.x, s4u.y, s4u.z, s4u.w};
-        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
+        uint16_t *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + (n >> 4) * 8 + (n & 7);
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-            if (n + e < p.N) yr[e] = __float2bfloat16_rn(silu_fast(g4[e] * (sg[e] * rs)) * (u4[e] * (su[e] * rs)));
+            if (n + e < p.N) yr[e] = out_bits(p, silu_fast(g4[e] * (sg[e] * rs)) * (u4[e] * (su[e] * rs)));
     } else {
         if (j >= mval) return;
-        __nv_bfloat16 *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
+        uint16_t *yr = p.y + static_cast<int64_t>(m0 + j) * p.ldy + n;
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
         const float sc[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
             if (n + e < p.N) {
                 float o = a4[e] * (sc[e] * rs);
-                if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + j) * p.ldr + n + e]);
-                yr[e] = __float2bfloat16_rn(o);
+                if (p.res) o += res_value(p, static_cast<int64_t>(m0 + j) * p.ldr + n + e);
+                yr[e] = out_bits(p, o);
             }
     }
 }
@@ -579,7 +589,7 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
                         const float a = combine_planes<S>(d) * (sc * rs);
                         const float u = __shfl_xor_sync(0xffffffffu, a, 8);
                         if (!(lane & 8) && n_ok && c0 + j < mval)
-                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + col] = __float2bfloat16_rn(silu_fast(a) * u);
+                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + col] = out_bits(p, silu_fast(a) * u);
                     }
                 } else if (whole) {
 #pragma unroll
@@ -590,8 +600,8 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
                         const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
                         if (n_ok && c0 + j < mval) {
                             float o = combine_planes<S>(d) * (sc * rs);
-                            if (p.res) o += __bfloat162float(p.res[static_cast<int64_t>(m0 + c0 + j) * p.ldr + n]);
-                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + n] = __float2bfloat16_rn(o);
+                            if (p.res) o += res_value(p, static_cast<int64_t>(m0 + c0 + j) * p.ldr + n);
+                            p.y[static_cast<int64_t>(m0 + c0 + j) * p.ldy + n] = out_bits(p, o);
                         }
                     }
                 } else {

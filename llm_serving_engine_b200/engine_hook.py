@@ -34,10 +34,19 @@ __all__ = ["enable_int8", "bind_paged_attention", "install", "uninstall", "insta
 
 
 def _attend_paged(runner, q, layer_idx, paging):
-    """`ModelRunner.attend_paged` on this package's kernel: same arguments, same result."""
-    return ops.paged_attention(q, runner._k_pool[layer_idx], runner._v_pool[layer_idx], paging.block_table,
-                               paging.context_len, paging.query_offset, paging.q_start, paging.q_len,
-                               runner._block_size, paging.max_q_len)
+    """`ModelRunner.attend_paged` on this package's kernels: same arguments, same result.  A
+    batch of single-token entries (every decode step; their rows are the entries in order) in
+    bf16 takes the decode kernel, unsplit (no workspace, so any capture stream records it); any
+    other batch the multi-token kernel."""
+    k_pool, v_pool = runner._k_pool[layer_idx], runner._v_pool[layer_idx]
+    E = paging.block_table.shape[0]
+    if paging.max_q_len == 1 and q.shape[1] == E and q.dtype == torch.bfloat16:
+        max_context = paging.block_table.shape[1] * runner._block_size
+        o = ops.paged_decode_attention(q.transpose(0, 1), k_pool, v_pool, paging.block_table, paging.context_len,
+                                       max_context, split=False)
+        return o.transpose(0, 1)
+    return ops.paged_attention(q, k_pool, v_pool, paging.block_table, paging.context_len, paging.query_offset,
+                               paging.q_start, paging.q_len, runner._block_size, paging.max_q_len)
 
 
 def bind_paged_attention(runner):

@@ -40,6 +40,9 @@ from . import ops
 __all__ = ["Int8Linear", "FusedInt8QKV", "Int8LlamaMLP", "quantize_llama_", "int8_weight_bytes"]
 
 
+_NATIVE = (torch.bfloat16, torch.float16)
+
+
 def _to_bf16(x: torch.Tensor) -> torch.Tensor:
     return x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
 
@@ -91,12 +94,14 @@ class Int8Linear(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """`x @ W.T`, or `residual + x @ W.T` rounded once (the decoder's residual add fused
-        into the kernel; bf16 models only)."""
-        if residual is not None and x.dtype != torch.bfloat16:
+        into the kernel).  bf16 and fp16 activations run natively (one `lse::int8_linear`
+        dispatcher call); other dtypes go through bf16."""
+        if x.dtype in _NATIVE and (residual is None or residual.dtype == x.dtype):
+            return ops.torch_ops().int8_linear(x, self.weight_packed, self.scale, self.out_features, self.in_features,
+                                               residual)
+        if residual is not None:
             return residual + self.forward(x)
-        y = ops.int8_linear_packed(_to_bf16(x), self.weight_packed, self.scale, self.out_features, self.in_features,
-                                   residual=residual)
-        return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
+        return self.forward(_to_bf16(x)).to(x.dtype)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, int8 per-channel, packed"
@@ -214,21 +219,19 @@ class Int8LlamaMLP(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """`down(act(gate(x)) * up(x))`, plus `residual` added in the down projection's
-        epilogue when given (bf16)."""
-        if residual is not None and x.dtype != torch.bfloat16:
-            return residual + self.forward(x)
+        epilogue when given.  bf16 and fp16 run natively; other dtypes go through bf16."""
+        if x.dtype not in _NATIVE or (residual is not None and residual.dtype != x.dtype):
+            if residual is not None:
+                return residual + self.forward(x)
+            return self.forward(_to_bf16(x)).to(x.dtype)
         I = self.intermediate_size
-        lead = x.shape[:-1]
-        x2 = _to_bf16(x).reshape(-1, x.shape[-1])
         if self._silu():
-            h = ops.int8_gate_up_silu_packed(x2, self.gate_up.weight_packed, self.gate_up.scale, I,
+            h = ops.torch_ops().gate_up_silu(x, self.gate_up.weight_packed, self.gate_up.scale, I,
                                              self.gate_up.in_features)
         else:
-            gu = self.gate_up(x2).view(-1, I // 8, 2, 8)
-            h = (self.act(gu[:, :, 0]) * gu[:, :, 1]).reshape(-1, I)
-        r2 = None if residual is None else residual.reshape(-1, residual.shape[-1])
-        y = self.down_proj(h, residual=r2).reshape(*lead, -1)
-        return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
+            gu = self.gate_up(x).view(*x.shape[:-1], I // 8, 2, 8)
+            h = (self.act(gu[..., 0, :]) * gu[..., 1, :]).reshape(*x.shape[:-1], I)
+        return self.down_proj(h, residual=residual)
 
 
 def quantize_llama_(model: nn.Module, fuse: bool = True, lm_head: bool = False) -> nn.Module:

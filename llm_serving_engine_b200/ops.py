@@ -25,6 +25,7 @@ import torch
 from . import _lib
 
 __all__ = [
+    "torch_ops",
     "int8_linear",
     "int8_linear_packed",
     "pack_weight",
@@ -35,6 +36,8 @@ __all__ = [
     "int8_gate_up_silu_packed",
     "GATE_UP_SILU_MAX_M",
     "paged_decode_attention",
+    "paged_attention",
+    "set_wait_limit",
     "rope_kv_write",
     "rms_norm",
     "pool_slot_offsets",
@@ -55,6 +58,29 @@ _DTYPE_CODES = {torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16, torch.
 
 _inited: set[int] = set()
 _ws_lock = threading.Lock()
+_torch_ops_lock = threading.Lock()
+_torch_ops_loaded = False
+
+
+def torch_ops():
+    """`torch.ops.lse` with `int8_linear` and `gate_up_silu` registered (liblse_torch.so, the
+    C++ operators over the C ABI: one dispatcher call per projection).  Built in-tree on first
+    use if missing."""
+    global _torch_ops_loaded
+    if not _torch_ops_loaded:
+        with _torch_ops_lock:
+            if not _torch_ops_loaded:
+                import os
+
+                from . import build as _build
+
+                _lib.load()  # the C ABI library the operators link to, built if missing
+                path = _build.TORCH_LIB_PATH
+                if not os.path.exists(path):
+                    _build.build_torch_ops()
+                torch.ops.load_library(path)
+                _torch_ops_loaded = True
+    return torch.ops.lse
 
 
 def _ensure_device(device: torch.device) -> None:
@@ -79,8 +105,8 @@ def _check_x(x: torch.Tensor, K: int, *tensors: torch.Tensor) -> None:
         raise RuntimeError("int8_linear runs on CUDA only (no CPU fallback)")
     if any(t.device != x.device for t in tensors):
         raise ValueError(f"int8_linear: tensors on different devices ({x.device}, {[t.device for t in tensors]})")
-    if x.dtype != torch.bfloat16:
-        raise ValueError(f"int8_linear: x must be bfloat16, got {x.dtype}")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"int8_linear: x must be bfloat16 or float16, got {x.dtype}")
     if x.shape[-1] != K:
         raise ValueError(f"int8_linear: x last dim {x.shape[-1]} != in_features {K}")
     if K % 16 != 0:
@@ -94,19 +120,21 @@ def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, ou
     if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
         x2 = x2.contiguous()
     M = x2.shape[0]
+    if not packed and x.dtype != torch.bfloat16:
+        raise ValueError("int8_linear: row-major weights take bf16 activations (fp16: the packed layout)")
     if out is None:
-        y2 = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        y2 = torch.empty((M, N), dtype=x.dtype, device=x.device)
         y = y2.view(*lead, N)
     else:
-        if out.dtype != torch.bfloat16 or out.shape != (*lead, N) or out.stride(-1) != 1:
-            raise ValueError("int8_linear: out must be bf16 [..., N] with a contiguous last dim")
+        if out.dtype != x.dtype or out.shape != (*lead, N) or out.stride(-1) != 1:
+            raise ValueError("int8_linear: out must be [..., N] of x's dtype with a contiguous last dim")
         y = out
         y2 = out.view(-1, N) if M > 0 else out.reshape(0, N)
     r2 = None
     if residual is not None:
-        if (residual.dtype != torch.bfloat16 or residual.device != x.device or residual.shape != (*lead, N)
+        if (residual.dtype != x.dtype or residual.device != x.device or residual.shape != (*lead, N)
                 or residual.stride(-1) != 1):
-            raise ValueError("int8_linear: residual must be bf16 [..., N] on x's device with a contiguous last dim")
+            raise ValueError("int8_linear: residual must be [..., N] of x's dtype and device with a contiguous last dim")
         r2 = residual.view(-1, N) if M > 0 else None
     if M == 0:
         return y
@@ -115,18 +143,20 @@ def _launch(x: torch.Tensor, w_ptr: int, scale: torch.Tensor, N: int, K: int, ou
     ws = linear_workspace(M, K, N, x.device, algo, packed)
     ws_ptr, ws_bytes = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     lib = _lib.load()
-    if r2 is not None:
-        if r2.data_ptr() == y2.data_ptr() and r2.stride(0) != y2.stride(0):
-            raise ValueError("int8_linear: residual and out overlap with different strides")
-        rc = lib.lse_int8_linear_packed_residual(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N,
-                                                 r2.data_ptr(), r2.stride(0), y2.data_ptr(), y2.stride(0),
-                                                 ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
-        _lib.check(rc, "lse_int8_linear_packed_residual")
+    if r2 is not None and r2.data_ptr() == y2.data_ptr() and r2.stride(0) != y2.stride(0):
+        raise ValueError("int8_linear: residual and out overlap with different strides")
+    if packed:
+        rc = lib.lse_int8_linear_packed_dt(x2.data_ptr(), _DTYPE_CODES[x.dtype], M, K, x2.stride(0), w_ptr,
+                                           scale.data_ptr(), N, r2.data_ptr() if r2 is not None else None,
+                                           r2.stride(0) if r2 is not None else 0, y2.data_ptr(), y2.stride(0),
+                                           ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
+        _lib.check(rc, "lse_int8_linear_packed_dt")
         return y
-    fn = lib.lse_int8_linear_packed if packed else lib.lse_int8_linear_ex
-    rc = fn(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N, y2.data_ptr(), y2.stride(0),
-            ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
-    _lib.check(rc, "lse_int8_linear_packed" if packed else "lse_int8_linear")
+    if r2 is not None:
+        raise ValueError("int8_linear: the residual add needs the packed weight layout")
+    rc = lib.lse_int8_linear_ex(x2.data_ptr(), M, K, x2.stride(0), w_ptr, scale.data_ptr(), N, y2.data_ptr(),
+                                y2.stride(0), ws_ptr, ws_bytes, int(algo), stream.cuda_stream)
+    _lib.check(rc, "lse_int8_linear")
     return y
 
 
@@ -220,24 +250,19 @@ def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: tor
         x2 = x2.contiguous()
     M = x2.shape[0]
     if out is None:
-        out = torch.empty((*lead, I), dtype=torch.bfloat16, device=x.device)
-    elif out.dtype != torch.bfloat16 or out.shape != (*lead, I) or not out.is_contiguous():
-        raise ValueError("int8_gate_up_silu_packed: out must be contiguous bf16 [..., intermediate]")
+        out = torch.empty((*lead, I), dtype=x.dtype, device=x.device)
+    elif out.dtype != x.dtype or out.shape != (*lead, I) or not out.is_contiguous():
+        raise ValueError("int8_gate_up_silu_packed: out must be contiguous [..., intermediate] of x's dtype")
     if M == 0:
         return out
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
-    lib = _lib.load()
-    if M <= GATE_UP_SILU_MAX_M:
-        rc = lib.lse_int8_gate_up_silu_packed(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
-                                              scale.data_ptr(), I, out.data_ptr(), I, stream.cuda_stream)
-        _lib.check(rc, "lse_int8_gate_up_silu_packed")
-        return out
-    ws = linear_workspace(M, K, 2 * I, x.device)
-    rc = lib.lse_int8_gate_up_silu_packed_ws(x2.data_ptr(), M, K, x2.stride(0), w_packed.data_ptr(),
-                                             scale.data_ptr(), I, out.data_ptr(), I, ws.data_ptr(), ws.numel(),
-                                             stream.cuda_stream)
-    _lib.check(rc, "lse_int8_gate_up_silu_packed_ws")
+    ws = linear_workspace(M, K, 2 * I, x.device) if M > GATE_UP_SILU_MAX_M else None
+    ws_ptr, ws_bytes = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    rc = _lib.load().lse_int8_gate_up_silu_packed_dt(x2.data_ptr(), _DTYPE_CODES[x.dtype], M, K, x2.stride(0),
+                                                     w_packed.data_ptr(), scale.data_ptr(), I, out.data_ptr(), I,
+                                                     ws_ptr, ws_bytes, stream.cuda_stream)
+    _lib.check(rc, "lse_int8_gate_up_silu_packed_dt")
     return out
 
 
@@ -345,7 +370,7 @@ _attn_ws_retired: list[torch.Tensor] = []  # outgrown buffers stay alive: captur
 
 def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
                            context_len: torch.Tensor, max_context: int, scale: float | None = None,
-                           out: torch.Tensor | None = None) -> torch.Tensor:
+                           out: torch.Tensor | None = None, split: bool = True) -> torch.Tensor:
     """Decode attention over the paged K/V pool: one query token per sequence.
 
     q: bf16 [E, H, D] (d contiguous); k_pool / v_pool: bf16 [num_blocks, block_size, H_KV, D]
@@ -354,6 +379,8 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     entry <= max_context (a launch-shape bound, fixed per captured graph).  Returns bf16
     [E, H, D] = softmax(q K^T * scale) V over each sequence's positions, scale = 1/sqrt(D) by
     default (`paged_attention_forward`, `kernels/flash_attention.py:287-332`, with q_len 1).
+    split=False runs one CTA per (sequence, KV head) with no workspace (nothing to size or keep
+    per stream; max_context <= 1023 * block_size).
     """
     if not all(t.is_cuda for t in (q, k_pool, v_pool, block_table, context_len)):
         raise RuntimeError("paged_decode_attention runs on CUDA only (no CPU fallback)")
@@ -379,7 +406,7 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     _ensure_device(q.device)
     lib = _lib.load()
     stream = torch.cuda.current_stream(q.device)
-    need = int(lib.lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, bs))
+    need = int(lib.lse_paged_decode_attention_workspace(E, H, H_kv, D, max_context, bs)) if split else 0
     key = (q.device.index, stream.cuda_stream)
     ws = _attn_ws.get(key)
     if need and (ws is None or ws.numel() < need):

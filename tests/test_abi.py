@@ -185,3 +185,21 @@ def test_python_ops_refuse_cpu_tensors():
     with pytest.raises((RuntimeError, ValueError)):
         ops.rope_kv_write(torch.zeros(2, 12 * 64, dtype=torch.bfloat16), 8, 2, 64, torch.zeros(2, 64),
                           torch.zeros(2, 64), pool, pool, torch.zeros(2, dtype=torch.int64))
+
+
+def test_torch_operators_register_without_a_gpu():
+    """liblse_torch.so loads on a machine without a GPU and registers the two operators with
+    the documented schemas; they have no CPU kernel (a CPU call is refused, nothing falls back)."""
+    import torch
+
+    from llm_serving_engine_b200 import ops
+
+    lse = ops.torch_ops()
+    assert str(lse.int8_linear.default._schema) == (
+        "lse::int8_linear(Tensor x, Tensor w_packed, Tensor scale, int N, int K, Tensor? residual=None, "
+        "int algo=0) -> Tensor")
+    assert str(lse.gate_up_silu.default._schema) == (
+        "lse::gate_up_silu(Tensor x, Tensor w_packed, Tensor scale, int I, int K) -> Tensor")
+    with pytest.raises((NotImplementedError, RuntimeError)):
+        lse.int8_linear(torch.zeros(2, 16, dtype=torch.bfloat16), torch.zeros(2048, dtype=torch.int8),
+                        torch.ones(16), 16, 16)

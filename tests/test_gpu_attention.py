@@ -175,3 +175,16 @@ def test_one_workspace_serves_changing_shapes():
             torch.cuda.synchronize()
             check_parity(o.reshape(-1, o.shape[-1]), ref.reshape(-1, ref.shape[-1]), "interleaved shapes")
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("E,ctx", [(1, [1025]), (4, [1, 17, 300, 1024])])
+def test_unsplit_launch_without_workspace(E, ctx):
+    """split=False (no workspace: what the engine binding uses inside its graphs) gives the
+    oracle's result too, for batches the planner would otherwise split."""
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(E, 32, 8, 128, 16, ctx, seed=5 + E)
+    o = ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda(), cl.cuda(), max_ctx, split=False)
+    torch.cuda.synchronize()
+    ref = ref_paged_decode_attention(q.float().numpy(), k_pool.float().numpy(), v_pool.float().numpy(),
+                                     bt.numpy(), cl.numpy())
+    check_parity(o.reshape(E * 32, 128), ref.reshape(E * 32, 128), f"unsplit attention E={E}")
+    assert ops.device_status() == 0

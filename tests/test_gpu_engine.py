@@ -55,16 +55,17 @@ def _hook():
     engine_hook.uninstall()
 
 
-def _int8_runner(tiny_dir):
-    runner = load_runner(tiny_dir, quantize="int8")
+def _int8_runner(tiny_dir, dtype="bfloat16"):
+    runner = load_runner(tiny_dir, quantize="int8", dtype=dtype)
     runner.allocate_kv_pool(NUM_BLOCKS, BLOCK_SIZE)
     return runner
 
 
-def _twin_runner(tiny_dir, int8_runner):
+def _twin_runner(tiny_dir, int8_runner, dtype="bfloat16"):
     """The same checkpoint with every projection replaced by the int8 runner's dequantized
-    weights (bf16), run by the reference's own bf16 path (cuBLAS nn.Linear)."""
-    twin = load_runner(tiny_dir, quantize="none")
+    weights (in the model dtype), run by the reference's own path (cuBLAS nn.Linear, Triton
+    attention)."""
+    twin = load_runner(tiny_dir, quantize="none", dtype=dtype)
     with torch.no_grad():
         for lt, li in zip(twin._layers, int8_runner._layers, strict=True):
             qkv = li.self_attn.qkv_int8
@@ -96,15 +97,17 @@ def test_quantize_int8_config_loads_an_int8_model(tiny_dir):
     runner.check_custom_kernel_support()
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 @pytest.mark.parametrize("prompt_lens", [(5,), (3, 17, 40)])
-def test_forward_fused_matches_dequantized_twin(tiny_dir, prompt_lens):
-    """Prefill then two decode steps through the reference's eager forward_fused: the int8 runner
-    and its dequantized bf16 twin give logits within normwise 2e-2 of the largest logit (bf16
+def test_forward_fused_matches_dequantized_twin(tiny_dir, prompt_lens, dtype):
+    """Prefill then two decode steps through the reference's eager forward_fused, in bf16 and in
+    fp16 (the reference's default dtype, run natively by the int8 operators): the int8 runner
+    and its dequantized twin give logits within normwise 2e-2 of the largest logit (16-bit
     activations through two layers) and the same greedy token wherever the twin's margin
     between its two best tokens exceeds four times the largest logit difference.  Both runners
     then continue with the twin's tokens, so one near-tie cannot make the sequences diverge."""
-    runner = _int8_runner(tiny_dir)
-    twin = _twin_runner(tiny_dir, runner)
+    runner = _int8_runner(tiny_dir, dtype)
+    twin = _twin_runner(tiny_dir, runner, dtype)
     alloc_a, alloc_b = BlockAllocator(NUM_BLOCKS, BLOCK_SIZE), BlockAllocator(NUM_BLOCKS, BLOCK_SIZE)
     prompts = [[(7 * i + 3 * j) % 120 + 1 for j in range(n)] for i, n in enumerate(prompt_lens)]
     seqs_a = [greedy_sequence(100 + i, p) for i, p in enumerate(prompts)]
@@ -132,8 +135,9 @@ def test_forward_fused_matches_dequantized_twin(tiny_dir, prompt_lens):
     assert decisive >= 2 * len(prompt_lens), f"only {decisive} decisive rows"
 
 
-def test_decode_graphs_capture_self_check_and_replay_equal_eager(tiny_dir, monkeypatch):
-    runner = _int8_runner(tiny_dir)
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_decode_graphs_capture_self_check_and_replay_equal_eager(tiny_dir, monkeypatch, dtype):
+    runner = _int8_runner(tiny_dir, dtype)
     buckets = decode_graph_buckets(8)
     runner.capture_decode_graphs(buckets)
     assert set(runner._decode_graphs.graphs) == set(buckets), "capture or self-check failed"
