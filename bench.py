@@ -242,9 +242,9 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
     """Config 5: Llama-3-70B projection shapes with the output rows (N) split over the
     `world` ranks.  Per point (max over ranks): the rank's kernel time on its N/world rows
     (CUDA graph over rotated weight copies, so the weights come from HBM), the NCCL
-    all-gather of the output shards, and the end to end time of kernel + gather + column
-    reorder (llm_serving_engine_b200.parallel.gather_columns), each in a CUDA graph, CUDA
-    events."""
+    all-gather of the output shards into the shard-major [world, M, N/world] the collective
+    produces (llm_serving_engine_b200.parallel.gather_columns, no reorder copy), and the end to
+    end time of kernel + gather, each in a CUDA graph, CUDA events."""
     from llm_serving_engine_b200.parallel import gather_columns
 
     g = torch.Generator(device=dev).manual_seed(77 + rank)
@@ -285,7 +285,7 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
                 # graphed decode step runs them); every rank captures the same sequence
                 def gather10(y=y):
                     for _ in range(10):
-                        gather_columns(y)
+                        gather_columns(y, layout="shard_major")
                 g2 = capture(gather10, warm)
                 time_graph(g2, 1)
                 t_g = time_graph(g2, 3) / 10
@@ -294,7 +294,7 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
             def e2e10(x=x, y=y):
                 for i in range(10):
                     ops.int8_linear_packed(x, ws[i % copies], s, n, K, out=y)
-                    gather_columns(y)
+                    gather_columns(y, layout="shard_major")
             g3 = capture(e2e10, warm)
             time_graph(g3, 1)
             t_e = time_graph(g3, 3) / 10
@@ -323,8 +323,84 @@ def tp70b_sweep(world: int, rank: int, dev, ops, warm):
         raise RuntimeError(f"config5 column split: gathered output differs from the one-GPU output: {pts}")
     return {"workload": f"config5: Llama-3-70B (K,N) qkv 8192x10240, o 8192x8192, gate_up 8192x57344, "
                         f"down 28672x8192; N split over {world} GPU(s); M in {list(TP_M)}",
-            "collective": "NCCL all_gather_into_tensor of the output shards + column reorder" if world > 1 else "none",
+            "collective": "NCCL all_gather_into_tensor of the output shards (shard-major, no reorder)" if world > 1 else "none",
             "parity": "gathered output == one-GPU output within normwise 1e-2 on sampled rows, every point, every rank",
+            "points": pts}
+
+
+MLP_M = (1, 32, 256, 4096)
+
+
+def mlp70b_tp(world: int, rank: int, dev, ops, warm):
+    """Config 5 strong scaling on the Llama-3-70B MLP block (H 8192, I 28672): gate_up split by
+    output rows with SiLU * mul fused on each rank, down split by input columns, one NCCL
+    all-reduce of the [M, H] output (llm_serving_engine_b200.parallel.TensorParallelInt8MLP).
+    End to end per M (max over ranks), CUDA graph over rotated weight copies (each rank's
+    weights stream from HBM), CUDA events.  Rank 0 also times the unsplit block on one GPU in
+    the same run (the other ranks wait), so every run states its own speed-up over one GPU; the
+    split output is checked against the unsplit one (normwise 1e-2)."""
+    from llm_serving_engine_b200.int8_linear import Int8LlamaMLP
+    from llm_serving_engine_b200.parallel import TensorParallelInt8MLP
+
+    H, I = 8192, 28672
+    gf = torch.Generator(device=dev).manual_seed(4242)  # identical full weights on every rank
+    q = {k: torch.randint(-127, 128, shape, generator=gf, device=dev, dtype=torch.int8)
+         for k, shape in (("g", (I, H)), ("u", (I, H)), ("d", (H, I)))}
+    sc = {k: torch.empty(q[k].shape[0], device=dev).uniform_(1e-4, 5e-4, generator=gf) for k in q}
+    per_rank_bytes = 3 * I * H // world
+    copies = max(1, min(6, -(-3 * 126 * 2**20 // per_rank_bytes)))
+    mlps = [TensorParallelInt8MLP.from_quantized(q["g"], sc["g"], q["u"], sc["u"], q["d"], sc["d"])]
+    gr = torch.Generator(device=dev).manual_seed(99 + rank)
+    for _ in range(copies - 1):  # further weights of the same shapes: only rotate the reads past L2
+        r = {k: torch.randint(-127, 128, q[k].shape, generator=gr, device=dev, dtype=torch.int8) for k in q}
+        mlps.append(TensorParallelInt8MLP.from_quantized(r["g"], sc["g"], r["u"], sc["u"], r["d"], sc["d"]))
+        del r
+    single = Int8LlamaMLP.from_quantized(torch.cat([q["g"], q["u"]]), torch.cat([sc["g"], sc["u"]]), q["d"], sc["d"], I) \
+        if rank == 0 else None
+    del q
+    torch.cuda.empty_cache()
+    pts = []
+    ok_all = True
+    for M in MLP_M:
+        x = torch.randn(M, H, generator=gf, device=dev).to(torch.bfloat16)  # same x on every rank
+
+        def run(x=x):
+            for m in mlps:
+                m(x)
+        g = capture(run, warm)
+        time_graph(g, 2)
+        t = time_graph(g, 5) / len(mlps)
+        del g
+        t = max_over_ranks(t, world)
+        y = mlps[0](x)
+        t1, err = None, 0.0
+        if rank == 0:
+            def run1(x=x):
+                for _ in range(3):
+                    single(x)
+            g1 = capture(run1, warm)
+            time_graph(g1, 1)
+            t1 = time_graph(g1, 3) / 3
+            del g1
+            ref = single(x).float()
+            err = ((y.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item()
+        barrier(world)
+        ok = max_over_ranks(0.0 if err <= 1e-2 else 1.0, world) == 0.0
+        ok_all = ok_all and ok
+        pt = {"M": M, "e2e_us": round(t * 1e3, 2), "TFLOPs": round(6.0 * M * H * I / t / 1e9, 1),
+              "weight_GBps_per_gpu": round(per_rank_bytes / t / 1e6, 1), "parity_vs_one_gpu_ok": ok}
+        if t1 is not None:
+            pt["one_gpu_us"] = round(t1 * 1e3, 2)
+            pt["speedup_vs_one_gpu"] = round(t1 / t, 3)
+        pts.append(pt)
+        del x, y
+    del mlps, single
+    torch.cuda.empty_cache()
+    if not ok_all:
+        raise RuntimeError(f"config5 MLP split: output differs from the one-GPU block: {pts}")
+    return {"workload": f"config5: Llama-3-70B MLP block (H {H}, I {I}), gate_up rows and down columns split over "
+                        f"{world} GPU(s), one NCCL all-reduce of the output; M in {list(MLP_M)}",
+            "n_gpus": world, "collective": "NCCL all_reduce (sum) of the bf16 [M, H] output" if world > 1 else "none",
             "points": pts}
 
 
@@ -816,6 +892,7 @@ def main():
     host = host_overhead(dev, ops)
     cublas = bf16_cublas_points(layers, dev, warm, xs)
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
+    mlp70b = None if args.no_70b else mlp70b_tp(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
 
     # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
@@ -876,6 +953,8 @@ def main():
                                                for p, c in zip(points, cublas)}
         if tp70b:
             line["config5_70b_column_split"] = tp70b
+        if mlp70b:
+            line["config5_mlp_strong_scaling"] = mlp70b
         if decode4:
             line["config4_e2e_decode"] = decode4
         if cpu_base:

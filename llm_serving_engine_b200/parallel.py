@@ -1,25 +1,30 @@
-"""Output-column (N) split of the int8 linear over the ranks of a process group.
+"""Splits of the int8 linear over the ranks of a process group.
 
-`y[:, n]` depends only on `W[n, :]`, `s[n]` and all of `x`, so the projections shard by
-output rows with no reduction across ranks: rank r of g holds rows [r*N/g, (r+1)*N/g) of the
-int8 weight and their scales, `x` is replicated (every rank already holds its own copy of
-the activation), and the only collective is an all-gather of the output shards, issued
-only where the consumer needs the full output (`gather_output`).  On B200 the gather is
-NCCL over NVLink 5; the shards' shapes keep each rank's kernel on the same configuration as
-a single-GPU call of N/g rows.
+`y[:, n]` depends only on `W[n, :]`, `s[n]` and all of `x`, so a projection shards by output
+rows with no reduction across ranks: rank r of g holds rows [r*N/g, (r+1)*N/g) of the int8
+weight and their scales, `x` is replicated (every rank already holds its own copy of the
+activation), and the only collective is an all-gather of the output shards, issued only where
+the consumer needs the full output.  On B200 the collectives are NCCL over NVLink 5; the
+shards' shapes keep each rank's kernel on the same configuration as a single-GPU call of N/g
+rows.
 
-* `ColumnParallelInt8Linear`: one projection, shard-local kernel, optional all-gather.
-* `TensorParallelInt8MLP`: `down(silu(gate(x)) * up(x))` with both projections N-split.
-  Rank r holds the gate rows and the up rows of intermediate block r, so SiLU * mul stays
-  local; the intermediate block is all-gathered once (down needs all of its K) and down's
-  output block is gathered at the end.  With the default (GPU) local linear and SiLU, the
-  rank's gate and up rows are stored interleaved in 8-row blocks and gate_up + SiLU * mul is
-  one fused launch (`ops.int8_gate_up_silu_packed`); otherwise the rank's gate block
-  precedes its up block and SiLU * mul runs after the projection.
+* `ColumnParallelInt8Linear`: one projection split by output rows, shard-local kernel, and
+  optionally the all-gather: `gather_output="shard_major"` returns the gathered shards as
+  `[g, ..., N/g]` exactly as the collective leaves them (no copy); `True` reorders them into
+  `[..., N]` (one more pass over the output).
+* `RowParallelInt8Linear`: one projection split by input columns (K): rank r holds
+  `W[:, K-block r]` and reads its block of x; the partial outputs (each with the full s[n])
+  are summed by one all-reduce.
+* `TensorParallelInt8MLP`: `down(silu(gate(x)) * up(x))` with gate_up split by output rows and
+  down by input columns over the same intermediate blocks, so SiLU * mul stays local, the
+  intermediate is never gathered, and the block's only collective is the all-reduce of its
+  [..., H] output.  With the default (GPU) local linear and SiLU, the rank's gate and up rows
+  are stored interleaved in 8-row blocks and gate_up + SiLU * mul is one fused launch;
+  otherwise the rank's gate block precedes its up block and SiLU * mul runs after it.
 
 The per-rank compute is `local_factory(q_rows, s_rows)`: by default an `Int8Linear` on this
 rank's GPU (the sm_100a kernels; there is no CPU path).  Tests substitute a factory to run
-the sharding and gather logic on CPU ranks.
+the sharding and collective logic on CPU ranks.
 """
 
 from __future__ import annotations
@@ -37,8 +42,8 @@ from .int8_linear import Int8Linear
 LocalLinear = Callable[[torch.Tensor], torch.Tensor]
 LocalFactory = Callable[[torch.Tensor, torch.Tensor], LocalLinear]
 
-__all__ = ["ColumnParallelInt8Linear", "TensorParallelInt8MLP", "shard_rows", "interleaved_rows", "fused_rows",
-           "gather_columns"]
+__all__ = ["ColumnParallelInt8Linear", "RowParallelInt8Linear", "TensorParallelInt8MLP", "shard_rows",
+           "interleaved_rows", "fused_rows", "gather_columns", "all_reduce_sum"]
 
 
 def _default_local(q: torch.Tensor, s: torch.Tensor) -> LocalLinear:
@@ -83,12 +88,17 @@ def _is_silu(act) -> bool:
     return act is F.silu or type(act).__name__ in ("SiLU", "SiLUActivation")
 
 
-def gather_columns(y: torch.Tensor, group=None) -> torch.Tensor:
-    """All-gather the ranks' column shards `y [..., n]` into `[..., world * n]` (rank order)."""
+def gather_columns(y: torch.Tensor, group=None, layout: str = "row_major") -> torch.Tensor:
+    """All-gather the ranks' column shards `y [..., n]` (rank order).  layout "shard_major":
+    `[world, ..., n]`, the collective's own output, no copy; "row_major": `[..., world * n]`,
+    the shards reordered into full rows (a copy of the output, except when the leading dims
+    hold one row)."""
     world, _ = _world(group)
-    if world == 1:
-        return y
+    if layout not in ("row_major", "shard_major"):
+        raise ValueError(f"gather_columns: layout must be 'row_major' or 'shard_major', got {layout!r}")
     lead, n = y.shape[:-1], y.shape[-1]
+    if world == 1:
+        return y.unsqueeze(0) if layout == "shard_major" else y
     flat = y.reshape(-1, n).contiguous()
     rows = flat.shape[0]
     if dist.get_backend(group) == "nccl":
@@ -99,7 +109,18 @@ def gather_columns(y: torch.Tensor, group=None) -> torch.Tensor:
         chunks = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(chunks, flat, group=group)
         parts = torch.stack(chunks)
+    if layout == "shard_major":
+        return parts.view(world, *lead, n)
     return parts.permute(1, 0, 2).reshape(*lead, world * n)
+
+
+def all_reduce_sum(y: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum `y` over the ranks of `group`, in place (NCCL on GPUs: on NVSwitch systems it may
+    reduce inside the switch)."""
+    world, _ = _world(group)
+    if world > 1:
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
 
 
 class ColumnParallelInt8Linear(nn.Module):
@@ -130,7 +151,9 @@ class ColumnParallelInt8Linear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         y = self.local(x)
-        return gather_columns(y, self.group) if self.gather_output else y
+        if not self.gather_output:
+            return y
+        return gather_columns(y, self.group, "shard_major" if self.gather_output == "shard_major" else "row_major")
 
     def extra_repr(self) -> str:
         world, rank = _world(self.group)
@@ -138,10 +161,46 @@ class ColumnParallelInt8Linear(nn.Module):
                 f"gather_output={self.gather_output}")
 
 
-class TensorParallelInt8MLP(nn.Module):
-    """`down(act(gate(x)) * up(x))` with gate_up and down split over output rows."""
+class RowParallelInt8Linear(nn.Module):
+    """The int8 linear with its input columns (K) split over the ranks of `group`: rank r holds
+    `W[:, K-block r]` with the full scales and takes x's block r; the partial outputs are summed
+    across the ranks (one all-reduce), or left to the caller with `reduce_output=False`."""
 
-    def __init__(self, gate_up: ColumnParallelInt8Linear, down: ColumnParallelInt8Linear, intermediate: int,
+    def __init__(self, local: LocalLinear, in_features: int, out_features: int, group=None,
+                 reduce_output: bool = True):
+        super().__init__()
+        self.local = local
+        self.in_features = in_features  # full K across the group
+        self.out_features = out_features
+        self.group = group
+        self.reduce_output = reduce_output
+
+    @classmethod
+    def from_quantized(cls, q: torch.Tensor, s: torch.Tensor, group=None, reduce_output: bool = True,
+                       local_factory: LocalFactory = _default_local) -> "RowParallelInt8Linear":
+        """Shard the full int8 weight `q [N, K]` (identical on every rank) by columns: keep this
+        rank's contiguous K block and every scale."""
+        world, rank = _world(group)
+        N, K = q.shape
+        cols = shard_rows(K, world, rank).to(q.device)
+        local = local_factory(q.index_select(1, cols).contiguous(), s.contiguous())
+        return cls(local, K, N, group, reduce_output)
+
+    def forward(self, x_block: torch.Tensor) -> torch.Tensor:
+        y = self.local(x_block)
+        return all_reduce_sum(y, self.group) if self.reduce_output else y
+
+    def extra_repr(self) -> str:
+        world, rank = _world(self.group)
+        return (f"in_features={self.in_features}, out_features={self.out_features}, rank {rank} of {world}, "
+                f"reduce_output={self.reduce_output}")
+
+
+class TensorParallelInt8MLP(nn.Module):
+    """`down(act(gate(x)) * up(x))` with gate_up split by output rows and down by input
+    columns over the same intermediate blocks: one all-reduce of the output, nothing gathered."""
+
+    def __init__(self, gate_up: ColumnParallelInt8Linear, down: RowParallelInt8Linear, intermediate: int,
                  group=None, act=F.silu, fused: bool = False):
         super().__init__()
         self.gate_up = gate_up
@@ -168,20 +227,17 @@ class TensorParallelInt8MLP(nn.Module):
         rows = fused_rows(intermediate, world, rank) if fused else interleaved_rows(intermediate, world, rank)
         gate_up = ColumnParallelInt8Linear.from_quantized(q_gu, s_gu, group, gather_output=False, rows=rows,
                                                           local_factory=local_factory)
-        down = ColumnParallelInt8Linear.from_quantized(q_down, s_down, group, gather_output=True,
-                                                       local_factory=local_factory)
+        down = RowParallelInt8Linear.from_quantized(q_down, s_down, group, local_factory=local_factory)
         return cls(gate_up, down, intermediate, group, act, fused=fused)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         world, _ = _world(self.group)
+        i_local = self.intermediate_size // world
         if self.fused:
             lin = self.gate_up.local
-            h_local = ops.int8_gate_up_silu_packed(x.to(torch.bfloat16), lin.weight_packed, lin.scale,
-                                                   self.intermediate_size // world, lin.in_features)
+            h_local = ops.torch_ops().gate_up_silu(x, lin.weight_packed, lin.scale, i_local, lin.in_features)
         else:
             gu = self.gate_up(x)  # [..., 2 * I / world]: this rank's gate block, then its up block
-            gate, up = gu.split(self.intermediate_size // world, dim=-1)
+            gate, up = gu.split(i_local, dim=-1)
             h_local = self.act(gate) * up
-        h = gather_columns(h_local, self.group)  # [..., I]
-        y = self.down_proj(h)
-        return y.to(x.dtype) if self.fused and y.dtype != x.dtype else y
+        return self.down_proj(h_local)  # this rank's intermediate block -> partial sums -> all-reduce

@@ -1,9 +1,12 @@
-"""Output-column split over NCCL ranks on real GPUs (one process per GPU, 2 GPUs).
+"""The splits over NCCL ranks on real GPUs (one process per GPU, 2 GPUs).
 
 Each rank runs the sm_100a kernel on its row block and the shards are all-gathered over
-NVLink; the result is compared with the unsplit single-GPU projection (same kernel family,
-different shape, so within the parity tolerance rather than bit for bit) and with the
-oracle.  Skipped when fewer than two GPUs are visible (a one-GPU run of the suite).
+NVLink (row-major, and shard-major as the collective leaves them); the result is compared
+with the unsplit single-GPU projection (same kernel family, different shape, so within the
+parity tolerance rather than bit for bit) and with the oracle.  The tensor-parallel MLP
+(gate_up split by rows, down by input columns, one all-reduce) is compared with the unsplit
+MLP arithmetic on one GPU.  Skipped when fewer than two GPUs are visible (a one-GPU run of
+the suite).
 """
 
 from __future__ import annotations
@@ -51,6 +54,9 @@ def _case(rank: int, world: int) -> None:
         single = Int8Linear.from_quantized(w.to(dev), s.to(dev))(xd)
         nw2, ok2, _ = parity_errors(y.float().cpu().numpy(), single.float().cpu().numpy().astype(np.float64))
         assert nw2 <= 1e-2 and ok2, (M, K, N, nw2)
+        sm = ColumnParallelInt8Linear.from_quantized(w.to(dev), s.to(dev), gather_output="shard_major")(xd)
+        assert sm.shape == (world, M, N // world)
+        assert torch.equal(sm.permute(1, 0, 2).reshape(M, N), y)
     # tensor-parallel MLP vs the unsplit MLP arithmetic on one GPU
     H, I, M = 1024, 4096, 8
     g = torch.Generator().manual_seed(9)

@@ -1,10 +1,12 @@
-"""Output-column split over ranks (llm_serving_engine_b200.parallel) on CPU gloo ranks.
+"""Splits over ranks (llm_serving_engine_b200.parallel) on CPU gloo ranks.
 
 The per-rank kernel is replaced by the oracle (a `local_factory` returning bf16-rounded fp64
-results), so these tests check what the split itself must get right - which rows each rank
-holds, the gate/up interleave, the all-gather and its column order, leading dimensions - at
-world sizes 2 and 4, bit for bit against the unsplit computation.  The GPU run of the same
-module over NCCL is tests/test_gpu_multi.py.
+results), so these tests check what the splits themselves must get right - which rows and
+columns each rank holds, the gate/up interleave, the all-gather and its column order (row-major
+and shard-major), the all-reduce of the K split, leading dimensions - at world sizes 2 and 4:
+the output-row split bit for bit against the unsplit computation; the K split (partials
+rounded to bf16 and summed) within the parity tolerance of the fp64 computation, identical on
+every rank.  The GPU run of the same modules over NCCL is tests/test_gpu_multi.py.
 """
 
 from __future__ import annotations
@@ -18,8 +20,9 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 import torch.nn.functional as F
 
-from llm_serving_engine_b200.parallel import (ColumnParallelInt8Linear, TensorParallelInt8MLP, fused_rows,
-                                              gather_columns, interleaved_rows, shard_rows)
+from llm_serving_engine_b200.parallel import (ColumnParallelInt8Linear, RowParallelInt8Linear,
+                                              TensorParallelInt8MLP, fused_rows, gather_columns, interleaved_rows,
+                                              shard_rows)
 from oracle.ref_linear import ref_int8_linear, ref_quantize
 
 
@@ -59,6 +62,35 @@ def _column_case(rank: int, world: int) -> None:
     # any leading shape
     x3 = _x(3, 2, 3, K)
     assert torch.equal(mod(x3), oracle_local(q, s)(x3))
+    # shard-major: the collective's [world, ..., n] as it is
+    sm = ColumnParallelInt8Linear.from_quantized(q, s, gather_output="shard_major", local_factory=oracle_local)(x3)
+    full3 = oracle_local(q, s)(x3)
+    assert sm.shape == (world, 2, 3, n)
+    for r in range(world):
+        assert torch.equal(sm[r], full3[..., r * n:(r + 1) * n])
+
+
+def _rel_err(y: torch.Tensor, ref: np.ndarray) -> float:
+    return float(np.abs(y.double().numpy() - ref).max() / np.abs(ref).max())
+
+
+def _same_on_every_rank(y: torch.Tensor, world: int) -> None:
+    ys = [torch.empty_like(y) for _ in range(world)]
+    dist.all_gather(ys, y.contiguous())
+    assert all(torch.equal(t, ys[0]) for t in ys)
+
+
+def _row_case(rank: int, world: int) -> None:
+    M, K, N = 4, 128, 40
+    q, s = _weights(11, N, K)
+    x = _x(12, 1, M, K)
+    k = K // world
+    mod = RowParallelInt8Linear.from_quantized(q, s, local_factory=oracle_local)
+    y = mod(x[..., rank * k:(rank + 1) * k])
+    assert y.shape == (1, M, N)
+    ref = ref_int8_linear(x.reshape(M, K).float().numpy().astype(np.float64), q.numpy(), s.numpy())
+    assert _rel_err(y.reshape(M, N), ref) <= 1e-2
+    _same_on_every_rank(y, world)
 
 
 def _mlp_case(rank: int, world: int) -> None:
@@ -67,13 +99,18 @@ def _mlp_case(rank: int, world: int) -> None:
     qu, su = _weights(5, I, H)
     qd, sd = _weights(6, H, I)
     x = _x(7, M, H)
-    # the unsplit path with the same roundings: fused gate_up, SiLU * mul in bf16, down
-    gu = oracle_local(torch.cat([qg, qu]), torch.cat([sg, su]))(x)
-    h = F.silu(gu[:, :I]) * gu[:, I:]
-    ref = oracle_local(qd, sd)(h)
+    # the unsplit computation in fp64
+    x64 = x.float().numpy().astype(np.float64)
+    g = ref_int8_linear(x64, qg.numpy(), sg.numpy())
+    u = ref_int8_linear(x64, qu.numpy(), su.numpy())
+    ref = ref_int8_linear(g / (1.0 + np.exp(-g)) * u, qd.numpy(), sd.numpy())
     mlp = TensorParallelInt8MLP.from_quantized(qg, sg, qu, su, qd, sd, local_factory=oracle_local)
     assert not mlp.fused  # a substituted local linear keeps gate block | up block and SiLU * mul after it
-    assert torch.equal(mlp(x), ref)
+    assert isinstance(mlp.down_proj, RowParallelInt8Linear)
+    y = mlp(x)
+    assert y.shape == (M, H)
+    assert _rel_err(y, ref) <= 2e-2
+    _same_on_every_rank(y, world)
 
 
 def _gather_order_case(rank: int, world: int) -> None:
@@ -114,6 +151,11 @@ def test_tensor_parallel_mlp_matches_unsplit(world):
 
 def test_gather_puts_rank_blocks_in_order():
     _run(_gather_order_case, 2)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_split_matches_unsplit(world):
+    _run(_row_case, world)
 
 
 def test_row_assignment():
