@@ -3,6 +3,8 @@ captures in profiles/ are taken on.
 
     python profile_case.py --M 16 --shape gate_up --algo tcgen05 --launches 4
     python profile_case.py --M 64 --gate-up-silu --launches 6
+    python profile_case.py --decode-step 64 --launches 2      (a whole Llama-3-8B decode step)
+    python profile_case.py --prefill-attention 1 --launches 4  (multi-token paged attention)
 
 Weights (in the packed layout the module stores) are rotated over enough distinct copies that each launch reads its weight from
 HBM, not from L2 (126 MB); the device footprint stays at a few GB.  Prints the CUDA-event
@@ -36,9 +38,20 @@ def main(argv=None):
     ap.add_argument("--attention", type=int, default=0, metavar="E",
                     help="profile the paged decode attention instead: E sequences of 1025 positions, "
                          "Llama-3-8B attention shape, three layers' pools in rotation")
+    ap.add_argument("--decode-step", type=int, default=0, metavar="B",
+                    help="time `--launches` CUDA-graph replays of one int8 decode step of a random-init "
+                         "Llama-3-8B at B sequences x 1024 cached positions (llama_decode.DecodeModel), "
+                         "inside an NVTX range 'step'")
+    ap.add_argument("--prefill-attention", type=int, default=0, metavar="E",
+                    help="profile the multi-token paged attention instead: E entries with a 2048 / E token "
+                         "chunk each, Llama-3-8B attention shape")
     args = ap.parse_args(argv)
     if args.attention:
         return attention_case(args.attention, args.launches)
+    if args.decode_step:
+        return decode_step_case(args.decode_step, args.launches)
+    if args.prefill_attention:
+        return prefill_attention_case(args.prefill_attention, args.launches)
     if args.gate_up_silu:
         args.shape = "gate_up"
     K, N = (LLAMA3_8B_SHAPES if args.model == "8b" else LLAMA3_70B_SHAPES)[args.shape]
@@ -116,6 +129,61 @@ def attention_case(E: int, launches: int) -> None:
     ms = a.elapsed_time(b) / launches
     byts = E * ctx * H_kv * D * 2 * 2
     print(f"paged decode attention E={E} ctx={ctx}: {ms * 1e3:.2f} us/launch ({byts / ms / 1e6:.0f} GB/s of K/V)")
+    assert ops.device_status() == 0
+
+
+def decode_step_case(B: int, launches: int) -> None:
+    from llm_serving_engine_b200.llama_decode import LLAMA3_8B, DecodeModel
+
+    m = DecodeModel(LLAMA3_8B, B, 1024, torch.device("cuda"), seed=11, quantize=True, attention="paged")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        m.step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        m.step()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("step")
+    a.record()
+    for _ in range(launches):
+        graph.replay()
+    b.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / launches
+    print(f"Llama-3-8B int8 decode step, {B} sequences x 1024 positions: {ms:.3f} ms/step ({B / ms * 1e3:.0f} tokens/s)")
+    assert ops.device_status() == 0
+
+
+def prefill_attention_case(E: int, launches: int) -> None:
+    H, H_kv, D, bs, qlen = 32, 8, 128, 16, 2048 // E
+    g = torch.Generator(device="cuda").manual_seed(0)
+    nbps = -(-qlen // bs)
+    nb = E * nbps + 1
+    bt = torch.randperm(nb, device="cuda", generator=g)[: E * nbps].view(E, nbps).to(torch.int32)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")
+    cl, off = i32([qlen] * E), i32([0] * E)
+    qs, ql = i32([e * qlen for e in range(E)]), i32([qlen] * E)
+    kp = torch.randn(nb, bs, H_kv, D, device="cuda", generator=g).to(torch.bfloat16)
+    vp = torch.randn(nb, bs, H_kv, D, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(H, E * qlen, D, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    for _ in range(2):
+        ops.paged_attention(q, kp, vp, bt, cl, off, qs, ql, bs, qlen, out=o)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(launches):
+        ops.paged_attention(q, kp, vp, bt, cl, off, qs, ql, bs, qlen, out=o)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / launches
+    flops = 4.0 * D * H * E * qlen * (qlen + 1) / 2
+    print(f"paged attention, {E} x {qlen}-token prefill: {ms * 1e3:.1f} us/launch ({flops / ms / 1e9:.1f} TFLOP/s)")
     assert ops.device_status() == 0
 
 
