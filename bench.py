@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-70b", action="store_true", help="skip the Llama-3-70B column-split sweep (config 5)")
     ap.add_argument("--no-e2e-decode", action="store_true", help="skip the end-to-end model decode (config 4)")
+    ap.add_argument("--no-engine-decode", action="store_true",
+                    help="skip config 4 through the reference engine's ModelRunner (needs baseline/_ref)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU sample length")
     return ap.parse_args()
@@ -457,6 +459,129 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
     out["small_batch"] = small
     del base, q8, q8_sdpa
     torch.cuda.empty_cache()
+    return out
+
+
+def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, context: int = 1024):
+    """Config 4 through the reference engine itself (its install in baseline/_ref): the
+    reference's `ModelRunner` with `use_custom_kernels` and `use_cuda_graphs`, decode graphs
+    captured at bucket `batch` (`capture_decode_graphs`, `_self_check` included), a
+    block_size-16 paged KV pool, `batch` greedy sequences prefilled to `context` tokens through
+    `forward_fused`, then decode steps through `ModelRunner.forward` (graph replay with the
+    engine's own host work: plan flattening, pinned H2D of the paging rows, one sampling sync
+    per step).  tokens/s = batch x steps / wall time.
+
+    Arms: `bf16_reference` (the stock engine: cuBLAS projections, its Triton paged attention),
+    `bf16_lse_attention` (the same with `attend_paged` bound to this package's kernel) and
+    `int8` (the `quantize="int8"` switch through `engine_hook.install()`: int8 projections and
+    this package's attention).  The weights are a random-init Llama-3-8B (seeded, built on the
+    GPU in place of `from_pretrained`: no checkpoint exists here); everything after the load is
+    the engine's unmodified code."""
+    import gc
+
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if os.path.isdir(ref_dir) and ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        import llm_serving_engine.model.model_runner as mr
+        from llm_serving_engine.config import ModelConfig
+        from llm_serving_engine.model.sampling import SamplingParams
+        from llm_serving_engine.observability.metrics import RequestMetrics
+        from llm_serving_engine.scheduling.allocator import BlockAllocator
+        from llm_serving_engine.scheduling.batch_plan import BatchEntry, BatchPlan
+        from llm_serving_engine.scheduling.sequence import Sequence
+    except Exception as e:  # noqa: BLE001 - the reference is optional here
+        return {"unavailable": f"the reference engine is not importable from baseline/_ref: {e}"}
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from llm_serving_engine_b200 import engine_hook
+
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                      num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=8192,
+                      rope_theta=500000.0, rms_norm_eps=1e-5, bos_token_id=None, eos_token_id=None,
+                      pad_token_id=None, tie_word_embeddings=False)
+
+    class _SyntheticLoader:
+        @staticmethod
+        def from_pretrained(path, dtype=None, **kwargs):
+            torch.manual_seed(0)
+            with torch.device(dev):
+                model = LlamaForCausalLM(cfg)
+            return model.to(dtype)
+
+    bs = 16
+    nblocks = batch * (-(-(context + warmup + steps + 1) // bs)) + 8
+    out = {"workload": f"config4 through the reference ModelRunner: Llama-3-8B shape, random init, {batch} sequences "
+                       f"prefilled to {context} tokens, greedy, decode graphs at bucket {batch}, block_size {bs}",
+           "unit": "tokens/s", "timing": "wall clock over the steps (each step ends in the engine's sampling sync)"}
+    original_loader = mr.AutoModelForCausalLM
+    mr.AutoModelForCausalLM = _SyntheticLoader
+    try:
+        for arm in ("bf16_reference", "bf16_lse_attention", "int8"):
+            quantize = "int8" if arm == "int8" else "none"
+            if arm == "int8":
+                engine_hook.install()
+            try:
+                runner = mr.ModelRunner(ModelConfig(model_name_or_path="synthetic-llama-3-8b", device=str(dev),
+                                                    dtype="bfloat16", quantize=quantize))
+            finally:
+                engine_hook.uninstall()
+            if arm == "bf16_lse_attention":
+                engine_hook.bind_paged_attention(runner)
+            runner.allocate_kv_pool(nblocks, bs)
+            runner.capture_decode_graphs([batch])
+            graphs_kept = batch in runner._decode_graphs.graphs
+            alloc = BlockAllocator(nblocks, bs)
+            gen = torch.Generator().manual_seed(5)
+            seqs = [Sequence(seq_id=i, prompt_tokens=torch.randint(1, 128000, (context,), generator=gen).tolist(),
+                             sampling_params=SamplingParams(temperature=0.0, max_tokens=1 << 20),
+                             metrics=RequestMetrics(enqueue_time=0.0)) for i in range(batch)]
+            by_id = {s.seq_id: s for s in seqs}
+            for c in range(0, batch, 8):  # prefill, 8 prompts per iteration (the scheduler's bookkeeping)
+                entries = []
+                for s in seqs[c:c + 8]:
+                    assert alloc.allocate(s, s.num_tokens)
+                    s.prefill_progress += s.num_tokens
+                    s.status = "DECODING"
+                    entries.append(BatchEntry(s.seq_id, s.num_tokens, is_prefill_chunk=True))
+                for sid, tok, _ in runner.forward(BatchPlan(entries=entries), by_id):
+                    by_id[sid].generated_tokens.append(tok)
+                    assert alloc.allocate(by_id[sid], 1)
+            eager = {"n": 0}
+            fused = runner.forward_fused
+
+            def counting_fused(*a, **k):
+                eager["n"] += 1
+                return fused(*a, **k)
+
+            runner.forward_fused = counting_fused
+
+            def step():
+                plan = BatchPlan(entries=[BatchEntry(s.seq_id, 1, is_prefill_chunk=False) for s in seqs])
+                for sid, tok, _ in runner.forward(plan, by_id):
+                    by_id[sid].generated_tokens.append(tok)
+                    assert alloc.allocate(by_id[sid], 1)
+
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize()
+            eager["n"] = 0
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                step()
+            torch.cuda.synchronize()
+            sec = time.perf_counter() - t0
+            out[arm] = {"tokens_per_s": round(batch * steps / sec, 1), "ms_per_step": round(sec / steps * 1e3, 4),
+                        "decode_graph_kept": graphs_kept, "eager_steps_in_timed_region": eager["n"],
+                        "context_at_end": seqs[0].num_tokens}
+            del runner, seqs, by_id, alloc
+            gc.collect()
+            torch.cuda.empty_cache()
+    finally:
+        mr.AutoModelForCausalLM = original_loader
+    out["int8_speedup_vs_bf16_reference"] = round(out["int8"]["tokens_per_s"] / out["bf16_reference"]["tokens_per_s"], 3)
+    out["int8_speedup_vs_bf16_lse_attention"] = round(
+        out["int8"]["tokens_per_s"] / out["bf16_lse_attention"]["tokens_per_s"], 3)
     return out
 
 
@@ -894,6 +1019,7 @@ def main():
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     mlp70b = None if args.no_70b else mlp70b_tp(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
+    engine4 = engine_decode(dev) if (world == 1 and not args.no_engine_decode) else None
 
     # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
     host_x = {k: v.cpu().pin_memory() for k, v in xs.items()}
@@ -957,6 +1083,8 @@ def main():
             line["config5_mlp_strong_scaling"] = mlp70b
         if decode4:
             line["config4_e2e_decode"] = decode4
+        if engine4:
+            line["config4_engine_decode"] = engine4
         if cpu_base:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)

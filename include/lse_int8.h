@@ -206,7 +206,9 @@ int lse_int8_gate_up_silu_packed_dt(const void *x, int dtype, int64_t M, int64_t
  *            launch shape and every call leaves them at zero, so one buffer per stream
  *            (grown when a shape needs more) serves all shapes.  workspace = NULL with
  *            workspace_bytes = 0 asks for the unsplit launch (one CTA per sequence and KV head,
- *            no workspace), available while max_context <= 1023 * block_size
+ *            no workspace) for any max_context; it covers a sequence's first 1024 blocks of
+ *            positions, and a longer context_len is cut there and reported as
+ *            LSE_ERR_UNSUPPORTED by lse_device_status
  * D = 64 or 128 and G in {1, 2, 4, 8} (LSE_ERR_UNSUPPORTED otherwise).  fp32 softmax and
  * accumulation, one bf16 rounding of o.  A sequence with context_len 0 gets zeros.
  */

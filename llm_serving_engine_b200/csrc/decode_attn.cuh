@@ -115,20 +115,27 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");  // q and the pool come from earlier kernels
 
     // The context length, this CTA's slice of the block table (every entry of positions below
-    // max_context: independent of the context length, so both loads are in flight together)
-    // and q (below) are read at once; block ids are range-checked where they are used.
+    // max_context, at most MAX_TABLE of them: independent of the context length, so both loads
+    // are in flight together) and q (below) are read at once; block ids are range-checked where
+    // they are used.  A split launch sizes its chunks so that a chunk's entries always fit; an
+    // unsplit launch (no workspace) sized for a long max_context stages the first MAX_TABLE
+    // entries and covers contexts up to MAX_TABLE blocks, reporting a longer one.
     __shared__ int s_blk[MAX_TABLE];
     const int begin = split * p.chunk;
     const int first_bi = begin / p.block_size;
     const int span = min(p.max_ctx, begin + p.chunk);  // positions this CTA may cover
-    const int n_bi = span > begin ? (span - 1) / p.block_size - first_bi + 1 : 0;
+    const int n_bi = span > begin ? min((span - 1) / p.block_size - first_bi + 1, MAX_TABLE) : 0;
     for (int i = threadIdx.x; i < n_bi; i += THREADS) s_blk[i] = p.block_table[e * p.bt_stride + first_bi + i];
     int ctx = p.context_len[e];
     if (ctx > p.max_ctx) {  // beyond the max_context the launch was sized for
         if (split == 0 && threadIdx.x == 0) report_status(LSE_ERR_INVALID_ARG);
         ctx = p.max_ctx;
     }
-    const int end = min(ctx, begin + p.chunk);
+    int end = min(ctx, begin + p.chunk);
+    if (end > (first_bi + n_bi) * p.block_size) {  // positions whose block ids were not staged
+        if (threadIdx.x == 0) report_status(LSE_ERR_UNSUPPORTED);
+        end = (first_bi + n_bi) * p.block_size;
+    }
 
     // Q as the row operand, rows = query heads (rows >= G and 8..15 are zero): per K16 step
     // j, a0 = Q[r0][16j + 2q4 .. +1], a2 = Q[r0][16j + 8 + 2q4 .. +1].

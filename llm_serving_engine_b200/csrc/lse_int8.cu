@@ -1130,8 +1130,11 @@ AttnPlan plan_attn(int64_t E, int64_t H_kv, int64_t max_context, int64_t block_s
     const int64_t min_chunk = attn_min_chunk();
     const int64_t target = attn_target_ctas(num_sms);
     const int64_t cap = std::max<int64_t>(1, (max_context + min_chunk - 1) / min_chunk);
+    if (unsplit)  // one CTA per (sequence, KV head) over all of max_context (the kernel stages
+                  // at most attn::MAX_TABLE block ids and reports a longer context)
+        return {1, static_cast<int>(std::max<int64_t>(32, (max_context + 31) / 32 * 32))};
     int64_t splits = 1;
-    if (!unsplit && 2 * pairs <= target && pairs <= kAttnMaxSplitPairs) splits = std::min<int64_t>(target / pairs, cap);
+    if (2 * pairs <= target && pairs <= kAttnMaxSplitPairs) splits = std::min<int64_t>(target / pairs, cap);
     // a CTA stages at most attn::MAX_TABLE block-table entries (chunk / block_size + 1)
     const int64_t max_chunk = (attn::MAX_TABLE - 1) * block_size / 32 * 32;
     splits = std::max<int64_t>(splits, (max_context + max_chunk - 1) / max_chunk);

@@ -380,7 +380,8 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     [E, H, D] = softmax(q K^T * scale) V over each sequence's positions, scale = 1/sqrt(D) by
     default (`paged_attention_forward`, `kernels/flash_attention.py:287-332`, with q_len 1).
     split=False runs one CTA per (sequence, KV head) with no workspace (nothing to size or keep
-    per stream; max_context <= 1023 * block_size).
+    per stream; any max_context, a sequence's first 1024 blocks of positions covered, a longer
+    context reported as LSE_ERR_UNSUPPORTED on the status word).
     """
     if not all(t.is_cuda for t in (q, k_pool, v_pool, block_table, context_len)):
         raise RuntimeError("paged_decode_attention runs on CUDA only (no CPU fallback)")

@@ -188,3 +188,28 @@ def test_unsplit_launch_without_workspace(E, ctx):
                                      bt.numpy(), cl.numpy())
     check_parity(o.reshape(E * 32, 128), ref.reshape(E * 32, 128), f"unsplit attention E={E}")
     assert ops.device_status() == 0
+
+
+def test_unsplit_launch_with_the_engines_wide_block_table():
+    """The engine's decode graphs size the launch by the block table's width (every block a
+    sequence may ever hold: here 4096 blocks, max_context 65536 positions), far beyond the
+    1024 block ids one CTA stages; the actual contexts are short.  The unsplit launch gives the
+    oracle's result, and a context past the staged 1024 blocks is cut and reported
+    (LSE_ERR_UNSUPPORTED on the status word), never read."""
+    E, H, H_kv, D, bs = 3, 32, 8, 128, 16
+    q, k_pool, v_pool, bt, cl, _ = _case(E, H, H_kv, D, bs, [5, 1000, 2049], seed=31)
+    wide = torch.zeros(E, 4096, dtype=torch.int32)
+    wide[:, : bt.shape[1]] = bt
+    o = ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), wide.cuda(), cl.cuda(), 4096 * bs,
+                                   split=False)
+    torch.cuda.synchronize()
+    ref = ref_paged_decode_attention(q.float().numpy(), k_pool.float().numpy(), v_pool.float().numpy(),
+                                     bt.numpy(), cl.numpy())
+    check_parity(o.reshape(E * H, D), ref.reshape(E * H, D), "unsplit attention, wide block table")
+    assert ops.device_status() == 0
+    # one sequence of 1025 blocks: cut at 1024 blocks and reported
+    q, k_pool, v_pool, bt, cl, _ = _case(1, H, H_kv, D, bs, [1024 * bs + 3], seed=32)
+    ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda(), cl.cuda(), 1024 * bs + 3,
+                               split=False)
+    assert ops.device_status() == _lib.LSE_ERR_UNSUPPORTED
+    assert ops.device_status() == 0
