@@ -68,6 +68,10 @@ cudaError_t set_tci8_attrs_all() {
     if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK, false>();
     if (e == cudaSuccess) e = set_tci8_attrs<64, 3, SILU, WPACK, true>();
     if (e == cudaSuccess) e = set_tci8_attrs<128, 2, SILU, WPACK, true>();
+#ifdef LSE_TUNING
+    if (e == cudaSuccess) e = set_tci8_attrs<64, 2, SILU, WPACK, false>();
+    if (e == cudaSuccess) e = set_tci8_attrs<64, 2, SILU, WPACK, true>();
+#endif
     return e;
 }
 
@@ -219,7 +223,8 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms, int dev) {
     // stream ran at the HBM rate, and the partial publication plus the last arriver's sum
     // added 6-9 us after the last MMA.
     if (t.tiles <= G / 2 && dev >= 0) {
-        int c = std::min(std::min(G / t.tiles, kMaxCluster), t.kb);
+        static const int cmax = tuning_knob("LSE_TC_CMAX", kMaxCluster);
+        int c = std::min(std::min(G / t.tiles, cmax), t.kb);
         while (c >= 2 && g_max_clusters[dev][t.nt == 128 ? 1 : 0][c] < t.tiles) --c;
         if (c >= 2) {
             t.cluster = c;
@@ -231,7 +236,10 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms, int dev) {
     }
     if (t.tiles % G == 0) t.dp_tiles = t.tiles;
     else if (t.tiles < G) t.dp_tiles = 0;
-    else t.dp_tiles = (t.tiles / G - 1) * G;
+    else {
+        static const int sk_waves = tuning_knob("LSE_TC_SK_WAVES", 2);  // waves left to stream-K: 1 or 2
+        t.dp_tiles = (t.tiles / G - (sk_waves >= 2 ? 1 : 0)) * G;
+    }
     // At most half a wave of tiles (decode shapes): split every tile's K range over the same
     // number s of CTAs (grid tiles * s, s = num_sms / tiles), so that each CTA works on one
     // tile and each tile's last arriver sums s partials.  Spreading the units evenly over all
@@ -293,7 +301,10 @@ int encode_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64
 
 // Digit planes of the int8 tensor-core path: 3 (24-bit activations) up to 64 tokens, where the
 // MMA's N = 3 x 64 costs nothing against the weight stream, 2 (16-bit) above.
-int digit_planes(int64_t M) { return M <= 64 ? 3 : 2; }
+int digit_planes(int64_t M) {
+    static const int s64 = tuning_knob("LSE_TC_S64", 3);
+    return M <= 64 ? s64 : 2;
+}
 
 size_t tci8_partial_bytes(int nt, int grid) { return static_cast<size_t>(2) * grid * nt * tci8::BN * sizeof(float); }
 
@@ -395,6 +406,10 @@ template <bool SILU>
 int run_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
               const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
               cudaStream_t st, bool xf16 = false) {
+#ifdef LSE_TUNING
+    if (pl.nt == 64 && digit_planes(M) == 2)
+        return launch_tc_i8<64, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
+#endif
     if (pl.nt == 64) return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
     return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
 }
