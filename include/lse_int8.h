@@ -250,6 +250,30 @@ int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int
 int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
                  int64_t ldy, void *stream);
 
+/*
+ * RMSNorm fused with the packed projection that consumes it, bf16 activations: the decoder
+ * layer's qkv(input_layernorm(h)) (model_runner.py:213-224 with the fused QKV of :310-326) and
+ * mlp(post_attention_layernorm(h)) up to the SiLU * mul (modeling_llama.py:171-184):
+ *   lse_int8_rms_norm_linear_packed:       y = lse_int8_linear_packed(rms_norm(x, norm_weight, eps))
+ *   lse_int8_rms_norm_gate_up_silu_packed: y = lse_int8_gate_up_silu_packed_ws(rms_norm(x, ...))
+ * with rms_norm as lse_rms_norm (K = the normalised width), and the same results bit for bit
+ * as those two calls in sequence.  Above 16 tokens the normalisation writes the tensor-core
+ * kernel's activation digit planes directly (no normalised copy of x, one launch fewer); up to
+ * 16 tokens the normalised rows pass through the workspace to the decode kernel.
+ *   norm_weight  bf16 [K], 16-byte aligned; eps >= 0
+ *   workspace    >= lse_int8_rms_norm_proj_workspace(M, K) bytes (the same N-independent
+ *                bound as lse_int8_linear_workspace above 16 tokens, M * K * 2 bytes up to 16),
+ *                16-byte aligned, contents irrelevant
+ * Other arguments and status codes as the unfused entries.
+ */
+size_t lse_int8_rms_norm_proj_workspace(int64_t M, int64_t K);
+int lse_int8_rms_norm_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const void *norm_weight,
+                                    float eps, const int8_t *w_packed, const float *scale, int64_t N, void *y,
+                                    int64_t ldy, void *workspace, size_t workspace_bytes, void *stream);
+int lse_int8_rms_norm_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const void *norm_weight,
+                                          float eps, const int8_t *w_packed, const float *scale, int64_t I, void *y,
+                                          int64_t ldy, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Bytes of the counter region at the start of every linear workspace (the tensor-core path
  * clears the counters it uses before each launch). */
 #define LSE_WS_COUNTER_BYTES 65536

@@ -59,6 +59,11 @@ SIGNATURES = {
                                   _I32),
     "lse_int8_gate_up_silu_packed_dt": ([_P, _I32, _I64, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _SZ, _P], _I32),
     "lse_rms_norm": ([_P, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P], _I32),
+    "lse_int8_rms_norm_proj_workspace": ([_I64, _I64], _SZ),
+    "lse_int8_rms_norm_linear_packed": ([_P, _I64, _I64, _I64, _P, ctypes.c_float, _P, _P, _I64, _P, _I64, _P, _SZ, _P],
+                                        _I32),
+    "lse_int8_rms_norm_gate_up_silu_packed": ([_P, _I64, _I64, _I64, _P, ctypes.c_float, _P, _P, _I64, _P, _I64, _P,
+                                               _SZ, _P], _I32),
     "lse_rope_kv_write": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P, _P, _I64, _P], _I32),
     "lse_paged_decode_attention_workspace": ([_I64, _I64, _I64, _I64, _I64, _I64], _SZ),
     "lse_paged_decode_attention": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64,

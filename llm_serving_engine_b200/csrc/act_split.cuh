@@ -189,5 +189,138 @@ act_split_kernel(const XT *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *_
     if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);
 }
 
+// RMSNorm fused in front of the split (bf16): the digit planes and row scale of
+//   x_n[m, :] = bf16( x[m, :] * rsqrt(mean(x[m, :]^2) + eps) * w[:] )
+// without writing x_n.  The sum of squares is accumulated in rms_norm_kernel's order (thread t
+// takes the 8-element chunks t, t + THREADS, ...; shuffle tree; the warps' sums in order) and
+// x_n is the same fp32 expression rounded once, so the planes equal act_split_kernel's planes
+// of rms_norm_kernel's output bit for bit.  A row of up to THREADS * CPT * 8 elements stays in
+// registers; a longer one is read again per pass.
+__device__ __forceinline__ uint32_t rms_scaled_pair(uint32_t u, uint32_t g, float r) {
+    const float a = __uint_as_float(u << 16) * r * __uint_as_float(g << 16);
+    const float b = __uint_as_float(u & 0xffff0000u) * r * __uint_as_float(g & 0xffff0000u);
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&p);
+}
+
+template <int S>
+__global__ void __launch_bounds__(THREADS)
+rms_norm_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, const __nv_bfloat16 *__restrict__ w,
+                      float eps, int K, int Kp, int8_t *__restrict__ planes, int64_t plane_stride,
+                      float *__restrict__ row_scale, int *__restrict__ counters, int n_counters) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    const int m = blockIdx.x;
+    if (m == 0)
+        for (int i = threadIdx.x; i < n_counters; i += THREADS) counters[i] = 0;
+    const __nv_bfloat16 *xr = x + static_cast<int64_t>(m) * ldx;
+    const int nk = K >> 3;
+    constexpr int BATCH = THREADS * CPT;
+    const bool one_batch = nk <= BATCH;
+    uint4 v[CPT];
+    auto load_x = [&](int base) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int c = base + threadIdx.x + i * THREADS;
+            v[i] = c < nk ? __ldg(reinterpret_cast<const uint4 *>(xr + 8 * c)) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float s_red[THREADS / 32];
+    __shared__ int s_bad[THREADS / 32];
+    // pass 1: sum of squares
+    float ss = 0.f;
+    for (int base = 0; base < nk; base += BATCH) {
+        load_x(base);
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+                ss = fmaf(a, a, fmaf(b, b, ss));
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) tot += s_red[i];
+    const float r = rsqrtf(tot / static_cast<float>(K) + eps);
+    __syncthreads();  // s_red is reused below
+    // pass 2: the normalised bf16 row and its maximum magnitude
+    auto normalise = [&](int base) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int c = base + threadIdx.x + i * THREADS;
+            if (c < nk) {
+                const uint4 g = __ldg(reinterpret_cast<const uint4 *>(w) + c);
+                v[i] = make_uint4(rms_scaled_pair(v[i].x, g.x, r), rms_scaled_pair(v[i].y, g.y, r),
+                                  rms_scaled_pair(v[i].z, g.z, r), rms_scaled_pair(v[i].w, g.w, r));
+            }
+        }
+    };
+    float amax = 0.f;
+    bool bad = false;
+    for (int base = 0; base < nk; base += BATCH) {
+        if (!one_batch) load_x(base);
+        normalise(base);
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float a = fabsf(act_lo<__nv_bfloat16>(u[k])), b = fabsf(act_hi<__nv_bfloat16>(u[k]));
+                bad |= !(a <= 3.4e38f) || !(b <= 3.4e38f);  // NaN or infinity
+                amax = fmaxf(amax, fmaxf(a, b));
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        bad |= __shfl_xor_sync(0xffffffffu, static_cast<int>(bad), o) != 0;
+    }
+    if (lane == 0) {
+        s_red[warp] = amax;
+        s_bad[warp] = bad;
+    }
+    __syncthreads();
+    amax = 0.f;
+    bad = false;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) {
+        amax = fmaxf(amax, s_red[i]);
+        bad |= s_bad[i] != 0;
+    }
+    int e = 0;
+    if (!bad && amax > 0.f) {
+        e = ilogbf(amax) - Digits<S>::kTopExp;
+        if (ldexpf(amax, -e) > static_cast<float>(Digits<S>::kMaxV)) ++e;  // an all-ones mantissa
+    }
+    const int ne = -e;
+    const int ne_hi = max(-126, min(127, ne));
+    const float inv_hi = exp2_exact(ne_hi), inv_lo = exp2_exact(ne - ne_hi);
+    // pass 3: digits
+    const int64_t row_off = static_cast<int64_t>(m) * Kp;
+    const int nkp = Kp >> 3;
+    for (int base = 0; base < nkp; base += BATCH) {
+        if (!one_batch) {
+            load_x(base);
+            normalise(base);
+        }
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int c = base + threadIdx.x + i * THREADS;
+            if (c < nkp)
+                store_digits<S, __nv_bfloat16>(planes, plane_stride, row_off, c, v[i], inv_hi, inv_lo, c < nk && !bad);
+        }
+    }
+    if (threadIdx.x == 0) row_scale[m] = bad ? __int_as_float(0x7FC00000) : ldexpf(1.f, e);
+}
+
 }  // namespace split
 }  // namespace lse

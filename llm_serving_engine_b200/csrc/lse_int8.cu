@@ -318,7 +318,7 @@ size_t tci8_workspace_bytes(int nt, int S, int grid, int64_t M, int64_t K) {
 template <int NT, int S, bool SILU>
 int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
                  const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws,
-                 bool packed, cudaStream_t st, bool xf16) {
+                 bool packed, cudaStream_t st, bool xf16, const void *norm_w, float eps) {
     const int64_t Kp = packed_cols(K);
     uint8_t *wsb = static_cast<uint8_t *>(ws);
     int *counters = reinterpret_cast<int *>(wsb);
@@ -326,13 +326,19 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
     int8_t *planes = reinterpret_cast<int8_t *>(wsb + LSE_WS_COUNTER_BYTES + tci8_partial_bytes(NT, pl.grid));
     const int64_t plane_stride = M * Kp;
     float *rscale = reinterpret_cast<float *>(planes + S * plane_stride);
-    // 1) activations -> digit planes + row scales (also clears this launch's stream-K counters)
+    // 1) activations -> digit planes + row scales (also clears this launch's stream-K counters);
+    //    with norm_w, of the RMSNorm of the activations (bf16)
     {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(split::THREADS), 0, st);
         const int n_counters = pl.cluster >= 2 ? 0 : static_cast<int>(pl.tiles - pl.dp_tiles);
-        cudaError_t e = xf16 ? cudaLaunchKernelEx(&cfg, split::act_split_kernel<S, __half>, static_cast<const __half *>(x),
+        cudaError_t e = norm_w ? cudaLaunchKernelEx(&cfg, split::rms_norm_split_kernel<S>,
+                                                    static_cast<const __nv_bfloat16 *>(x), ldx,
+                                                    static_cast<const __nv_bfloat16 *>(norm_w), eps, static_cast<int>(K),
+                                                    static_cast<int>(Kp), planes, plane_stride, rscale, counters,
+                                                    n_counters)
+                      : xf16 ? cudaLaunchKernelEx(&cfg, split::act_split_kernel<S, __half>, static_cast<const __half *>(x),
                                                   ldx, static_cast<int>(K), static_cast<int>(Kp), planes, plane_stride,
                                                   rscale, counters, n_counters)
                              : cudaLaunchKernelEx(&cfg, split::act_split_kernel<S, __nv_bfloat16>,
@@ -405,13 +411,14 @@ int launch_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t 
 template <bool SILU>
 int run_tc_i8(const TcPlan &pl, const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w,
               const float *scale, int64_t N, void *y, int64_t ldy, const void *res, int64_t ldr, void *ws, bool packed,
-              cudaStream_t st, bool xf16 = false) {
+              cudaStream_t st, bool xf16 = false, const void *norm_w = nullptr, float eps = 0.f) {
 #ifdef LSE_TUNING
     if (pl.nt == 64 && digit_planes(M) == 2)
-        return launch_tc_i8<64, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
+        return launch_tc_i8<64, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16, norm_w, eps);
 #endif
-    if (pl.nt == 64) return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
-    return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16);
+    if (pl.nt == 64)
+        return launch_tc_i8<64, 3, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16, norm_w, eps);
+    return launch_tc_i8<128, 2, SILU>(pl, x, M, K, ldx, w, scale, N, y, ldy, res, ldr, ws, packed, st, xf16, norm_w, eps);
 }
 
 template <int MT, int ROWS>
@@ -1356,4 +1363,70 @@ extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, co
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "rms_norm launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// RMSNorm fused with the projection that consumes it (bf16): the decoder layer's
+// q/k/v(input_layernorm(h)) and mlp.gate_up(post_attention_layernorm(h)).  Up to 16 tokens
+// the normalised rows go through the workspace to the decode kernel; above, the digit planes
+// are written straight from the normalisation (split::rms_norm_split_kernel) and the separate
+// split launch disappears.
+// ---------------------------------------------------------------------------------------
+namespace lse {
+namespace {
+size_t norm_proj_workspace(int64_t M, int64_t K) {
+    if (M <= 0 || K < 0) return 0;
+    if (M <= 16) return (static_cast<size_t>(M) * K * 2 + 15) / 16 * 16;
+    return tci8_workspace_bytes(token_tile(M), digit_planes(M), kMaxGridForWorkspace, M, K);
+}
+
+int norm_proj_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const void *norm_w, float eps,
+                   const int8_t *w_packed, const float *scale, int64_t N_out, bool silu, void *y, int64_t ldy,
+                   void *workspace, size_t workspace_bytes, void *stream) {
+    if (M < 0 || N_out < 0 || K < 0 || !(eps >= 0.f)) return LSE_ERR_INVALID_ARG;
+    if (M == 0 || N_out == 0) return LSE_OK;
+    if (!x || !norm_w || !w_packed || !scale || !y) return LSE_ERR_INVALID_ARG;
+    if (ldx < K || ldy < N_out || K == 0) return LSE_ERR_INVALID_ARG;
+    if (silu && (N_out % 8)) return LSE_ERR_UNSUPPORTED;
+    const int64_t N = silu ? 2 * N_out : N_out;
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LSE_ERR_UNSUPPORTED;
+    if ((K & 15) || (ldx & 7) || !aligned16(x) || !aligned16(w_packed) || !aligned16(norm_w)) return LSE_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(y) & 1u) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return LSE_ERR_ALIGNMENT;
+    if (!workspace || !aligned16(workspace) || workspace_bytes < norm_proj_workspace(M, K)) return LSE_ERR_WORKSPACE;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (M <= 16) {
+        rc = lse_rms_norm(x, M, K, ldx, norm_w, eps, workspace, K, stream);
+        if (rc) return rc;
+        return silu ? gate_up_impl(workspace, M, K, K, w_packed, scale, N_out, y, ldy, nullptr, 0, stream, false, true)
+                    : linear_impl(workspace, M, K, K, w_packed, scale, N, y, ldy, nullptr, 0, LSE_ALGO_SKINNY, true,
+                                  stream);
+    }
+    const TcPlan pl = plan_tc(M, K, N, g_dev[dev].num_sms, dev);
+    if (workspace_bytes < tci8_workspace_bytes(pl.nt, digit_planes(M), pl.grid, M, K)) return LSE_ERR_WORKSPACE;
+    return silu ? run_tc_i8<true>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st, false,
+                                  norm_w, eps)
+                : run_tc_i8<false>(pl, x, M, K, ldx, w_packed, scale, N, y, ldy, nullptr, 0, workspace, true, st,
+                                   false, norm_w, eps);
+}
+}  // namespace
+}  // namespace lse
+
+extern "C" size_t lse_int8_rms_norm_proj_workspace(int64_t M, int64_t K) { return norm_proj_workspace(M, K); }
+
+extern "C" int lse_int8_rms_norm_linear_packed(const void *x, int64_t M, int64_t K, int64_t ldx, const void *norm_weight,
+                                               float eps, const int8_t *w_packed, const float *scale, int64_t N, void *y,
+                                               int64_t ldy, void *workspace, size_t workspace_bytes, void *stream) {
+    return norm_proj_impl(x, M, K, ldx, norm_weight, eps, w_packed, scale, N, false, y, ldy, workspace,
+                          workspace_bytes, stream);
+}
+
+extern "C" int lse_int8_rms_norm_gate_up_silu_packed(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                                     const void *norm_weight, float eps, const int8_t *w_packed,
+                                                     const float *scale, int64_t I, void *y, int64_t ldy,
+                                                     void *workspace, size_t workspace_bytes, void *stream) {
+    return norm_proj_impl(x, M, K, ldx, norm_weight, eps, w_packed, scale, I, true, y, ldy, workspace,
+                          workspace_bytes, stream);
 }

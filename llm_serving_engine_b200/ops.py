@@ -39,7 +39,7 @@ __all__ = [
     "paged_attention",
     "set_wait_limit",
     "rope_kv_write",
-    "rms_norm",
+    "rms_norm", "rms_norm_proj",
     "pool_slot_offsets",
     "linear_workspace",
     "device_status",
@@ -310,6 +310,43 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tenso
     rc = _lib.load().lse_rms_norm(x2.data_ptr(), x2.shape[0], N, x2.stride(0), weight.data_ptr(), float(eps),
                                   y2.data_ptr(), y2.stride(0), torch.cuda.current_stream(x.device).cuda_stream)
     _lib.check(rc, "lse_rms_norm")
+    return out
+
+
+def rms_norm_proj(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, w_packed: torch.Tensor, scale: torch.Tensor,
+                  N: int, K: int, silu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The packed projection of `rms_norm(x, norm_weight, eps)` in one call, bf16: with
+    silu=False `int8_linear_packed(rms_norm(x), w_packed, scale, N, K)` ([..., N]); with
+    silu=True `int8_gate_up_silu_packed(rms_norm(x), w_packed, scale, N, K)` ([..., N], the
+    weight holding 2N interleaved gate/up rows).  Bitwise the same as those two calls; above 16
+    tokens the normalisation writes the tensor-core kernel's digit planes directly."""
+    _check_x(x, K, norm_weight, w_packed, scale)
+    if x.dtype != torch.bfloat16 or norm_weight.dtype != torch.bfloat16 or norm_weight.shape != (K,) \
+            or not norm_weight.is_contiguous():
+        raise ValueError(f"rms_norm_proj: x must be bf16 and norm_weight contiguous bf16 [{K}]")
+    rows = 2 * N if silu else N
+    if w_packed.dtype != torch.int8 or w_packed.numel() != packed_weight_bytes(rows, K) or not w_packed.is_contiguous():
+        raise ValueError(f"rms_norm_proj: w_packed must be the packed int8 buffer of [{rows}, {K}]")
+    if scale.dtype != torch.float32 or scale.shape != (rows,):
+        raise ValueError(f"rms_norm_proj: scale must be float32 [{rows}]")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    elif out.dtype != x.dtype or out.shape != (*lead, N) or not out.is_contiguous():
+        raise ValueError("rms_norm_proj: out must be contiguous [..., N] bf16")
+    if M == 0:
+        return out
+    _ensure_device(x.device)
+    lib = _lib.load()
+    ws = torch.empty(int(lib.lse_int8_rms_norm_proj_workspace(M, K)), dtype=torch.uint8, device=x.device)
+    fn = lib.lse_int8_rms_norm_gate_up_silu_packed if silu else lib.lse_int8_rms_norm_linear_packed
+    rc = fn(x2.data_ptr(), M, K, x2.stride(0), norm_weight.data_ptr(), float(eps), w_packed.data_ptr(), scale.data_ptr(),
+            N, out.data_ptr(), N, ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(rc, "lse_int8_rms_norm_gate_up_silu_packed" if silu else "lse_int8_rms_norm_linear_packed")
     return out
 
 

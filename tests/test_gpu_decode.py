@@ -132,3 +132,15 @@ def test_paged_attention_step_matches_sdpa_on_the_same_cache():
     a, b = paged.logits(tokens), sdpa.logits(tokens)
     err = ((a - b).abs().max() / b.abs().max()).item()
     assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("batch", [4, 24])  # decode kernel / tensor-core kernel
+def test_fused_norm_projections_give_the_same_step(batch):
+    """fuse_norms=True (each RMSNorm fused into the projection that consumes it) produces the
+    same logits bit for bit as the separate RMSNorm and projection launches."""
+    m = DecodeModel(TINY, batch=batch, context=16, device="cuda", seed=9, quantize=True)
+    tokens = (torch.arange(batch, device="cuda") * 13) % TINY.vocab
+    separate = m.logits(tokens).clone()
+    m.fuse_norms = True
+    fused = m.logits(tokens)
+    assert torch.equal(fused, separate)
