@@ -472,9 +472,10 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     per step).  tokens/s = batch x steps / wall time.
 
     Arms: `bf16_reference` (the stock engine: cuBLAS projections, its Triton paged attention),
-    `bf16_lse_attention` (the same with `attend_paged` bound to this package's kernel) and
-    `int8` (the `quantize="int8"` switch through `engine_hook.install()`: int8 projections and
-    this package's attention).  The weights are a random-init Llama-3-8B (seeded, built on the
+    `bf16_lse_attention` (the same with `attend_paged` bound to this package's kernel),
+    `int8` (the `quantize="int8"` switch through `engine_hook.install()`: int8 projections, this
+    package's attention, and `write_kv_and_project_q` on the fused QKV output with the RoPE +
+    K/V write kernel) and `int8_no_rope` (the same without that last binding).  The weights are a random-init Llama-3-8B (seeded, built on the
     GPU in place of `from_pretrained`: no checkpoint exists here); everything after the load is
     the engine's unmodified code."""
     import gc
@@ -517,10 +518,10 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     original_loader = mr.AutoModelForCausalLM
     mr.AutoModelForCausalLM = _SyntheticLoader
     try:
-        for arm in ("bf16_reference", "bf16_lse_attention", "int8"):
-            quantize = "int8" if arm == "int8" else "none"
-            if arm == "int8":
-                engine_hook.install()
+        for arm in ("bf16_reference", "bf16_lse_attention", "int8_no_rope", "int8"):
+            quantize = "int8" if arm.startswith("int8") else "none"
+            if quantize == "int8":
+                engine_hook.install(rope=arm == "int8")
             try:
                 runner = mr.ModelRunner(ModelConfig(model_name_or_path="synthetic-llama-3-8b", device=str(dev),
                                                     dtype="bfloat16", quantize=quantize))
@@ -582,6 +583,8 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     out["int8_speedup_vs_bf16_reference"] = round(out["int8"]["tokens_per_s"] / out["bf16_reference"]["tokens_per_s"], 3)
     out["int8_speedup_vs_bf16_lse_attention"] = round(
         out["int8"]["tokens_per_s"] / out["bf16_lse_attention"]["tokens_per_s"], 3)
+    out["int8_no_rope_speedup_vs_bf16_lse_attention"] = round(
+        out["int8_no_rope"]["tokens_per_s"] / out["bf16_lse_attention"]["tokens_per_s"], 3)
     return out
 
 

@@ -30,7 +30,7 @@ import torch
 from . import ops
 from .int8_linear import quantize_llama_
 
-__all__ = ["enable_int8", "bind_paged_attention", "install", "uninstall", "installed"]
+__all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "install", "uninstall", "installed"]
 
 
 def _attend_paged(runner, q, layer_idx, paging):
@@ -49,6 +49,34 @@ def _attend_paged(runner, q, layer_idx, paging):
                                paging.q_start, paging.q_len, runner._block_size, paging.max_q_len)
 
 
+def _write_kv_and_project_q(runner, original, normed, position_embeddings, layer_idx, dest_block_id, dest_within):
+    """`ModelRunner.write_kv_and_project_q` (`model_runner.py:342-355`) as two launches: the
+    layer's fused int8 QKV projection, then one kernel that rotates q and k (rotate-half RoPE
+    in fp32, one rounding), writes k and v into their pool slots and returns q as (heads,
+    tokens, head_dim).  Layers without a fused int8 QKV, and dtypes other than bf16, take the
+    reference's own code."""
+    attn = runner._layers[layer_idx].self_attn
+    qkv_mod = getattr(attn, "qkv_int8", None)
+    if qkv_mod is None or normed.dtype != torch.bfloat16:
+        return original(normed, position_embeddings, layer_idx, dest_block_id, dest_within)
+    cos, sin = position_embeddings
+    T = normed.shape[1]
+    qkv = qkv_mod.fused(normed[0])  # [T, (H + 2 H_kv) * D]
+    k_pool, v_pool = runner._k_pool[layer_idx], runner._v_pool[layer_idx]
+    off = ops.pool_slot_offsets(dest_block_id, dest_within, k_pool)
+    return ops.rope_kv_write(qkv, runner.n_heads, runner.n_kv_heads, runner.head_dim, cos[0].reshape(T, -1),
+                             sin[0].reshape(T, -1), k_pool, v_pool, off)
+
+
+def bind_rope_kv_write(runner):
+    """Route the runner's `write_kv_and_project_q` (the K/V write and q of paged attention, in
+    the eager, decode-graph and piecewise paths) through the fused QKV projection and this
+    package's RoPE + K/V write kernel (an instance attribute, as `bind_paged_attention`)."""
+    runner.write_kv_and_project_q = functools.partial(_write_kv_and_project_q, runner,
+                                                      runner.write_kv_and_project_q)
+    return runner
+
+
 def bind_paged_attention(runner):
     """Route the runner's paged attention to `ops.paged_attention` (an instance attribute, so
     the runner's own `paged_attention` and the graph runners call it)."""
@@ -56,19 +84,22 @@ def bind_paged_attention(runner):
     return runner
 
 
-def enable_int8(runner, lm_head: bool = False, attention: bool = True):
+def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: bool = True):
     """Swap a loaded `ModelRunner`'s projections to int8 in place.  `runner.model` is the
     Llama-family model the runner loaded; every decoder layer's q/k/v (one fused int8 QKV),
     o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`;
-    with `attention=True` the paged attention runs on this package's kernel too.  Nothing else
-    needs preparing: the ops hold no per-stream state, so the engine's graph captures on any
-    stream record them as they are."""
+    with `attention=True` the paged attention runs on this package's kernel too, and with
+    `rope=True` the K/V write and q (`write_kv_and_project_q`) on the fused QKV projection and
+    the RoPE + K/V write kernel.  Nothing else needs preparing: the ops hold no per-stream
+    state, so the engine's graph captures on any stream record them as they are."""
     device = torch.device(runner.device)
     if device.type != "cuda":
         raise RuntimeError(f"int8 weight-only quantization needs a CUDA device, got {runner.device!r}")
     quantize_llama_(runner.model, lm_head=lm_head)
     if attention:
         bind_paged_attention(runner)
+    if rope:
+        bind_rope_kv_write(runner)
     return runner
 
 
@@ -89,8 +120,9 @@ def installed() -> bool:
     return getattr(_runner_class().__init__, "_lse_int8", False)
 
 
-def install(lm_head: bool = False) -> None:
-    """Make `ModelRunner(ModelConfig(quantize="int8"))` load an int8 model (idempotent)."""
+def install(lm_head: bool = False, rope: bool = True) -> None:
+    """Make `ModelRunner(ModelConfig(quantize="int8"))` load an int8 model (idempotent; the
+    options of the first call stay until `uninstall`)."""
     cls = _runner_class()
     if installed():
         return
@@ -103,7 +135,7 @@ def install(lm_head: bool = False) -> None:
         _check_cuda(config)
         original(self, dataclasses.replace(config, quantize="none"), *args, **kwargs)
         self.config = config
-        enable_int8(self, lm_head=lm_head)
+        enable_int8(self, lm_head=lm_head, rope=rope)
 
     __init__._lse_int8 = True
     __init__._lse_original = original

@@ -58,3 +58,19 @@ def test_install_is_idempotent_and_uninstall_restores():
     engine_hook.uninstall()
     assert ModelRunner.__init__ is original
     assert not engine_hook.installed()
+
+
+def test_rope_binding_defers_to_the_reference_without_a_fused_int8_qkv(tiny_dir):
+    """`bind_rope_kv_write` only takes layers that carry a fused int8 QKV (in bf16); any other
+    layer runs the reference's own `write_kv_and_project_q`, with the same arguments."""
+    import torch
+
+    runner = ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cpu", dtype="float32",
+                                     use_custom_kernels=False))
+    calls = []
+    runner.write_kv_and_project_q = lambda *args: calls.append(args) or "reference"
+    engine_hook.bind_rope_kv_write(runner)
+    normed = torch.zeros(1, 3, 256)
+    out = runner.write_kv_and_project_q(normed, (None, None), 0, "blocks", "within")
+    assert out == "reference" and len(calls) == 1
+    assert calls[0][0] is normed and calls[0][2:] == (0, "blocks", "within")
