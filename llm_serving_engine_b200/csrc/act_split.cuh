@@ -31,6 +31,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "rms_norm.cuh"
 
 namespace lse {
 namespace split {
@@ -190,19 +191,12 @@ act_split_kernel(const XT *__restrict__ x, int64_t ldx, int K, int Kp, int8_t *_
 }
 
 // RMSNorm fused in front of the split (bf16): the digit planes and row scale of
-//   x_n[m, :] = bf16( x[m, :] * rsqrt(mean(x[m, :]^2) + eps) * w[:] )
+//   x_n[m, :] = bf16( w[:] * bf16( x[m, :] * rsqrt(mean(x[m, :]^2) + eps) ) )
 // without writing x_n.  The sum of squares is accumulated in rms_norm_kernel's order (thread t
 // takes the 8-element chunks t, t + THREADS, ...; shuffle tree; the warps' sums in order) and
-// x_n is the same fp32 expression rounded once, so the planes equal act_split_kernel's planes
+// x_n is the same expression with the same roundings, so the planes equal act_split_kernel's planes
 // of rms_norm_kernel's output bit for bit.  A row of up to THREADS * CPT * 8 elements stays in
 // registers; a longer one is read again per pass.
-__device__ __forceinline__ uint32_t rms_scaled_pair(uint32_t u, uint32_t g, float r) {
-    const float a = __uint_as_float(u << 16) * r * __uint_as_float(g << 16);
-    const float b = __uint_as_float(u & 0xffff0000u) * r * __uint_as_float(g & 0xffff0000u);
-    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&p);
-}
-
 template <int S>
 __global__ void __launch_bounds__(THREADS)
 rms_norm_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, const __nv_bfloat16 *__restrict__ w,
@@ -258,8 +252,8 @@ rms_norm_split_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx, const __
             const int c = base + threadIdx.x + i * THREADS;
             if (c < nk) {
                 const uint4 g = __ldg(reinterpret_cast<const uint4 *>(w) + c);
-                v[i] = make_uint4(rms_scaled_pair(v[i].x, g.x, r), rms_scaled_pair(v[i].y, g.y, r),
-                                  rms_scaled_pair(v[i].z, g.z, r), rms_scaled_pair(v[i].w, g.w, r));
+                v[i] = make_uint4(norm::rms_scale_pair(v[i].x, g.x, r), norm::rms_scale_pair(v[i].y, g.y, r),
+                                  norm::rms_scale_pair(v[i].z, g.z, r), norm::rms_scale_pair(v[i].w, g.w, r));
             }
         }
     };

@@ -1,11 +1,11 @@
 // RMSNorm of bf16 rows (transformers' LlamaRMSNorm, reached at model_runner.py:213-224 through
 // every decoder layer's input_layernorm / post_attention_layernorm and the final norm):
 //
-//   y[m, :] = bf16( x[m, :] * rsqrt(mean(x[m, :]^2) + eps) * w[:] )     (fp32 arithmetic)
+//   y[m, :] = bf16( w[:] * bf16( x[m, :] * rsqrt(mean(x[m, :]^2) + eps) ) )   (fp32 arithmetic)
 //
 // One CTA per row: 16-byte loads, the sum of squares reduced through warp shuffles and a
-// small shared buffer, one bf16 rounding (transformers rounds the normalised row to the
-// input dtype before the weight multiply; the difference is within one bf16 ulp).
+// small shared buffer; like transformers, the normalised row is rounded to bf16 before the
+// weight multiply, whose product is rounded again.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -15,6 +15,16 @@ namespace lse {
 namespace norm {
 
 constexpr int THREADS = 256;
+
+// Two bf16 elements (a 32-bit word) of a row with 1 / rms `r` and their two weights:
+// bf16(w * bf16(x * r)) each, transformers' LlamaRMSNorm rounding.
+__device__ __forceinline__ uint32_t rms_scale_pair(uint32_t u, uint32_t g, float r) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(__uint_as_float(u << 16) * r, __uint_as_float(u & 0xffff0000u) * r);
+    const uint32_t tb = *reinterpret_cast<const uint32_t *>(&t);
+    const __nv_bfloat162 p = __floats2bfloat162_rn(__uint_as_float(tb << 16) * __uint_as_float(g << 16),
+                                                   __uint_as_float(tb & 0xffff0000u) * __uint_as_float(g & 0xffff0000u));
+    return *reinterpret_cast<const uint32_t *>(&p);
+}
 
 __global__ void __launch_bounds__(THREADS) rms_norm_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ldx,
                                                            const __nv_bfloat16 *__restrict__ w, int N, float eps,
@@ -51,10 +61,7 @@ __global__ void __launch_bounds__(THREADS) rms_norm_kernel(const __nv_bfloat16 *
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float a = __uint_as_float(u[j] << 16) * r * __uint_as_float(gw[j] << 16);
-            const float b = __uint_as_float(u[j] & 0xffff0000u) * r * __uint_as_float(gw[j] & 0xffff0000u);
-            const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-            o[j] = *reinterpret_cast<const uint32_t *>(&p);
+            o[j] = rms_scale_pair(u[j], gw[j], r);
         }
         reinterpret_cast<uint4 *>(yr)[i] = make_uint4(o[0], o[1], o[2], o[3]);
     }

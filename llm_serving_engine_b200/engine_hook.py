@@ -30,7 +30,8 @@ import torch
 from . import ops
 from .int8_linear import quantize_llama_
 
-__all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "install", "uninstall", "installed"]
+__all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "bind_rms_norms", "install", "uninstall",
+           "installed"]
 
 
 def _attend_paged(runner, q, layer_idx, paging):
@@ -77,6 +78,37 @@ def bind_rope_kv_write(runner):
     return runner
 
 
+class _KernelRMSNorm(torch.nn.Module):
+    """A LlamaRMSNorm slot served by the one-launch RMSNorm kernel (`ops.rms_norm`: the same
+    roundings as transformers' module, the fp32 mean in another order) for bf16 CUDA rows;
+    any other input goes to the module it replaced."""
+
+    def __init__(self, original: torch.nn.Module):
+        super().__init__()
+        self.original = original
+        self.weight = original.weight
+        self.eps = float(getattr(original, "variance_epsilon", getattr(original, "eps", 1e-6)))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16:
+            return ops.rms_norm(x, self.weight, self.eps)
+        return self.original(x)
+
+
+def bind_rms_norms(runner):
+    """Serve every decoder layer's `input_layernorm` / `post_attention_layernorm` and the final
+    norm (`model_runner.py:213-224`) with the RMSNorm kernel: one launch each instead of
+    torch's seven.  Idempotent."""
+    def wrap(module):
+        return module if isinstance(module, _KernelRMSNorm) else _KernelRMSNorm(module)
+
+    for layer in runner._layers:
+        layer.input_layernorm = wrap(layer.input_layernorm)
+        layer.post_attention_layernorm = wrap(layer.post_attention_layernorm)
+    runner.model.model.norm = wrap(runner.model.model.norm)
+    return runner
+
+
 def bind_paged_attention(runner):
     """Route the runner's paged attention to `ops.paged_attention` (an instance attribute, so
     the runner's own `paged_attention` and the graph runners call it)."""
@@ -84,13 +116,14 @@ def bind_paged_attention(runner):
     return runner
 
 
-def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: bool = True):
+def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: bool = True, norms: bool = True):
     """Swap a loaded `ModelRunner`'s projections to int8 in place.  `runner.model` is the
     Llama-family model the runner loaded; every decoder layer's q/k/v (one fused int8 QKV),
     o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`;
     with `attention=True` the paged attention runs on this package's kernel too, and with
     `rope=True` the K/V write and q (`write_kv_and_project_q`) on the fused QKV projection and
-    the RoPE + K/V write kernel.  Nothing else needs preparing: the ops hold no per-stream
+    the RoPE + K/V write kernel, and with `norms=True` the RMSNorms on the RMSNorm kernel.
+    Nothing else needs preparing: the ops hold no per-stream
     state, so the engine's graph captures on any stream record them as they are."""
     device = torch.device(runner.device)
     if device.type != "cuda":
@@ -100,6 +133,8 @@ def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: boo
         bind_paged_attention(runner)
     if rope:
         bind_rope_kv_write(runner)
+    if norms:
+        bind_rms_norms(runner)
     return runner
 
 
@@ -120,7 +155,7 @@ def installed() -> bool:
     return getattr(_runner_class().__init__, "_lse_int8", False)
 
 
-def install(lm_head: bool = False, rope: bool = True) -> None:
+def install(lm_head: bool = False, rope: bool = True, norms: bool = True) -> None:
     """Make `ModelRunner(ModelConfig(quantize="int8"))` load an int8 model (idempotent; the
     options of the first call stay until `uninstall`)."""
     cls = _runner_class()
@@ -135,7 +170,7 @@ def install(lm_head: bool = False, rope: bool = True) -> None:
         _check_cuda(config)
         original(self, dataclasses.replace(config, quantize="none"), *args, **kwargs)
         self.config = config
-        enable_int8(self, lm_head=lm_head, rope=rope)
+        enable_int8(self, lm_head=lm_head, rope=rope, norms=norms)
 
     __init__._lse_int8 = True
     __init__._lse_original = original

@@ -74,3 +74,22 @@ def test_rope_binding_defers_to_the_reference_without_a_fused_int8_qkv(tiny_dir)
     out = runner.write_kv_and_project_q(normed, (None, None), 0, "blocks", "within")
     assert out == "reference" and len(calls) == 1
     assert calls[0][0] is normed and calls[0][2:] == (0, "blocks", "within")
+
+
+def test_norm_binding_wraps_every_norm_once_and_defers_on_cpu(tiny_dir):
+    """`bind_rms_norms` puts the kernel-served module in every RMSNorm slot (idempotently);
+    rows it cannot serve (here fp32 on the CPU) go to the module it replaced, unchanged."""
+    import torch
+
+    runner = ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cpu", dtype="float32",
+                                     use_custom_kernels=False))
+    layer = runner.model.model.layers[0]
+    x = torch.randn(1, 3, 256)
+    before = layer.input_layernorm(x)
+    engine_hook.bind_rms_norms(runner)
+    engine_hook.bind_rms_norms(runner)
+    assert type(layer.input_layernorm).__name__ == "_KernelRMSNorm"
+    assert type(layer.input_layernorm.original).__name__ == "LlamaRMSNorm"
+    assert type(runner.model.model.norm).__name__ == "_KernelRMSNorm"
+    assert all(type(lay.post_attention_layernorm).__name__ == "_KernelRMSNorm" for lay in runner.model.model.layers)
+    assert torch.equal(layer.input_layernorm(x), before)

@@ -159,6 +159,16 @@ def test_rms_norm_matches_torch(M, N):
     xf = x.double()
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.double()
     torch.testing.assert_close(y.double(), ref, rtol=8e-3, atol=1e-3)
+    # transformers' own module (the engine's input/post-attention norms), same roundings: only
+    # the fp32 reduction order of the mean differs
+    from transformers.models.llama.modeling_llama import LlamaRMSNorm
+
+    norm = LlamaRMSNorm(N, eps=1e-5).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(w)
+        tf = norm(x)
+    torch.testing.assert_close(y.float(), tf.float(), rtol=2 ** -7, atol=1e-3)
+    assert (y == tf).float().mean().item() > 0.99
 
 
 def test_one_workspace_serves_changing_shapes():

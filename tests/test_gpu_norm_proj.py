@@ -25,7 +25,7 @@ def _norm_ref(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """The normalised rows as the kernels round them (bf16), for the oracle's input."""
     xf = x.float()
     r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + EPS)
-    return (xf * r * w.float()).to(torch.bfloat16)
+    return ((xf * r).to(torch.bfloat16).float() * w.float()).to(torch.bfloat16)
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (5, 1024, 2048), (16, 4096, 4096), (17, 2048, 3072),
