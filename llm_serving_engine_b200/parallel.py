@@ -42,7 +42,8 @@ from .int8_linear import Int8Linear
 LocalLinear = Callable[[torch.Tensor], torch.Tensor]
 LocalFactory = Callable[[torch.Tensor, torch.Tensor], LocalLinear]
 
-__all__ = ["ColumnParallelInt8Linear", "RowParallelInt8Linear", "TensorParallelInt8MLP", "shard_rows",
+__all__ = ["ColumnParallelInt8Linear", "RowParallelInt8Linear", "TensorParallelInt8MLP", "PeerWatch", "PeerLeft",
+           "shard_rows",
            "interleaved_rows", "fused_rows", "gather_columns", "all_reduce_sum"]
 
 
@@ -121,6 +122,53 @@ def all_reduce_sum(y: torch.Tensor, group=None) -> torch.Tensor:
     if world > 1:
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
+
+
+class PeerLeft(RuntimeError):
+    """A peer rank left (or stopped checking in) between steps."""
+
+    def __init__(self, rank: int, why: str):
+        super().__init__(f"rank {rank} {why}")
+        self.rank = rank
+
+
+class PeerWatch:
+    """Failure detection on the host, between steps: before launching a step's collectives a
+    rank checks in under the step number in the process group's key-value store and waits,
+    bounded, until every peer has checked in.  A rank that stops says so (`leave`) before it
+    goes.  A departed peer, or one that does not check in within `timeout_s`, raises `PeerLeft`
+    on every other rank before any of its collectives is launched, so no GPU waits on a
+    collective that cannot complete."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "lse"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    @classmethod
+    def for_default_group(cls, timeout_s: float = 5.0) -> "PeerWatch":
+        from torch.distributed import distributed_c10d as c10d
+
+        return cls(c10d._get_default_store(), dist.get_rank(), dist.get_world_size(), timeout_s)
+
+    def step(self, n: int) -> None:
+        import time
+
+        self.store.set(f"{self.prefix}/alive/{n}/{self.rank}", "1")
+        deadline = time.monotonic() + self.timeout_s
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            while True:
+                if self.store.check([f"{self.prefix}/left/{r}"]):
+                    raise PeerLeft(r, f"left before step {n}")
+                if self.store.check([f"{self.prefix}/alive/{n}/{r}"]):
+                    break
+                if time.monotonic() > deadline:
+                    raise PeerLeft(r, f"did not check in for step {n} within {self.timeout_s} s")
+                time.sleep(0.005)
+
+    def leave(self) -> None:
+        self.store.set(f"{self.prefix}/left/{self.rank}", "1")
 
 
 class ColumnParallelInt8Linear(nn.Module):

@@ -90,3 +90,61 @@ def test_column_split_over_nccl_matches_single_gpu():
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     mp.spawn(_worker, args=(WORLD, _free_port()), nprocs=WORLD, join=True)
+
+
+def _leaving_worker(rank: int, world: int, port: int, out) -> None:
+    """Step 0 over NCCL with every rank; then the last rank leaves with no collective in
+    flight, and the others learn it on the host (PeerWatch) before launching step 1's."""
+    import datetime
+    import time
+
+    from llm_serving_engine_b200.inputs import make_inputs
+    from llm_serving_engine_b200.parallel import ColumnParallelInt8Linear, PeerLeft, PeerWatch
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=datetime.timedelta(seconds=20))
+    try:
+        x, w, s = make_inputs(8, 1024, 2048, seed=3)
+        mod = ColumnParallelInt8Linear.from_quantized(w.to(dev), s.to(dev))
+        watch = PeerWatch.for_default_group(timeout_s=5.0)
+        watch.step(0)
+        y = mod(x.to(dev))
+        torch.cuda.synchronize(dev)  # step 0's gather is complete on this rank
+        if rank == world - 1:
+            watch.leave()
+            out.put((rank, "left"))
+            return
+        t0 = time.time()
+        try:
+            watch.step(1)
+            mod(x.to(dev))
+            out.put((rank, "completed"))
+        except PeerLeft as e:
+            out.put((rank, f"PeerLeft {e.rank} after {time.time() - t0:.2f} s, step 0 {tuple(y.shape)}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rank_leaving_between_steps_is_reported_before_the_next_collective():
+    """The NCCL form of the host-side failure test: no GPU waits on a collective that cannot
+    complete, because the surviving rank raises PeerLeft from the store check before launching
+    it (NVLS off, plain NCCL)."""
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, WORLD, port, out)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = dict(out.get(timeout=180) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    assert results[WORLD - 1] == "left"
+    assert results[0].startswith(f"PeerLeft {WORLD - 1} after"), results

@@ -226,3 +226,56 @@ def test_fused_rows_interleave_the_rank_block_in_8_row_blocks():
         assert sorted(f.tolist()) == sorted(interleaved_rows(I, world, rank).tolist())
     with pytest.raises(ValueError):
         fused_rows(24, 2, 0)  # 12 rows per rank
+
+
+# ---- the same failure detected on the host before any collective (PeerWatch) -----------
+def _watched_worker(rank: int, world: int, port: int, out) -> None:
+    import datetime
+    import time
+
+    from llm_serving_engine_b200.parallel import PeerLeft, PeerWatch
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        q, s = _weights(1, 48, 64)
+        mod = ColumnParallelInt8Linear.from_quantized(q, s, local_factory=oracle_local)
+        watch = PeerWatch.for_default_group(timeout_s=5.0)
+        watch.step(0)
+        y = mod(_x(2, 5, 64))  # step 0: every rank present
+        if rank == world - 1:
+            watch.leave()
+            out.put((rank, "left after step 0"))
+            return
+        t0 = time.time()
+        try:
+            watch.step(1)
+            mod(_x(2, 5, 64))
+            out.put((rank, "completed"))
+        except PeerLeft as e:
+            out.put((rank, f"PeerLeft {e.rank} after {time.time() - t0:.2f} s; step 0 shape {tuple(y.shape)}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_watch_reports_a_departed_rank_before_the_collective(world):
+    """The last rank leaves after a completed step; every other rank learns it from the store at
+    its next check-in and raises PeerLeft at once, long before the process group's 30 s timeout,
+    without launching the step's collective."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_watched_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(out.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    assert results[world - 1] == "left after step 0"
+    for r in range(world - 1):
+        assert results[r].startswith(f"PeerLeft {world - 1} after"), results
+        assert float(results[r].split("after ")[1].split(" s")[0]) < 5.0
