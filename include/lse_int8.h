@@ -99,14 +99,18 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx,
 
 /*
  * Packed weights.  Both kernels stream weights from one packed layout: W is zero padded to
- * Np = 128*ceil(N/128) rows and Kp = 128*ceil(K/128) columns and cut into groups of 8 rows;
- * group g is one contiguous run of 8*Kp bytes made of 512-byte atoms, one per 64 columns,
- * each holding its 8 rows' 64 columns (64 bytes per row) with the 16-byte chunk c of row r
- * stored at chunk position c ^ ((r >> 1) & 3) (the tensor core's 64-byte swizzle):
- *   W[8*g + r][64*a + 16*c + e]  at  g*8*Kp + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e
- * (r < 8, c < 4, e < 16), plain two's-complement bytes.  A 128 x 128 tile is then the tensor
- * core's K-major operand as it stands (16 runs of 1 KB, one bulk-tensor copy), and one 128-bit
- * load per lane gives the decode kernel a warp-MMA operand fragment, without any shuffling.
+ * Np = 128*ceil(N/128) rows and Kp = 128*ceil(K/128) columns and cut into row blocks of 16
+ * rows; row block b is one contiguous run of 16*Kp bytes made of 2 KB blocks, one per 128
+ * columns, each holding the block's two 8-row groups (h) one after the other as two 512-byte
+ * atoms of 64 columns (a); an atom holds its 8 rows' 64 columns (64 bytes per row) with the
+ * 16-byte chunk c of row r stored at chunk position c ^ ((r >> 1) & 3) (the tensor core's
+ * 64-byte swizzle):
+ *   W[16b + 8h + r][128t + 64a + 16c + e]  at
+ *     b*16*Kp + t*2048 + h*1024 + a*512 + r*64 + (c ^ ((r >> 1) & 3))*16 + e
+ * (h, a < 2, r < 8, c < 4, e < 16), plain two's-complement bytes.  A 128 x 128 tile is then
+ * the tensor core's K-major operand as it stands (eight runs of 2 KB, one bulk-tensor copy),
+ * and one 128-bit load per lane gives the decode kernel a warp-MMA operand fragment, without
+ * any shuffling.
  * The repack happens once, at load (the build's counterpart of the reference loading
  * nn.Linear weights at model_runner.py:50-53); lse_int8_linear_packed then has the same
  * contract as lse_int8_linear_ex with `w_packed` in place of the row-major W.  Its auto
@@ -239,6 +243,11 @@ int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, i
 int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
                       const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
                       void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride, void *stream);
+/* The same with the rows' type given: dtype LSE_BF16 or LSE_F16 for qkv, q_out and the
+ * caches; cs_dtype LSE_F32, LSE_BF16 or LSE_F16 for the cos / sin tables. */
+int lse_rope_kv_write_dt(const void *qkv, int dtype, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
+                         const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out, void *k_dst,
+                         void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride, void *stream);
 
 /*
  * RMSNorm of bf16 rows (transformers' LlamaRMSNorm, every decoder layer's input and
@@ -249,6 +258,9 @@ int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int
  */
 int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
                  int64_t ldy, void *stream);
+/* The same with the rows' type given: dtype LSE_BF16 or LSE_F16 (x, weight and y alike). */
+int lse_rms_norm_dt(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps,
+                    void *y, int64_t ldy, void *stream);
 
 /*
  * RMSNorm fused with the packed projection that consumes it, bf16 activations: the decoder

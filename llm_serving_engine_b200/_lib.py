@@ -65,6 +65,9 @@ SIGNATURES = {
     "lse_int8_rms_norm_gate_up_silu_packed": ([_P, _I64, _I64, _I64, _P, ctypes.c_float, _P, _P, _I64, _P, _I64, _P,
                                                _SZ, _P], _I32),
     "lse_rope_kv_write": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P, _P, _I64, _P], _I32),
+    "lse_rope_kv_write_dt": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P, _P, _I64, _P],
+                             _I32),
+    "lse_rms_norm_dt": ([_P, _I32, _I64, _I64, _I64, _P, ctypes.c_float, _P, _I64, _P], _I32),
     "lse_paged_decode_attention_workspace": ([_I64, _I64, _I64, _I64, _I64, _I64], _SZ),
     "lse_paged_decode_attention": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64,
                                     ctypes.c_float, _P, _I64, _I64, _P, _SZ, _P], _I32),

@@ -1300,15 +1300,51 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
 // lse_rope_kv_write: RoPE on q and k of the fused QKV output, q transposed to
 // (heads, tokens, head_dim), k and v written to their per-token slots (rope_kv.cuh).
 // ---------------------------------------------------------------------------------------
-extern "C" int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
-                                 const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
-                                 void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride,
-                                 void *stream) {
+namespace lse {
+namespace {
+template <typename T>
+int launch_rope(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D, const void *cos,
+                const void *sin, int64_t ld_cs, int cs_dtype, void *q_out, void *k_dst, void *v_dst,
+                const int64_t *kv_offset, int64_t kv_head_stride, int num_sms, cudaStream_t st) {
+    rope::Params<T> p{};
+    p.qkv = static_cast<const T *>(qkv);
+    p.ld_qkv = ld_qkv;
+    p.cos = cos;
+    p.sin = sin;
+    p.ld_cs = ld_cs;
+    p.cs_type = cs_dtype == LSE_BF16 ? 1 : cs_dtype == LSE_F16 ? 2 : 0;
+    p.q_out = static_cast<T *>(q_out);
+    p.k_dst = static_cast<T *>(k_dst);
+    p.v_dst = static_cast<T *>(v_dst);
+    p.kv_off = kv_offset;
+    p.kv_head_stride = kv_head_stride;
+    p.M = static_cast<int>(M);
+    p.H = static_cast<int>(H);
+    p.H_kv = static_cast<int>(H_kv);
+    p.D = static_cast<int>(D);
+    const int64_t total = M * (H + 2 * H_kv) * (D / 2);
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 8LL * num_sms);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    launch_config(cfg, attr, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, rope::rope_kv_kernel<T>, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e, "rope_kv_write launch"); return LSE_ERR_CUDA; }
+    return LSE_OK;
+}
+}  // namespace
+}  // namespace lse
+
+extern "C" int lse_rope_kv_write_dt(const void *qkv, int dtype, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv,
+                                    int64_t D, const void *cos, const void *sin, int64_t ld_cs, int cs_dtype,
+                                    void *q_out, void *k_dst, void *v_dst, const int64_t *kv_offset,
+                                    int64_t kv_head_stride, void *stream) {
     if (M < 0 || H <= 0 || H_kv <= 0 || D <= 0 || (D & 1)) return LSE_ERR_INVALID_ARG;
+    if (dtype != LSE_BF16 && dtype != LSE_F16) return LSE_ERR_UNSUPPORTED;
     if (M == 0) return LSE_OK;
     if (!qkv || !cos || !sin || !q_out || !k_dst || !v_dst || !kv_offset) return LSE_ERR_INVALID_ARG;
     if (ld_qkv < (H + 2 * H_kv) * D || ld_cs < D) return LSE_ERR_INVALID_ARG;
-    if (cs_dtype != LSE_F32 && cs_dtype != LSE_BF16) return LSE_ERR_INVALID_ARG;
+    if (cs_dtype != LSE_F32 && cs_dtype != LSE_BF16 && cs_dtype != LSE_F16) return LSE_ERR_INVALID_ARG;
     if (M > INT32_MAX || (H + 2 * H_kv) * D > INT32_MAX) return LSE_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(qkv) & 1u) || (reinterpret_cast<uintptr_t>(q_out) & 1u) ||
         (reinterpret_cast<uintptr_t>(k_dst) & 1u) || (reinterpret_cast<uintptr_t>(v_dst) & 1u) ||
@@ -1319,39 +1355,29 @@ extern "C" int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
-    rope::Params p{};
-    p.qkv = static_cast<const __nv_bfloat16 *>(qkv);
-    p.ld_qkv = ld_qkv;
-    p.cos = cos;
-    p.sin = sin;
-    p.ld_cs = ld_cs;
-    p.cs_bf16 = cs_dtype == LSE_BF16;
-    p.q_out = static_cast<__nv_bfloat16 *>(q_out);
-    p.k_dst = static_cast<__nv_bfloat16 *>(k_dst);
-    p.v_dst = static_cast<__nv_bfloat16 *>(v_dst);
-    p.kv_off = kv_offset;
-    p.kv_head_stride = kv_head_stride;
-    p.M = static_cast<int>(M);
-    p.H = static_cast<int>(H);
-    p.H_kv = static_cast<int>(H_kv);
-    p.D = static_cast<int>(D);
-    const int64_t total = M * (H + 2 * H_kv) * (D / 2);
-    const int64_t blocks = std::min<int64_t>((total + 255) / 256, 8LL * g_dev[dev].num_sms);
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    launch_config(cfg, attr, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream));
-    cudaError_t e = cudaLaunchKernelEx(&cfg, rope::rope_kv_kernel, p);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) { set_cuda_error(e, "rope_kv_write launch"); return LSE_ERR_CUDA; }
-    return LSE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int cs = cs_dtype;
+    return dtype == LSE_F16 ? launch_rope<__half>(qkv, M, ld_qkv, H, H_kv, D, cos, sin, ld_cs, cs, q_out, k_dst, v_dst,
+                                                  kv_offset, kv_head_stride, g_dev[dev].num_sms, st)
+                            : launch_rope<__nv_bfloat16>(qkv, M, ld_qkv, H, H_kv, D, cos, sin, ld_cs, cs, q_out, k_dst,
+                                                         v_dst, kv_offset, kv_head_stride, g_dev[dev].num_sms, st);
+}
+
+extern "C" int lse_rope_kv_write(const void *qkv, int64_t M, int64_t ld_qkv, int64_t H, int64_t H_kv, int64_t D,
+                                 const void *cos, const void *sin, int64_t ld_cs, int cs_dtype, void *q_out,
+                                 void *k_dst, void *v_dst, const int64_t *kv_offset, int64_t kv_head_stride,
+                                 void *stream) {
+    return lse_rope_kv_write_dt(qkv, LSE_BF16, M, ld_qkv, H, H_kv, D, cos, sin, ld_cs, cs_dtype, q_out, k_dst, v_dst,
+                                kv_offset, kv_head_stride, stream);
 }
 
 // ---------------------------------------------------------------------------------------
-// lse_rms_norm: RMSNorm of bf16 rows (rms_norm.cuh).
+// lse_rms_norm(_dt): RMSNorm of bf16 or fp16 rows (rms_norm.cuh).
 // ---------------------------------------------------------------------------------------
-extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
-                            int64_t ldy, void *stream) {
+extern "C" int lse_rms_norm_dt(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, const void *weight,
+                               float eps, void *y, int64_t ldy, void *stream) {
     if (M < 0 || N <= 0 || ldx < N || ldy < N || !(eps >= 0.f)) return LSE_ERR_INVALID_ARG;
+    if (dtype != LSE_BF16 && dtype != LSE_F16) return LSE_ERR_UNSUPPORTED;
     if (M == 0) return LSE_OK;
     if (!x || !weight || !y) return LSE_ERR_INVALID_ARG;
     if (M > INT32_MAX || N > INT32_MAX) return LSE_ERR_UNSUPPORTED;
@@ -1363,12 +1389,21 @@ extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, co
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     launch_config(cfg, attr, dim3(static_cast<unsigned>(M)), dim3(norm::THREADS), 0, static_cast<cudaStream_t>(stream));
-    cudaError_t e = cudaLaunchKernelEx(&cfg, norm::rms_norm_kernel, static_cast<const __nv_bfloat16 *>(x), ldx,
-                                       static_cast<const __nv_bfloat16 *>(weight), static_cast<int>(N), eps,
-                                       static_cast<__nv_bfloat16 *>(y), ldy);
+    cudaError_t e =
+        dtype == LSE_F16
+            ? cudaLaunchKernelEx(&cfg, norm::rms_norm_kernel<__half>, static_cast<const __half *>(x), ldx,
+                                 static_cast<const __half *>(weight), static_cast<int>(N), eps, static_cast<__half *>(y), ldy)
+            : cudaLaunchKernelEx(&cfg, norm::rms_norm_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16 *>(x), ldx,
+                                 static_cast<const __nv_bfloat16 *>(weight), static_cast<int>(N), eps,
+                                 static_cast<__nv_bfloat16 *>(y), ldy);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { set_cuda_error(e, "rms_norm launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
+}
+
+extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, const void *weight, float eps, void *y,
+                            int64_t ldy, void *stream) {
+    return lse_rms_norm_dt(x, LSE_BF16, M, N, ldx, weight, eps, y, ldy, stream);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -54,11 +54,11 @@ def _write_kv_and_project_q(runner, original, normed, position_embeddings, layer
     """`ModelRunner.write_kv_and_project_q` (`model_runner.py:342-355`) as two launches: the
     layer's fused int8 QKV projection, then one kernel that rotates q and k (rotate-half RoPE
     in fp32, one rounding), writes k and v into their pool slots and returns q as (heads,
-    tokens, head_dim).  Layers without a fused int8 QKV, and dtypes other than bf16, take the
-    reference's own code."""
+    tokens, head_dim).  Layers without a fused int8 QKV, and dtypes other than bf16 and fp16,
+    take the reference's own code."""
     attn = runner._layers[layer_idx].self_attn
     qkv_mod = getattr(attn, "qkv_int8", None)
-    if qkv_mod is None or normed.dtype != torch.bfloat16:
+    if qkv_mod is None or normed.dtype not in (torch.bfloat16, torch.float16):
         return original(normed, position_embeddings, layer_idx, dest_block_id, dest_within)
     cos, sin = position_embeddings
     T = normed.shape[1]
@@ -80,7 +80,8 @@ def bind_rope_kv_write(runner):
 
 class _KernelRMSNorm(torch.nn.Module):
     """A LlamaRMSNorm slot served by the one-launch RMSNorm kernel (`ops.rms_norm`: the same
-    roundings as transformers' module, the fp32 mean in another order) for bf16 CUDA rows;
+    roundings as transformers' module, the fp32 mean in another order) for bf16 and fp16 CUDA
+    rows;
     any other input goes to the module it replaced."""
 
     def __init__(self, original: torch.nn.Module):
@@ -90,7 +91,7 @@ class _KernelRMSNorm(torch.nn.Module):
         self.eps = float(getattr(original, "variance_epsilon", getattr(original, "eps", 1e-6)))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16:
+        if x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and self.weight.dtype == x.dtype:
             return ops.rms_norm(x, self.weight, self.eps)
         return self.original(x)
 

@@ -289,10 +289,10 @@ def quantize_per_channel(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """transformers' LlamaRMSNorm on bf16 rows in one kernel: x [..., N] bf16 (last dim
-    contiguous), weight bf16 [N]; fp32 arithmetic, one bf16 rounding."""
-    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or not (x.is_cuda and weight.is_cuda):
-        raise ValueError("rms_norm: x and weight must be bf16 CUDA tensors")
+    """transformers' LlamaRMSNorm on bf16 or fp16 rows in one kernel: x [..., N] (last dim
+    contiguous), weight [N] of x's dtype; fp32 arithmetic with the module's two roundings."""
+    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype or not (x.is_cuda and weight.is_cuda):
+        raise ValueError("rms_norm: x and weight must be bf16 or fp16 CUDA tensors of one dtype")
     N = x.shape[-1]
     if weight.shape != (N,) or not weight.is_contiguous():
         raise ValueError(f"rms_norm: weight must be contiguous [{N}]")
@@ -300,16 +300,17 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tenso
     if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
         x2 = x2.contiguous()
     if out is None:
-        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
-    elif out.dtype != torch.bfloat16 or out.shape != x.shape or not out.is_contiguous():
-        raise ValueError("rms_norm: out must be a contiguous bf16 tensor of x's shape")
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    elif out.dtype != x.dtype or out.shape != x.shape or not out.is_contiguous():
+        raise ValueError("rms_norm: out must be a contiguous tensor of x's shape and dtype")
     y2 = out.view(-1, N)
     if x2.shape[0] == 0:
         return out
     _ensure_device(x.device)
-    rc = _lib.load().lse_rms_norm(x2.data_ptr(), x2.shape[0], N, x2.stride(0), weight.data_ptr(), float(eps),
-                                  y2.data_ptr(), y2.stride(0), torch.cuda.current_stream(x.device).cuda_stream)
-    _lib.check(rc, "lse_rms_norm")
+    rc = _lib.load().lse_rms_norm_dt(x2.data_ptr(), _DTYPE_CODES[x.dtype], x2.shape[0], N, x2.stride(0),
+                                     weight.data_ptr(), float(eps), y2.data_ptr(), y2.stride(0),
+                                     torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(rc, "lse_rms_norm_dt")
     return out
 
 
@@ -363,38 +364,42 @@ def rope_kv_write(qkv: torch.Tensor, n_heads: int, n_kv_heads: int, head_dim: in
     """RoPE on q and k of the fused QKV output, k and v written to their slots, q returned as
     (n_heads, tokens, head_dim) - `write_kv_and_project_q` after the projection, in one launch.
 
-    qkv: bf16 [M, (H + 2 H_kv) * D] (last dim contiguous); cos / sin: [M, D] fp32 or bf16
-    (transformers' per-token rotary embedding, duplicated halves); k_dst / v_dst: bf16 caches
+    qkv: bf16 or fp16 [M, (H + 2 H_kv) * D] (last dim contiguous); cos / sin: [M, D] fp32, bf16
+    or fp16 (transformers' per-token rotary embedding, duplicated halves); k_dst / v_dst: caches
+    of qkv's dtype
     (e.g. the [num_blocks, block_size, H_kv, D] pools); kv_offset: int64 [M] element offsets
     of each token's slot for KV head 0 (`pool_slot_offsets`), KV heads kv_head_stride apart
     (default head_dim).
     """
     M = qkv.shape[0]
     D = head_dim
-    if qkv.dtype != torch.bfloat16 or qkv.dim() != 2 or qkv.stride(-1) != 1 or qkv.shape[1] != (n_heads + 2 * n_kv_heads) * D:
-        raise ValueError("rope_kv_write: qkv must be bf16 [M, (H + 2 H_kv) * D] with a contiguous last dim")
+    dt = qkv.dtype
+    if dt not in (torch.bfloat16, torch.float16) or qkv.dim() != 2 or qkv.stride(-1) != 1 \
+            or qkv.shape[1] != (n_heads + 2 * n_kv_heads) * D:
+        raise ValueError("rope_kv_write: qkv must be bf16 or fp16 [M, (H + 2 H_kv) * D] with a contiguous last dim")
     if cos.shape != (M, D) or sin.shape != (M, D) or cos.dtype != sin.dtype or cos.stride() != sin.stride() \
-            or cos.stride(-1) != 1 or cos.dtype not in (torch.float32, torch.bfloat16):
-        raise ValueError("rope_kv_write: cos / sin must be [M, D] fp32 or bf16 with equal, row-contiguous strides")
-    if k_dst.dtype != torch.bfloat16 or v_dst.dtype != torch.bfloat16 or not (k_dst.is_contiguous() and v_dst.is_contiguous()):
-        raise ValueError("rope_kv_write: k_dst / v_dst must be contiguous bf16")
+            or cos.stride(-1) != 1 or cos.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise ValueError("rope_kv_write: cos / sin must be [M, D] fp32, bf16 or fp16 with equal, row-contiguous strides")
+    if k_dst.dtype != dt or v_dst.dtype != dt or not (k_dst.is_contiguous() and v_dst.is_contiguous()):
+        raise ValueError("rope_kv_write: k_dst / v_dst must be contiguous, of qkv's dtype")
     if kv_offset.dtype != torch.int64 or kv_offset.shape != (M,) or not kv_offset.is_contiguous():
         raise ValueError("rope_kv_write: kv_offset must be int64 [M]")
     if not all(t.is_cuda and t.device == qkv.device for t in (cos, sin, k_dst, v_dst, kv_offset)):
         raise RuntimeError("rope_kv_write runs on CUDA only, all tensors on qkv's device")
     if q_out is None:
-        q_out = torch.empty((n_heads, M, D), dtype=torch.bfloat16, device=qkv.device)
-    elif q_out.dtype != torch.bfloat16 or q_out.shape != (n_heads, M, D) or not q_out.is_contiguous():
-        raise ValueError("rope_kv_write: q_out must be contiguous bf16 [H, M, D]")
+        q_out = torch.empty((n_heads, M, D), dtype=dt, device=qkv.device)
+    elif q_out.dtype != dt or q_out.shape != (n_heads, M, D) or not q_out.is_contiguous():
+        raise ValueError("rope_kv_write: q_out must be contiguous [H, M, D] of qkv's dtype")
     if M == 0:
         return q_out
     _ensure_device(qkv.device)
-    cs = _lib.DT_F32 if cos.dtype == torch.float32 else _lib.DT_BF16
-    rc = _lib.load().lse_rope_kv_write(
-        qkv.data_ptr(), M, qkv.stride(0), n_heads, n_kv_heads, D, cos.data_ptr(), sin.data_ptr(), cos.stride(0), cs,
+    cs = _DTYPE_CODES[cos.dtype]
+    rc = _lib.load().lse_rope_kv_write_dt(
+        qkv.data_ptr(), _DTYPE_CODES[dt], M, qkv.stride(0), n_heads, n_kv_heads, D, cos.data_ptr(), sin.data_ptr(),
+        cos.stride(0), cs,
         q_out.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), kv_offset.data_ptr(),
         D if kv_head_stride is None else int(kv_head_stride), torch.cuda.current_stream(qkv.device).cuda_stream)
-    _lib.check(rc, "lse_rope_kv_write")
+    _lib.check(rc, "lse_rope_kv_write_dt")
     return q_out
 
 

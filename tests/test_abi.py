@@ -139,11 +139,14 @@ def test_attention_rope_norm_host_validation():
                                           128, None, 0, None) == _lib.LSE_ERR_ALIGNMENT
     assert lib.lse_paged_decode_attention(P, 0, 8, 128, 1024, 128, P, P, 10, 16, 8, P, 4, P, 64, 0.1, P, 1024, 128,
                                           None, 0, None) == _lib.LSE_OK  # no sequences: nothing to do
-    # odd head_dim; cos/sin dtype code outside {F32, BF16}
+    # odd head_dim; cos/sin dtype code outside {F32, BF16, F16}; rows of another type
     assert lib.lse_rope_kv_write(P, 4, 1000, 8, 2, 63, P, P, 63, _lib.DT_F32, P, P, P, P, 63, None) == \
         _lib.LSE_ERR_INVALID_ARG
-    assert lib.lse_rope_kv_write(P, 4, 1536, 8, 2, 128, P, P, 128, _lib.DT_F16, P, P, P, P, 128, None) == \
+    assert lib.lse_rope_kv_write(P, 4, 1536, 8, 2, 128, P, P, 128, 7, P, P, P, P, 128, None) == \
         _lib.LSE_ERR_INVALID_ARG
+    assert lib.lse_rope_kv_write_dt(P, _lib.DT_F32, 4, 1536, 8, 2, 128, P, P, 128, _lib.DT_F32, P, P, P, P, 128,
+                                    None) == _lib.LSE_ERR_UNSUPPORTED
+    assert lib.lse_rms_norm_dt(P, _lib.DT_F32, 4, 64, 64, P, 1e-5, P, 64, None) == _lib.LSE_ERR_UNSUPPORTED
     # RMSNorm: N % 8, ld < N, negative eps
     assert lib.lse_rms_norm(P, 4, 12, 16, P, 1e-5, P, 16, None) == _lib.LSE_ERR_ALIGNMENT
     assert lib.lse_rms_norm(P, 4, 64, 32, P, 1e-5, P, 64, None) == _lib.LSE_ERR_INVALID_ARG

@@ -121,24 +121,27 @@ def _rope_ref(x, cos, sin):
     return x * cos[:, None, :] + rot * sin[:, None, :]
 
 
-@pytest.mark.parametrize("M,H,H_kv,D,cs_dtype", [(1, 32, 8, 128, torch.float32), (7, 32, 8, 128, torch.bfloat16),
-                                                 (64, 8, 2, 64, torch.float32), (130, 4, 4, 128, torch.bfloat16)])
-def test_rope_kv_write_matches_torch(M, H, H_kv, D, cs_dtype):
+@pytest.mark.parametrize("M,H,H_kv,D,cs_dtype,dtype", [
+    (1, 32, 8, 128, torch.float32, torch.bfloat16), (7, 32, 8, 128, torch.bfloat16, torch.bfloat16),
+    (64, 8, 2, 64, torch.float32, torch.bfloat16), (130, 4, 4, 128, torch.bfloat16, torch.bfloat16),
+    (9, 32, 8, 128, torch.float16, torch.float16), (64, 8, 2, 64, torch.float32, torch.float16)])
+def test_rope_kv_write_matches_torch(M, H, H_kv, D, cs_dtype, dtype):
     g = torch.Generator().manual_seed(M + H)
-    qkv = torch.randn(M, (H + 2 * H_kv) * D, generator=g).to(torch.bfloat16).cuda()
+    qkv = torch.randn(M, (H + 2 * H_kv) * D, generator=g).to(dtype).cuda()
     pos = torch.randint(0, 4096, (M,), generator=g).float()
     inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2).float() / D))
     ang = pos[:, None] * inv[None, :]
     cos = torch.cat([ang.cos(), ang.cos()], -1).to(cs_dtype).cuda()
     sin = torch.cat([ang.sin(), ang.sin()], -1).to(cs_dtype).cuda()
     bs, nb = 16, M + 5
-    k_pool = torch.zeros(nb, bs, H_kv, D, dtype=torch.bfloat16, device="cuda")
+    k_pool = torch.zeros(nb, bs, H_kv, D, dtype=dtype, device="cuda")
     v_pool = torch.zeros_like(k_pool)
     dest_block = torch.randperm(nb, generator=g)[:M].cuda()
     dest_within = torch.randint(0, bs, (M,), generator=g).cuda()
     off = ops.pool_slot_offsets(dest_block, dest_within, k_pool)
     q = ops.rope_kv_write(qkv, H, H_kv, D, cos, sin, k_pool, v_pool, off)
     torch.cuda.synchronize()
+    assert q.dtype == dtype
     x = qkv.float().view(M, H + 2 * H_kv, D)
     qr = _rope_ref(x[:, :H], cos.float(), sin.float())
     kr = _rope_ref(x[:, H:H + H_kv], cos.float(), sin.float())
@@ -150,11 +153,12 @@ def test_rope_kv_write_matches_torch(M, H, H_kv, D, cs_dtype):
     assert torch.all(k_pool[untouched] == 0) and torch.all(v_pool[untouched] == 0)
 
 
-@pytest.mark.parametrize("M,N", [(1, 4096), (64, 4096), (5, 8192), (3, 136)])
-def test_rms_norm_matches_torch(M, N):
+@pytest.mark.parametrize("M,N,dtype", [(1, 4096, torch.bfloat16), (64, 4096, torch.bfloat16), (5, 8192, torch.bfloat16),
+                                       (3, 136, torch.bfloat16), (64, 4096, torch.float16), (7, 1024, torch.float16)])
+def test_rms_norm_matches_torch(M, N, dtype):
     g = torch.Generator().manual_seed(M + N)
-    x = (torch.randn(M, N, generator=g) * 3).to(torch.bfloat16).cuda()
-    w = (torch.rand(N, generator=g) + 0.5).to(torch.bfloat16).cuda()
+    x = (torch.randn(M, N, generator=g) * 3).to(dtype).cuda()
+    w = (torch.rand(N, generator=g) + 0.5).to(dtype).cuda()
     y = ops.rms_norm(x, w, 1e-5)
     xf = x.double()
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.double()
@@ -163,10 +167,11 @@ def test_rms_norm_matches_torch(M, N):
     # the fp32 reduction order of the mean differs
     from transformers.models.llama.modeling_llama import LlamaRMSNorm
 
-    norm = LlamaRMSNorm(N, eps=1e-5).cuda().to(torch.bfloat16)
+    norm = LlamaRMSNorm(N, eps=1e-5).cuda().to(dtype)
     with torch.no_grad():
         norm.weight.copy_(w)
         tf = norm(x)
+    assert y.dtype == dtype
     torch.testing.assert_close(y.float(), tf.float(), rtol=2 ** -7, atol=1e-3)
     assert (y == tf).float().mean().item() > 0.99
 
