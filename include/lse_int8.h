@@ -224,6 +224,13 @@ int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, i
                                const int32_t *context_len, int64_t max_context, float scale, void *o,
                                int64_t o_stride_e, int64_t o_stride_h, void *workspace, size_t workspace_bytes,
                                void *stream);
+/* The same with q, the pools and o of `dtype` (LSE_BF16 or LSE_F16; fp16 MMA for fp16). */
+int lse_paged_decode_attention_dt(const void *q, int dtype, int64_t E, int64_t H, int64_t D, int64_t q_stride_e,
+                                  int64_t q_stride_h, const void *k_pool, const void *v_pool, int64_t num_blocks,
+                                  int64_t block_size, int64_t H_kv, const int32_t *block_table, int64_t bt_stride,
+                                  const int32_t *context_len, int64_t max_context, float scale, void *o,
+                                  int64_t o_stride_e, int64_t o_stride_h, void *workspace, size_t workspace_bytes,
+                                  void *stream);
 
 /*
  * RoPE and K/V write on the fused QKV output (the reference's write_kv_and_project_q,

@@ -71,6 +71,8 @@ SIGNATURES = {
     "lse_paged_decode_attention_workspace": ([_I64, _I64, _I64, _I64, _I64, _I64], _SZ),
     "lse_paged_decode_attention": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64,
                                     ctypes.c_float, _P, _I64, _I64, _P, _SZ, _P], _I32),
+    "lse_paged_decode_attention_dt": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64,
+                                    ctypes.c_float, _P, _I64, _I64, _P, _SZ, _P], _I32),
     "lse_int8_packed_weight_bytes": ([_I64, _I64], _SZ),
     "lse_int8_pack_weight": ([_P, _I64, _I64, _I64, _P, _P], _I32),
     "lse_int8_unpack_weight": ([_P, _I64, _I64, _P, _P], _I32),

@@ -3,7 +3,7 @@
 //   o[e, h, :] = softmax(q[e, h, :] . K[e, 0:ctx, kvh(h), :]^T * scale) V[e, 0:ctx, kvh(h), :]
 //
 // with K/V in the reference engine's shared per-layer pool [num_blocks, block_size, H_KV, D]
-// (bf16, contiguous) and key position p of sequence e in pool block block_table[e, p /
+// (bf16 or fp16, contiguous) and key position p of sequence e in pool block block_table[e, p /
 // block_size], slot p % block_size.  Grouped-query attention: the G = H / H_KV query heads
 // of one KV head share every K/V row read.
 //
@@ -41,18 +41,19 @@ constexpr int MAX_TABLE = 1024;  // block-table entries one CTA stages (chunk / 
 constexpr int STAGES = 3;        // cp.async iterations in flight per warp
 constexpr int MAX_SPLITS = 64;   // position splits per (sequence, KV head) the merge stages
 
-// Dynamic shared memory of one CTA: per warp STAGES x (16 K rows + 16 V rows) of D bf16.
+// Dynamic shared memory of one CTA: per warp STAGES x (16 K rows + 16 V rows) of D 16-bit elements.
 template <int D>
 constexpr int attn_smem_bytes() { return WARPS * STAGES * 2 * 16 * D * 2; }
 
+// q, the pools and o hold bf16 or fp16 elements (the kernel's T).
 struct Params {
-    const __nv_bfloat16 *q;   // [E, H, D], d contiguous
+    const void *q;            // [E, H, D], d contiguous
     int64_t q_stride_e, q_stride_h;
-    const __nv_bfloat16 *k_pool, *v_pool;  // [num_blocks, block_size, H_KV, D] contiguous
+    const void *k_pool, *v_pool;  // [num_blocks, block_size, H_KV, D] contiguous
     const int *block_table;   // [E, >= ceil(ctx / block_size)]
     int64_t bt_stride;
     const int *context_len;   // [E]
-    __nv_bfloat16 *o;         // [E, H, D], d contiguous
+    void *o;                  // [E, H, D], d contiguous
     int64_t o_stride_e, o_stride_h;
     int E, H_kv, block_size, num_blocks, chunk, splits, max_ctx;
     float scale_log2;         // softmax scale * log2(e)
@@ -74,17 +75,30 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
 }
-// D (16x8 fp32) += A (16x16 bf16, row) * B (16x8 bf16, col)
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+// D (16x8 fp32) += A (16x16, row) * B (16x8, col), bf16 or fp16 operands (T)
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    if constexpr (std::is_same_v<T, __half>)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t *>(&v);
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if constexpr (std::is_same_v<T, __half>) {
+        const __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t *>(&v);
+    } else {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t *>(&v);
+    }
 }
 
 // Per warp and iteration, 16 positions: K and V rows staged in shared memory by cp.async
@@ -95,8 +109,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 //   online softmax on the S accumulators (base 2), whose two tiles are exactly the row
 //     operand of P V;
 //   O[head, dims] += P V: V from ldmatrix.trans as the column operand, D/8 dim tiles.
-template <int D, int G>
+template <int D, int G, typename T = __nv_bfloat16>
 __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
+    const T *q_ptr = static_cast<const T *>(p.q);
+    const T *k_ptr = static_cast<const T *>(p.k_pool);
+    const T *v_ptr = static_cast<const T *>(p.v_pool);
+    T *o_ptr = static_cast<T *>(p.o);
     static_assert(D == 64 || D == 128, "head_dim");
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head");
     constexpr int CH = D / 8;           // 16-byte chunks per row
@@ -144,7 +162,7 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
     for (int j = 0; j < D / 16; ++j) {
         qa[j][0] = qa[j][1] = 0u;
         if (r0 < G) {
-            const __nv_bfloat16 *qp = p.q + e * p.q_stride_e + (kvh * G + r0) * p.q_stride_h + 16 * j + 2 * q4;
+            const T *qp = q_ptr + e * p.q_stride_e + (kvh * G + r0) * p.q_stride_h + 16 * j + 2 * q4;
             qa[j][0] = *reinterpret_cast<const uint32_t *>(qp);
             qa[j][1] = *reinterpret_cast<const uint32_t *>(qp + 8);
         }
@@ -172,8 +190,8 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
             const bool ok = g0 < end && slot >= 0;
             const int64_t off = (ok ? slot : 0) * row_elems + kvh * D + c * 8;
             const uint32_t sw = r * ROWB + ((c ^ (r & 7)) << 4);
-            cp_async16_zfill(kdst + sw, p.k_pool + off, ok);
-            cp_async16_zfill(vdst + sw, p.v_pool + off, ok);
+            cp_async16_zfill(kdst + sw, k_ptr + off, ok);
+            cp_async16_zfill(vdst + sw, v_ptr + off, ok);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         return __ballot_sync(0xffffffffu, lane < KEYS && my_slot >= 0);  // bit k: position g0 + k valid
@@ -220,8 +238,8 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
                 ldsm_x4(rowp + ((c ^ (r & 7)) << 4), b);
                 float (&d0)[4] = (j & 1) ? s2[0] : s[0];
                 float (&d1)[4] = (j & 1) ? s2[1] : s[1];
-                mma_bf16_16816(d0, qa[j][0], 0u, qa[j][1], 0u, b[0], b[1]);
-                mma_bf16_16816(d1, qa[j][0], 0u, qa[j][1], 0u, b[2], b[3]);
+                mma_16816<T>(d0, qa[j][0], 0u, qa[j][1], 0u, b[0], b[1]);
+                mma_16816<T>(d1, qa[j][0], 0u, qa[j][1], 0u, b[2], b[3]);
             }
 #pragma unroll
             for (int i = 0; i < 2; ++i)
@@ -253,7 +271,7 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
         l_run = l_run * alpha + ps;
         m_run = m_new;
         // P as the row operand: a0 = row r0 keys 2q4..+1, a2 = row r0 keys 8+2q4..+1
-        const uint32_t pa0 = pack_bf16x2(pv[0], pv[1]), pa2 = pack_bf16x2(pv[2], pv[3]);
+        const uint32_t pa0 = pack2<T>(pv[0], pv[1]), pa2 = pack2<T>(pv[2], pv[3]);
 #pragma unroll
         for (int t = 0; t < NT; t += 2) {
             // matrices: keys 0-7 / dims 8t.., keys 8-15 / 8t.., keys 0-7 / 8t+8.., keys 8-15 / 8t+8..
@@ -264,8 +282,8 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
             acc[t][1] *= alpha;
             acc[t + 1][0] *= alpha;
             acc[t + 1][1] *= alpha;
-            mma_bf16_16816(acc[t], pa0, 0u, pa2, 0u, b[0], b[1]);
-            mma_bf16_16816(acc[t + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
+            mma_16816<T>(acc[t], pa0, 0u, pa2, 0u, b[0], b[1]);
+            mma_16816<T>(acc[t + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
         }
         __syncwarp();  // the stage is free for the copies issued next iteration
         st = st + 1 == STAGES ? 0 : st + 1;
@@ -325,7 +343,7 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
             if (idx >= G * D) continue;
             const int h = idx / D, d = idx % D;
             const float out = res_l[it] > 0.f ? res_a[it] / res_l[it] : 0.f;
-            p.o[e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d] = __float2bfloat16_rn(out);
+            o_ptr[e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d] = from_float<T>(out);
         }
         return;
     }
@@ -425,11 +443,11 @@ __global__ void __launch_bounds__(THREADS) paged_decode_kernel(const Params p) {
         if (f >= F4) continue;
         const int h = (4 * f) / D, d = (4 * f) % D;
         const float L = s_L[h];
-        __nv_bfloat16 *op = p.o + e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d;
-        op[0] = __float2bfloat16_rn(L > 0.f ? A[i].x / L : 0.f);
-        op[1] = __float2bfloat16_rn(L > 0.f ? A[i].y / L : 0.f);
-        op[2] = __float2bfloat16_rn(L > 0.f ? A[i].z / L : 0.f);
-        op[3] = __float2bfloat16_rn(L > 0.f ? A[i].w / L : 0.f);
+        T *op = o_ptr + e * p.o_stride_e + (kvh * G + h) * p.o_stride_h + d;
+        op[0] = from_float<T>(L > 0.f ? A[i].x / L : 0.f);
+        op[1] = from_float<T>(L > 0.f ? A[i].y / L : 0.f);
+        op[2] = from_float<T>(L > 0.f ? A[i].z / L : 0.f);
+        op[3] = from_float<T>(L > 0.f ? A[i].w / L : 0.f);
     }
 }
 

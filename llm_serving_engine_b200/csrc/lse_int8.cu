@@ -1178,10 +1178,10 @@ size_t attn_workspace_bytes(const AttnPlan &pl, int64_t E, int64_t H, int64_t H_
     return kAttnCounterBytes + static_cast<size_t>(E * H_kv) * pl.splits * G * (D + 2) * sizeof(float);
 }
 
-template <int D, int G>
+template <int D, int G, typename T>
 cudaError_t launch_attn(const attn::Params &p, int64_t E, cudaStream_t st) {
     constexpr int smem = attn::attn_smem_bytes<D>();
-    auto kernel = attn::paged_decode_kernel<D, G>;
+    auto kernel = attn::paged_decode_kernel<D, G, T>;
     {  // opt in to the ring's shared memory (with the static part it exceeds 48 KB), once per device
         static std::once_flag once[kMaxDevices];
         static cudaError_t set_err[kMaxDevices];
@@ -1200,6 +1200,28 @@ cudaError_t launch_attn(const attn::Params &p, int64_t E, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+// The kernel instance for head_dim D (64 or 128) and group size G (1, 2, 4, 8).
+template <typename T>
+cudaError_t launch_attn_dg(const attn::Params &p, int64_t D, int64_t G, int64_t E, cudaStream_t st) {
+    cudaError_t e;
+    if (D == 128) {
+        switch (G) {
+            case 1: e = launch_attn<128, 1, T>(p, E, st); break;
+            case 2: e = launch_attn<128, 2, T>(p, E, st); break;
+            case 4: e = launch_attn<128, 4, T>(p, E, st); break;
+            default: e = launch_attn<128, 8, T>(p, E, st); break;
+        }
+    } else {
+        switch (G) {
+            case 1: e = launch_attn<64, 1, T>(p, E, st); break;
+            case 2: e = launch_attn<64, 2, T>(p, E, st); break;
+            case 4: e = launch_attn<64, 4, T>(p, E, st); break;
+            default: e = launch_attn<64, 8, T>(p, E, st); break;
+        }
+    }
+    return e == cudaSuccess ? cudaGetLastError() : e;
+}
+
 }  // namespace
 }  // namespace lse
 
@@ -1211,15 +1233,16 @@ extern "C" size_t lse_paged_decode_attention_workspace(int64_t E, int64_t H, int
     return attn_workspace_bytes(plan_attn(E, H_kv, max_context, block_size, g_dev[dev].num_sms), E, H, H_kv, D);
 }
 
-extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, int64_t q_stride_e,
-                                          int64_t q_stride_h, const void *k_pool, const void *v_pool,
-                                          int64_t num_blocks, int64_t block_size, int64_t H_kv,
-                                          const int32_t *block_table, int64_t bt_stride, const int32_t *context_len,
-                                          int64_t max_context, float scale, void *o, int64_t o_stride_e,
-                                          int64_t o_stride_h, void *workspace, size_t workspace_bytes,
-                                          void *stream) {
+extern "C" int lse_paged_decode_attention_dt(const void *q, int dtype, int64_t E, int64_t H, int64_t D,
+                                             int64_t q_stride_e, int64_t q_stride_h, const void *k_pool,
+                                             const void *v_pool, int64_t num_blocks, int64_t block_size, int64_t H_kv,
+                                             const int32_t *block_table, int64_t bt_stride,
+                                             const int32_t *context_len, int64_t max_context, float scale, void *o,
+                                             int64_t o_stride_e, int64_t o_stride_h, void *workspace,
+                                             size_t workspace_bytes, void *stream) {
     if (E < 0 || H <= 0 || H_kv <= 0 || D <= 0 || num_blocks <= 0 || block_size <= 0 || max_context < 0)
         return LSE_ERR_INVALID_ARG;
+    if (dtype != LSE_BF16 && dtype != LSE_F16) return LSE_ERR_UNSUPPORTED;
     if (E == 0) return LSE_OK;
     if (!q || !k_pool || !v_pool || !block_table || !context_len || !o) return LSE_ERR_INVALID_ARG;
     if (H % H_kv) return LSE_ERR_INVALID_ARG;
@@ -1254,15 +1277,15 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
     const size_t need = attn_workspace_bytes(pl, E, H, H_kv, D);
     if (need && (!workspace || workspace_bytes < need || !aligned16(workspace))) return LSE_ERR_WORKSPACE;
     attn::Params p{};
-    p.q = static_cast<const __nv_bfloat16 *>(q);
+    p.q = q;
     p.q_stride_e = q_stride_e;
     p.q_stride_h = q_stride_h;
-    p.k_pool = static_cast<const __nv_bfloat16 *>(k_pool);
-    p.v_pool = static_cast<const __nv_bfloat16 *>(v_pool);
+    p.k_pool = k_pool;
+    p.v_pool = v_pool;
     p.block_table = block_table;
     p.bt_stride = bt_stride;
     p.context_len = context_len;
-    p.o = static_cast<__nv_bfloat16 *>(o);
+    p.o = o;
     p.o_stride_e = o_stride_e;
     p.o_stride_h = o_stride_h;
     p.E = static_cast<int>(E);
@@ -1275,25 +1298,22 @@ extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, i
     p.scale_log2 = scale * 1.4426950408889634f;  // log2(e): softmax in base 2
     p.counters = static_cast<int *>(workspace);
     p.part = need ? reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kAttnCounterBytes) : nullptr;
-    cudaError_t e;
-    if (D == 128) {
-        switch (G) {
-            case 1: e = launch_attn<128, 1>(p, E, st); break;
-            case 2: e = launch_attn<128, 2>(p, E, st); break;
-            case 4: e = launch_attn<128, 4>(p, E, st); break;
-            default: e = launch_attn<128, 8>(p, E, st); break;
-        }
-    } else {
-        switch (G) {
-            case 1: e = launch_attn<64, 1>(p, E, st); break;
-            case 2: e = launch_attn<64, 2>(p, E, st); break;
-            case 4: e = launch_attn<64, 4>(p, E, st); break;
-            default: e = launch_attn<64, 8>(p, E, st); break;
-        }
-    }
-    if (e == cudaSuccess) e = cudaGetLastError();
+    const cudaError_t e = dtype == LSE_F16 ? launch_attn_dg<__half>(p, D, G, E, st)
+                                           : launch_attn_dg<__nv_bfloat16>(p, D, G, E, st);
     if (e != cudaSuccess) { set_cuda_error(e, "paged_decode_attention launch"); return LSE_ERR_CUDA; }
     return LSE_OK;
+}
+
+extern "C" int lse_paged_decode_attention(const void *q, int64_t E, int64_t H, int64_t D, int64_t q_stride_e,
+                                          int64_t q_stride_h, const void *k_pool, const void *v_pool,
+                                          int64_t num_blocks, int64_t block_size, int64_t H_kv,
+                                          const int32_t *block_table, int64_t bt_stride, const int32_t *context_len,
+                                          int64_t max_context, float scale, void *o, int64_t o_stride_e,
+                                          int64_t o_stride_h, void *workspace, size_t workspace_bytes,
+                                          void *stream) {
+    return lse_paged_decode_attention_dt(q, LSE_BF16, E, H, D, q_stride_e, q_stride_h, k_pool, v_pool, num_blocks,
+                                         block_size, H_kv, block_table, bt_stride, context_len, max_context, scale, o,
+                                         o_stride_e, o_stride_h, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------------------

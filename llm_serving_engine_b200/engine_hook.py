@@ -37,11 +37,11 @@ __all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "bind_rm
 def _attend_paged(runner, q, layer_idx, paging):
     """`ModelRunner.attend_paged` on this package's kernels: same arguments, same result.  A
     batch of single-token entries (every decode step; their rows are the entries in order) in
-    bf16 takes the decode kernel, unsplit (no workspace, so any capture stream records it); any
+    bf16 or fp16 takes the decode kernel, unsplit (no workspace, so any capture stream records it); any
     other batch the multi-token kernel."""
     k_pool, v_pool = runner._k_pool[layer_idx], runner._v_pool[layer_idx]
     E = paging.block_table.shape[0]
-    if paging.max_q_len == 1 and q.shape[1] == E and q.dtype == torch.bfloat16:
+    if paging.max_q_len == 1 and q.shape[1] == E and q.dtype in (torch.bfloat16, torch.float16):
         max_context = paging.block_table.shape[1] * runner._block_size
         o = ops.paged_decode_attention(q.transpose(0, 1), k_pool, v_pool, paging.block_table, paging.context_len,
                                        max_context, split=False)

@@ -427,8 +427,8 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
     """
     if not all(t.is_cuda for t in (q, k_pool, v_pool, block_table, context_len)):
         raise RuntimeError("paged_decode_attention runs on CUDA only (no CPU fallback)")
-    if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or v_pool.dtype != torch.bfloat16:
-        raise ValueError("paged_decode_attention: q and the pools must be bfloat16")
+    if q.dtype not in (torch.bfloat16, torch.float16) or k_pool.dtype != q.dtype or v_pool.dtype != q.dtype:
+        raise ValueError("paged_decode_attention: q and the pools must be bfloat16 or float16, of one dtype")
     if q.dim() != 3 or q.stride(-1) != 1:
         raise ValueError("paged_decode_attention: q must be [E, H, D] with a contiguous last dim")
     if k_pool.shape != v_pool.shape or k_pool.dim() != 4 or not (k_pool.is_contiguous() and v_pool.is_contiguous()):
@@ -441,9 +441,9 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
             or block_table.stride(1) != 1 or context_len.shape != (E,) or block_table.shape[0] != E:
         raise ValueError("paged_decode_attention: block_table int32 [E, n] and context_len int32 [E]")
     if out is None:
-        out = torch.empty((E, H, D), dtype=torch.bfloat16, device=q.device)
-    elif out.dtype != torch.bfloat16 or out.shape != (E, H, D) or out.stride(-1) != 1:
-        raise ValueError("paged_decode_attention: out must be bf16 [E, H, D] with a contiguous last dim")
+        out = torch.empty((E, H, D), dtype=q.dtype, device=q.device)
+    elif out.dtype != q.dtype or out.shape != (E, H, D) or out.stride(-1) != 1:
+        raise ValueError("paged_decode_attention: out must be [E, H, D] of q's dtype with a contiguous last dim")
     if E == 0:
         return out
     _ensure_device(q.device)
@@ -464,11 +464,11 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
                 ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
                 _attn_ws[key] = ws
     scale = 1.0 / float(D) ** 0.5 if scale is None else float(scale)
-    rc = lib.lse_paged_decode_attention(
-        q.data_ptr(), E, H, D, q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), nb, bs, H_kv,
+    rc = lib.lse_paged_decode_attention_dt(
+        q.data_ptr(), _DTYPE_CODES[q.dtype], E, H, D, q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), nb, bs, H_kv,
         block_table.data_ptr(), block_table.stride(0), context_len.data_ptr(), int(max_context), scale,
         out.data_ptr(), out.stride(0), out.stride(1), ws.data_ptr() if need else None, need, stream.cuda_stream)
-    _lib.check(rc, "lse_paged_decode_attention")
+    _lib.check(rc, "lse_paged_decode_attention_dt")
     return out
 
 

@@ -228,3 +228,19 @@ def test_unsplit_launch_with_the_engines_wide_block_table():
                                split=False)
     assert ops.device_status() == _lib.LSE_ERR_UNSUPPORTED
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("E,ctx,split", [(4, [1, 17, 300, 1024], True), (64, list(range(962, 1026)), True),
+                                         (3, [5, 129, 2049], False)])
+def test_paged_decode_attention_fp16(E, ctx, split):
+    """fp16 q and pools (the reference's default dtype) on the fp16 MMA, split and unsplit,
+    against the fp64 oracle on the same (fp16-rounded) inputs."""
+    q, k_pool, v_pool, bt, cl, max_ctx = _case(E, 32, 8, 128, 16, ctx, seed=21 + E)
+    q, k_pool, v_pool = q.half(), k_pool.half(), v_pool.half()
+    o = ops.paged_decode_attention(q.cuda(), k_pool.cuda(), v_pool.cuda(), bt.cuda(), cl.cuda(), max_ctx, split=split)
+    torch.cuda.synchronize()
+    assert o.dtype == torch.float16
+    ref = ref_paged_decode_attention(q.float().numpy(), k_pool.float().numpy(), v_pool.float().numpy(),
+                                     bt.numpy(), cl.numpy())
+    check_parity(o.reshape(E * 32, 128), ref.reshape(E * 32, 128), f"fp16 decode attention E={E}")
+    assert ops.device_status() == 0
