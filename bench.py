@@ -477,7 +477,9 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     `quantize="int8"` switch through `engine_hook.install()` with its defaults: int8
     projections, the same attention and norms, and `write_kv_and_project_q` on the fused int8
     QKV output with the RoPE + K/V write kernel) and `int8_no_rope` (the switch without that
-    last binding: against `bf16_lse` it differs in the projections alone).  The weights are a random-init Llama-3-8B (seeded, built on the
+    last binding: against `bf16_lse` it differs in the projections alone); and in fp16, the
+    reference's default dtype, `fp16_reference` (the stock engine) and `fp16_int8` (the switch
+    with its defaults).  The weights are a random-init Llama-3-8B (seeded, built on the
     GPU in place of `from_pretrained`: no checkpoint exists here); everything after the load is
     the engine's unmodified code."""
     import gc
@@ -520,13 +522,14 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     original_loader = mr.AutoModelForCausalLM
     mr.AutoModelForCausalLM = _SyntheticLoader
     try:
-        for arm in ("bf16_reference", "bf16_lse", "int8_no_rope", "int8"):
-            quantize = "int8" if arm.startswith("int8") else "none"
+        for arm in ("bf16_reference", "bf16_lse", "int8_no_rope", "int8", "fp16_reference", "fp16_int8"):
+            quantize = "int8" if "int8" in arm else "none"
             if quantize == "int8":
-                engine_hook.install(rope=arm == "int8")
+                engine_hook.install(rope=arm != "int8_no_rope")
             try:
                 runner = mr.ModelRunner(ModelConfig(model_name_or_path="synthetic-llama-3-8b", device=str(dev),
-                                                    dtype="bfloat16", quantize=quantize))
+                                                    dtype="float16" if arm.startswith("fp16") else "bfloat16",
+                                                    quantize=quantize))
             finally:
                 engine_hook.uninstall()
             if arm == "bf16_lse":
@@ -587,6 +590,8 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     out["int8_speedup_vs_bf16_lse"] = round(out["int8"]["tokens_per_s"] / out["bf16_lse"]["tokens_per_s"], 3)
     out["int8_no_rope_speedup_vs_bf16_lse"] = round(
         out["int8_no_rope"]["tokens_per_s"] / out["bf16_lse"]["tokens_per_s"], 3)
+    out["fp16_int8_speedup_vs_fp16_reference"] = round(
+        out["fp16_int8"]["tokens_per_s"] / out["fp16_reference"]["tokens_per_s"], 3)
     return out
 
 
