@@ -462,7 +462,7 @@ def e2e_decode(dev, warm, hbm_peak, steps: int = 20):
     return out
 
 
-def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, context: int = 1024):
+def engine_decode(dev, hbm_peak: float, steps: int = 20, warmup: int = 5, batch: int = 64, context: int = 1024):
     """Config 4 through the reference engine itself (its install in baseline/_ref): the
     reference's `ModelRunner` with `use_custom_kernels` and `use_cuda_graphs`, decode graphs
     captured at bucket `batch` (`capture_decode_graphs`, `_self_check` included), a
@@ -500,6 +500,7 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
     from transformers import LlamaConfig, LlamaForCausalLM
 
     from llm_serving_engine_b200 import engine_hook
+    from llm_serving_engine_b200.llama_decode import LLAMA3_8B, decode_bytes_per_step
 
     cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
                       num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=8192,
@@ -578,7 +579,11 @@ def engine_decode(dev, steps: int = 20, warmup: int = 5, batch: int = 64, contex
                 step()
             torch.cuda.synchronize()
             sec = time.perf_counter() - t0
+            # the step's HBM bound (weights, K/V at the mean context of the timed steps, lm_head)
+            byts = decode_bytes_per_step(LLAMA3_8B, batch, context + warmup + steps // 2, quantize == "int8")
             out[arm] = {"tokens_per_s": round(batch * steps / sec, 1), "ms_per_step": round(sec / steps * 1e3, 4),
+                        "bytes_per_step": byts, "GBps": round(byts * steps / sec / 1e9, 1),
+                        "frac_of_hbm": round(byts * steps / sec / 1e9 / hbm_peak, 4),
                         "decode_graph_kept": graphs_kept, "eager_steps_in_timed_region": eager["n"],
                         "context_at_end": seqs[0].num_tokens}
             del runner, seqs, by_id, alloc
@@ -1029,7 +1034,7 @@ def main():
     tp70b = None if args.no_70b else tp70b_sweep(world, rank, dev, ops, warm)
     mlp70b = None if args.no_70b else mlp70b_tp(world, rank, dev, ops, warm)
     decode4 = e2e_decode(dev, warm, hbm_peak) if (world == 1 and not args.no_e2e_decode) else None
-    engine4 = engine_decode(dev) if (world == 1 and not args.no_engine_decode) else None
+    engine4 = engine_decode(dev, hbm_peak) if (world == 1 and not args.no_engine_decode) else None
 
     # ---- e2e: pinned host activations in, graph replay, outputs back, every step -------
     host_x = {k: v.cpu().pin_memory() for k, v in xs.items()}
