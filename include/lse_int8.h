@@ -114,7 +114,9 @@ int lse_int8_linear_ex(const void *x, int64_t M, int64_t K, int64_t ldx,
  * The repack happens once, at load (the build's counterpart of the reference loading
  * nn.Linear weights at model_runner.py:50-53); lse_int8_linear_packed then has the same
  * contract as lse_int8_linear_ex with `w_packed` in place of the row-major W.  Its auto
- * choice is LSE_ALGO_SKINNY for M <= 16 (decode) and LSE_ALGO_TCGEN05 above.
+ * choice is LSE_ALGO_SKINNY for M <= 16 (decode), and for M <= 32 when N * K <= 32 MiB (where
+ * the tensor-core kernel's fixed cost per launch outweighs its faster weight stream), and
+ * LSE_ALGO_TCGEN05 otherwise.
  */
 size_t lse_int8_packed_weight_bytes(int64_t N, int64_t K);
 int lse_int8_pack_weight(const int8_t *w, int64_t N, int64_t K, int64_t ldw, int8_t *w_packed, void *stream);
@@ -276,12 +278,13 @@ int lse_rms_norm_dt(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx,
  *   lse_int8_rms_norm_linear_packed:       y = lse_int8_linear_packed(rms_norm(x, norm_weight, eps))
  *   lse_int8_rms_norm_gate_up_silu_packed: y = lse_int8_gate_up_silu_packed_ws(rms_norm(x, ...))
  * with rms_norm as lse_rms_norm (K = the normalised width), and the same results bit for bit
- * as those two calls in sequence.  Above 16 tokens the normalisation writes the tensor-core
- * kernel's activation digit planes directly (no normalised copy of x, one launch fewer); up to
- * 16 tokens the normalised rows pass through the workspace to the decode kernel.
+ * as those two calls in sequence.  Where the projection alone takes the tensor-core kernel
+ * (the entries' automatic choice) the normalisation writes its activation digit planes
+ * directly (no normalised copy of x, one launch fewer); where it takes the decode kernel the
+ * normalised rows pass through the workspace to it.
  *   norm_weight  bf16 [K], 16-byte aligned; eps >= 0
- *   workspace    >= lse_int8_rms_norm_proj_workspace(M, K) bytes (the same N-independent
- *                bound as lse_int8_linear_workspace above 16 tokens, M * K * 2 bytes up to 16),
+ *   workspace    >= lse_int8_rms_norm_proj_workspace(M, K) bytes (N-independent: M * K * 2
+ *                bytes up to 16 tokens, at least lse_int8_linear_workspace's bound above),
  *                16-byte aligned, contents irrelevant
  * Other arguments and status codes as the unfused entries.
  */

@@ -596,10 +596,18 @@ int run_skinny(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *w
 
 // Auto policy.  Row-major W: the CUDA-core GEMV while its FMA work stays under the HBM
 // stream (M <= 2), the tensor-core kernel from there on.  Packed W: the warp-MMA skinny
-// kernel while the weight stream, not MMA issue, is the bound (M <= 16), the tcgen05
-// kernel from there on.
-int auto_algo(int64_t M, bool packed) {
-    if (packed) return M <= 16 ? LSE_ALGO_SKINNY : LSE_ALGO_TCGEN05;
+// kernel while the weight stream, not MMA issue, is the bound (M <= 16); from 17 to 32 tokens
+// still the skinny kernel for a weight of at most kSkinnySmallWeight bytes, where the
+// tensor-core kernel's fixed cost per launch (the split launch in front of it, the first stage,
+// the cluster reduction) outweighs its faster stream; the tcgen05 kernel otherwise.  Measured
+// on B200 (32 layers' weights per CUDA graph, us per launch, skinny against tcgen05) at
+// M = 17 / 32: QKV 4096 x 6144 11.7 / 12.4 against 13.2 / 13.6, O 4096 x 4096 7.3 / 8.4
+// against 10.7 / 11.2, down 14336 x 4096 20.8 / 23.1 against 17.3 / 19.4, gate_up
+// 4096 x 28672 37.3 / 41.3 against 28.8 / 30.1: the two lines cross near 32 MB.
+constexpr int64_t kSkinnySmallWeight = int64_t(32) << 20;
+int auto_algo(int64_t M, int64_t K, int64_t N, bool packed) {
+    if (packed)
+        return (M <= 16 || (M <= kSkinnyMaxM && N * K <= kSkinnySmallWeight)) ? LSE_ALGO_SKINNY : LSE_ALGO_TCGEN05;
     return M <= 2 ? LSE_ALGO_GEMV : LSE_ALGO_TCGEN05;
 }
 
@@ -636,7 +644,7 @@ size_t lse_int8_linear_workspace(int64_t M, int64_t K, int64_t N) {
 }
 
 size_t lse_int8_linear_workspace_for(int64_t M, int64_t K, int64_t N, int algo, int packed) {
-    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed != 0);
+    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, K, N, packed != 0);
     if (algo != LSE_ALGO_TCGEN05) return 0;
     return lse_int8_linear_workspace(M, K, N);
 }
@@ -676,7 +684,7 @@ int linear_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const int8_t *
         if (e != cudaSuccess) { set_cuda_error(e, "K == 0 output"); return LSE_ERR_CUDA; }
         return LSE_OK;
     }
-    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, packed);
+    if (algo == LSE_ALGO_AUTO) algo = auto_algo(M, K, N, packed);
     if (xf16 && !packed) return LSE_ERR_UNSUPPORTED;  // fp16 activations: packed weights only
     if (algo == LSE_ALGO_GEMV) return run_gemv(x, M, K, ldx, w, scale, N, y, ldy, st);  // row-major: no res
     if (algo == LSE_ALGO_SKINNY)
@@ -1428,17 +1436,20 @@ extern "C" int lse_rms_norm(const void *x, int64_t M, int64_t N, int64_t ldx, co
 
 // ---------------------------------------------------------------------------------------
 // RMSNorm fused with the projection that consumes it (bf16): the decoder layer's
-// q/k/v(input_layernorm(h)) and mlp.gate_up(post_attention_layernorm(h)).  Up to 16 tokens
-// the normalised rows go through the workspace to the decode kernel; above, the digit planes
-// are written straight from the normalisation (split::rms_norm_split_kernel) and the separate
-// split launch disappears.
+// q/k/v(input_layernorm(h)) and mlp.gate_up(post_attention_layernorm(h)).  Wherever the
+// projection alone would take the decode kernel (lse_int8_linear_packed's and
+// lse_int8_gate_up_silu_packed's automatic choice) the normalised rows go through the
+// workspace to it; otherwise the digit planes are written straight from the normalisation
+// (split::rms_norm_split_kernel) and the separate split launch disappears.
 // ---------------------------------------------------------------------------------------
 namespace lse {
 namespace {
 size_t norm_proj_workspace(int64_t M, int64_t K) {
     if (M <= 0 || K < 0) return 0;
-    if (M <= 16) return (static_cast<size_t>(M) * K * 2 + 15) / 16 * 16;
-    return tci8_workspace_bytes(token_tile(M), digit_planes(M), kMaxGridForWorkspace, M, K);
+    const size_t rows = (static_cast<size_t>(M) * K * 2 + 15) / 16 * 16;  // the normalised rows
+    if (M <= 16) return rows;
+    // 17..32 tokens take either route, by the weight's size
+    return std::max(rows, tci8_workspace_bytes(token_tile(M), digit_planes(M), kMaxGridForWorkspace, M, K));
 }
 
 int norm_proj_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const void *norm_w, float eps,
@@ -1458,7 +1469,7 @@ int norm_proj_impl(const void *x, int64_t M, int64_t K, int64_t ldx, const void 
     int rc = current_device(&dev);
     if (rc) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (M <= 16) {
+    if (M <= 16 || (!silu && auto_algo(M, K, N, true) == LSE_ALGO_SKINNY)) {
         rc = lse_rms_norm(x, M, K, ldx, norm_w, eps, workspace, K, stream);
         if (rc) return rc;
         return silu ? gate_up_impl(workspace, M, K, K, w_packed, scale, N_out, y, ldy, nullptr, 0, stream, false, true)

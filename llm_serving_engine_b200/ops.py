@@ -257,7 +257,8 @@ def int8_gate_up_silu_packed(x: torch.Tensor, w_packed: torch.Tensor, scale: tor
         return out
     _ensure_device(x.device)
     stream = torch.cuda.current_stream(x.device)
-    ws = linear_workspace(M, K, 2 * I, x.device) if M > GATE_UP_SILU_MAX_M else None
+    # above the decode kernel's range the fused entry always runs the tensor-core kernel
+    ws = linear_workspace(M, K, 2 * I, x.device, _lib.ALGO_TCGEN05) if M > GATE_UP_SILU_MAX_M else None
     ws_ptr, ws_bytes = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     rc = _lib.load().lse_int8_gate_up_silu_packed_dt(x2.data_ptr(), _DTYPE_CODES[x.dtype], M, K, x2.stride(0),
                                                      w_packed.data_ptr(), scale.data_ptr(), I, out.data_ptr(), I,
@@ -319,8 +320,8 @@ def rms_norm_proj(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, w_pack
     """The packed projection of `rms_norm(x, norm_weight, eps)` in one call, bf16: with
     silu=False `int8_linear_packed(rms_norm(x), w_packed, scale, N, K)` ([..., N]); with
     silu=True `int8_gate_up_silu_packed(rms_norm(x), w_packed, scale, N, K)` ([..., N], the
-    weight holding 2N interleaved gate/up rows).  Bitwise the same as those two calls; above 16
-    tokens the normalisation writes the tensor-core kernel's digit planes directly."""
+    weight holding 2N interleaved gate/up rows).  Bitwise the same as those two calls; where the
+    projection takes the tensor-core kernel the normalisation writes its digit planes directly."""
     _check_x(x, K, norm_weight, w_packed, scale)
     if x.dtype != torch.bfloat16 or norm_weight.dtype != torch.bfloat16 or norm_weight.shape != (K,) \
             or not norm_weight.is_contiguous():

@@ -83,15 +83,23 @@ def test_workspace_size_covers_counter_region():
 
 
 def test_workspace_for_follows_the_kernel_choice():
-    """No scratch where the decode kernel (packed, M <= 16) or the GEMV (row-major, M <= 2)
-    runs; the tensor-core size everywhere else, growing with M and K (digit planes)."""
+    """No scratch where the decode kernel (packed, M <= 16, or M <= 32 with N * K <= 32 MiB)
+    or the GEMV (row-major, M <= 2) runs; the tensor-core size everywhere else, growing with M
+    and K (digit planes)."""
     lib = _lib.load()
     for M in (1, 8, 16):
         assert lib.lse_int8_linear_workspace_for(M, 4096, 4096, _lib.ALGO_AUTO, 1) == 0
         assert lib.lse_int8_linear_workspace_for(M, 4096, 4096, _lib.ALGO_SKINNY, 1) == 0
+        assert lib.lse_int8_linear_workspace_for(M, 14336, 4096, _lib.ALGO_AUTO, 1) == 0
+    for M in (17, 32):  # by the weight's size
+        for K, N in ((4096, 6144), (4096, 8192), (8192, 4096)):
+            assert lib.lse_int8_linear_workspace_for(M, K, N, _lib.ALGO_AUTO, 1) == 0
+        for K, N in ((4096, 8200), (14336, 4096), (4096, 28672)):
+            need = lib.lse_int8_linear_workspace_for(M, K, N, _lib.ALGO_AUTO, 1)
+            assert need == lib.lse_int8_linear_workspace(M, K, N) > _lib.WS_COUNTER_BYTES
     for M in (1, 2):
         assert lib.lse_int8_linear_workspace_for(M, 4096, 4096, _lib.ALGO_AUTO, 0) == 0
-    for M, packed in ((17, 1), (3, 0), (64, 1), (4096, 0)):
+    for M, packed in ((33, 1), (17, 0), (3, 0), (64, 1), (4096, 0)):
         need = lib.lse_int8_linear_workspace_for(M, 4096, 4096, _lib.ALGO_AUTO, packed)
         assert need == lib.lse_int8_linear_workspace(M, 4096, 4096) > _lib.WS_COUNTER_BYTES
     assert lib.lse_int8_linear_workspace_for(4, 4096, 4096, _lib.ALGO_TCGEN05, 1) > 0

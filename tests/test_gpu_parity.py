@@ -302,6 +302,25 @@ def test_skinny_deterministic_and_linear(ws, M, K, N):
     assert torch.equal(a, b) and torch.equal(c, a * 2)
 
 
+@pytest.mark.parametrize("M", [17, 24, 32])
+@pytest.mark.parametrize("K,N,expect", [(4096, 6144, "skinny"), (4096, 4096, "skinny"), (8192, 4096, "skinny"),
+                                        (14336, 4096, "tcgen05"), (4096, 8200, "tcgen05")])
+def test_auto_choice_17_to_32_tokens(ws, M, K, N, expect):
+    """From 17 to 32 tokens the automatic choice takes the decode kernel for weights of at most
+    32 MiB (N * K) and the tensor-core kernel above: bit for bit the pinned algorithm's result,
+    within the parity criterion of the oracle either way."""
+    x, w, s = make_inputs(M, K, N, seed=M + N)
+    packed = ops.pack_weight(w.cuda())
+    xd, sd = x.cuda(), s.cuda()
+    auto = _packed_call(xd, packed, sd, N, K, ws, _lib.ALGO_AUTO)
+    pinned = _packed_call(xd, packed, sd, N, K, ws, ALGOS[expect])
+    torch.cuda.synchronize()
+    assert torch.equal(auto, pinned), f"M={M} K={K} N={N}: auto is not {expect}"
+    rows = np.unique(np.linspace(0, M - 1, 6).astype(int))
+    check_parity(auto[torch.as_tensor(rows, device="cuda")], oracle_rows(x, w, s, rows), f"auto M={M} K={K} N={N}")
+    assert ws.counters_clear() and ws.guard_intact()
+
+
 # ---- fused gate_up + SiLU * mul (decode) ------------------------------------------------
 def _silu_mul_ref(x, qg, sg, qu, su):
     g = ref_int8_linear(x, qg, sg)

@@ -1,7 +1,7 @@
 """The torch.library operators `lse::int8_linear` and `lse::gate_up_silu` (liblse_torch.so, C++
 over the C ABI) in bf16 and fp16, against the fp64 oracle on the same inputs: every kernel the
-automatic choice reaches (decode kernel M <= 16, tensor-core kernel above, both tile and
-schedule families), the fused residual add, the fused gate/up + SiLU, the int8 modules
+automatic choice reaches (decode kernel up to 16 tokens and, for weights of at most 32 MiB,
+up to 32; tensor-core kernel above, both tile and schedule families), the fused residual add, the fused gate/up + SiLU, the int8 modules
 dispatching to them natively in fp16, and the host-side refusals before any launch.
 """
 
@@ -29,7 +29,7 @@ def _case(M, K, N, dtype, seed):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("M", [1, 5, 16, 17, 64, 300])
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 32, 64, 300])
 def test_int8_linear_op(M, dtype):
     K, N = 2048, 3072
     x, w, s, xd, wp, sd = _case(M, K, N, dtype, seed=M)
