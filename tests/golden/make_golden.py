@@ -20,7 +20,7 @@ ref_tiny_llama_int8.npz
     2 layers, 4 heads, 2 KV heads, seed 0).
 
 config1.npz
-    BASELINE config 1 (x bf16 [8, 2048] ~ N(0,1), W int8 [2048, 2048] uniform [-127, 127],
+    Config 1, the CPU case (x bf16 [8, 2048] ~ N(0,1), W int8 [2048, 2048] uniform [-127, 127],
     s uniform [1e-4, 5e-4], seed 0): SHA-256 of the seeded inputs, the oracle output, and the
     output of the reference's CPU nn.Linear (float32 `F.linear` on the dequantized weight) on
     the same inputs.

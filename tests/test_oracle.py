@@ -66,8 +66,9 @@ def test_fused_qkv_split_matches_separate_projections(tiny, layer):
 
 
 def test_config1_inputs_and_outputs_reproduce(golden_dir):
-    """the seeded generator gives the recorded bits, the oracle gives the
-    recorded output, and it agrees with the reference's CPU nn.Linear."""
+    """Config 1, the CPU case (M=8, K=2048, N=2048): the seeded generator gives the recorded
+    bits, the oracle gives the recorded output, and it agrees with the reference's CPU
+    nn.Linear."""
     g = np.load(os.path.join(golden_dir, "config1.npz"))
     x, w, s = make_inputs(8, 2048, 2048, seed=0)
     sha = lambda t: hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()  # noqa: E731
