@@ -475,9 +475,10 @@ def engine_decode(dev, hbm_peak: float, steps: int = 20, warmup: int = 5, batch:
     `bf16_lse` (bf16 projections with every binding that applies to them: `attend_paged` on
     this package's attention kernel, the RMSNorm kernel in the norm slots), `int8` (the
     `quantize="int8"` switch through `engine_hook.install()` with its defaults: int8
-    projections, the same attention and norms, and `write_kv_and_project_q` on the fused int8
-    QKV output with the RoPE + K/V write kernel) and `int8_no_rope` (the switch without that
-    last binding: against `bf16_lse` it differs in the projections alone); and in fp16, the
+    projections, the same attention and norms, `write_kv_and_project_q` on the fused int8
+    QKV output with the RoPE + K/V write kernel, and the residual adds in the o_proj and down
+    epilogues) and `int8_no_rope` (the switch without those last two bindings: against
+    `bf16_lse` it differs in the projections alone); and in fp16, the
     reference's default dtype, `fp16_reference` (the stock engine) and `fp16_int8` (the switch
     with its defaults).  The weights are a random-init Llama-3-8B (seeded, built on the
     GPU in place of `from_pretrained`: no checkpoint exists here); everything after the load is
@@ -526,7 +527,7 @@ def engine_decode(dev, hbm_peak: float, steps: int = 20, warmup: int = 5, batch:
         for arm in ("bf16_reference", "bf16_lse", "int8_no_rope", "int8", "fp16_reference", "fp16_int8"):
             quantize = "int8" if "int8" in arm else "none"
             if quantize == "int8":
-                engine_hook.install(rope=arm != "int8_no_rope")
+                engine_hook.install(rope=arm != "int8_no_rope", residuals=arm != "int8_no_rope")
             try:
                 runner = mr.ModelRunner(ModelConfig(model_name_or_path="synthetic-llama-3-8b", device=str(dev),
                                                     dtype="float16" if arm.startswith("fp16") else "bfloat16",

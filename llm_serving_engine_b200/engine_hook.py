@@ -15,7 +15,10 @@ After the swap nothing else in the engine changes: `forward`, `forward_fused`,
 (`ModelRunner.attend_paged`, `model_runner.py:357-363`, reached from `paged_attention` in the
 eager and decode-graph paths and from the piecewise runner between its segments) is bound to
 this package's kernel on the same arguments (`ops.paged_attention`, the drop-in for the
-reference's Triton `paged_attention_forward`).  int8 needs CUDA; on a CPU-only
+reference's Triton `paged_attention_forward`).  `decoder_hidden` and `attention_output`
+(eager and decode-graph paths) are bound to forms that add each layer's residual in the int8
+o_proj and down epilogues (same layer order; the sum is rounded once instead of twice).
+int8 needs CUDA; on a CPU-only
 machine the switch raises `RuntimeError` at load, the way the reference's custom-kernel
 check refuses a CPU device (`model_runner.py:77-94`); there is no CPU fallback.
 """
@@ -28,10 +31,10 @@ import functools
 import torch
 
 from . import ops
-from .int8_linear import quantize_llama_
+from .int8_linear import Int8Linear, Int8LlamaMLP, quantize_llama_
 
-__all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "bind_rms_norms", "install", "uninstall",
-           "installed"]
+__all__ = ["enable_int8", "bind_paged_attention", "bind_rope_kv_write", "bind_rms_norms", "bind_residual_epilogues",
+           "install", "uninstall", "installed"]
 
 
 def _attend_paged(runner, q, layer_idx, paging):
@@ -110,6 +113,59 @@ def bind_rms_norms(runner):
     return runner
 
 
+def _attention_output(runner, original, attn, layer_idx):
+    """`ModelRunner.attention_output` (`model_runner.py:365-369`) with the layer's residual added
+    in the int8 o_proj's epilogue when the bound `decoder_hidden` left it for this layer;
+    otherwise (the piecewise runner between its segments, a float o_proj, a foreign shape) the
+    reference's own code."""
+    pending = runner._lse_residual
+    o_proj = runner._layers[layer_idx].self_attn.o_proj
+    T = attn.shape[1]
+    if (pending is None or pending[0] != layer_idx or not isinstance(o_proj, Int8Linear)
+            or pending[1].shape != (1, T, o_proj.out_features) or pending[1].dtype != attn.dtype):
+        return original(attn, layer_idx)
+    runner._lse_residual = None
+    out = attn.transpose(0, 1).reshape(1, T, runner.n_heads * runner.head_dim)
+    return o_proj(out, residual=pending[1])
+
+
+def _decoder_hidden(runner, original, input_ids, position_ids, attend):
+    """`ModelRunner.decoder_hidden` (`model_runner.py:213-224`) with each layer's two residual
+    adds in the epilogues of its int8 projections: `hidden + o_proj(attn)` and
+    `hidden + mlp(normed)` each come out of the projection kernel rounded once, instead of a
+    projection output plus an elementwise add (two launches fewer per layer).  o_proj runs
+    inside `attend` (`attention_output`), so the residual is left for it there; when `attend`
+    does not take it (`contiguous_attention` calls o_proj itself) or a slot is not int8, the add
+    runs as the reference writes it."""
+    model = runner.model
+    hidden = model.get_input_embeddings()(input_ids)
+    position_embeddings = model.model.rotary_emb(hidden, position_ids)
+    for layer_idx, layer in enumerate(runner._layers):
+        runner._lse_residual = (layer_idx, hidden)
+        try:
+            out = attend(layer.input_layernorm(hidden), position_embeddings, layer_idx)
+            taken = runner._lse_residual is None
+        finally:
+            runner._lse_residual = None
+        hidden = out if taken else hidden + out
+        normed = layer.post_attention_layernorm(hidden)
+        hidden = layer.mlp(normed, residual=hidden) if isinstance(layer.mlp, Int8LlamaMLP) else hidden + layer.mlp(normed)
+    return model.model.norm(hidden)
+
+
+def bind_residual_epilogues(runner):
+    """Route the runner's `decoder_hidden` (the eager and decode-graph paths) and
+    `attention_output` through the fused residual epilogues (instance attributes, as
+    `bind_paged_attention`).  Idempotent."""
+    if getattr(runner, "_lse_residual_bound", False):
+        return runner
+    runner._lse_residual = None
+    runner.attention_output = functools.partial(_attention_output, runner, runner.attention_output)
+    runner.decoder_hidden = functools.partial(_decoder_hidden, runner, runner.decoder_hidden)
+    runner._lse_residual_bound = True
+    return runner
+
+
 def bind_paged_attention(runner):
     """Route the runner's paged attention to `ops.paged_attention` (an instance attribute, so
     the runner's own `paged_attention` and the graph runners call it)."""
@@ -117,13 +173,15 @@ def bind_paged_attention(runner):
     return runner
 
 
-def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: bool = True, norms: bool = True):
+def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: bool = True, norms: bool = True,
+                residuals: bool = True):
     """Swap a loaded `ModelRunner`'s projections to int8 in place.  `runner.model` is the
     Llama-family model the runner loaded; every decoder layer's q/k/v (one fused int8 QKV),
     o_proj and MLP become int8 (`quantize_llama_`), and the lm_head too with `lm_head=True`;
     with `attention=True` the paged attention runs on this package's kernel too, and with
     `rope=True` the K/V write and q (`write_kv_and_project_q`) on the fused QKV projection and
-    the RoPE + K/V write kernel, and with `norms=True` the RMSNorms on the RMSNorm kernel.
+    the RoPE + K/V write kernel, with `norms=True` the RMSNorms on the RMSNorm kernel, and with
+    `residuals=True` the decoder's residual adds in the o_proj and down epilogues.
     Nothing else needs preparing: the ops hold no per-stream
     state, so the engine's graph captures on any stream record them as they are."""
     device = torch.device(runner.device)
@@ -136,6 +194,8 @@ def enable_int8(runner, lm_head: bool = False, attention: bool = True, rope: boo
         bind_rope_kv_write(runner)
     if norms:
         bind_rms_norms(runner)
+    if residuals:
+        bind_residual_epilogues(runner)
     return runner
 
 
@@ -156,7 +216,7 @@ def installed() -> bool:
     return getattr(_runner_class().__init__, "_lse_int8", False)
 
 
-def install(lm_head: bool = False, rope: bool = True, norms: bool = True) -> None:
+def install(lm_head: bool = False, rope: bool = True, norms: bool = True, residuals: bool = True) -> None:
     """Make `ModelRunner(ModelConfig(quantize="int8"))` load an int8 model (idempotent; the
     options of the first call stay until `uninstall`)."""
     cls = _runner_class()
@@ -171,7 +231,7 @@ def install(lm_head: bool = False, rope: bool = True, norms: bool = True) -> Non
         _check_cuda(config)
         original(self, dataclasses.replace(config, quantize="none"), *args, **kwargs)
         self.config = config
-        enable_int8(self, lm_head=lm_head, rope=rope, norms=norms)
+        enable_int8(self, lm_head=lm_head, rope=rope, norms=norms, residuals=residuals)
 
     __init__._lse_int8 = True
     __init__._lse_original = original

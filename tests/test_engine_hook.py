@@ -93,3 +93,71 @@ def test_norm_binding_wraps_every_norm_once_and_defers_on_cpu(tiny_dir):
     assert type(runner.model.model.norm).__name__ == "_KernelRMSNorm"
     assert all(type(lay.post_attention_layernorm).__name__ == "_KernelRMSNorm" for lay in runner.model.model.layers)
     assert torch.equal(layer.input_layernorm(x), before)
+
+
+def test_residual_binding_matches_the_reference_loop(tiny_dir, monkeypatch):
+    """`bind_residual_epilogues` runs the reference's layer loop with each residual handed to the
+    o_proj (through `attention_output`) and the MLP.  On the CPU, with stand-ins for the int8
+    modules whose epilogue computes `residual + module(x)` in the reference's order, the hidden
+    state is bit for bit the reference's `decoder_hidden`, and every layer hands both residuals
+    over; an `attend` that calls o_proj itself (as `contiguous_attention` does) gets the
+    reference's add; the piecewise runner's direct `attention_output` calls defer."""
+    import torch
+
+    runner = ModelRunner(ModelConfig(model_name_or_path=tiny_dir, device="cpu", dtype="float32",
+                                     use_custom_kernels=False))
+    calls = []
+
+    class FakeLinear(torch.nn.Module):
+        def __init__(self, inner):
+            super().__init__()
+            self.inner, self.out_features = inner, inner.out_features
+
+        def forward(self, x, residual=None):
+            calls.append(("o_proj", residual is not None))
+            return self.inner(x) if residual is None else residual + self.inner(x)
+
+    class FakeMLP(torch.nn.Module):
+        def __init__(self, inner):
+            super().__init__()
+            self.inner = inner
+
+        def forward(self, x, residual=None):
+            calls.append(("mlp", residual is not None))
+            return self.inner(x) if residual is None else residual + self.inner(x)
+
+    monkeypatch.setattr(engine_hook, "Int8Linear", FakeLinear)
+    monkeypatch.setattr(engine_hook, "Int8LlamaMLP", FakeMLP)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(1, 120, (1, 6), generator=g)
+    pos = torch.arange(6).unsqueeze(0)
+    nh, hd = runner.n_heads, runner.head_dim
+
+    def heads(normed):  # any (1, T, H) -> (heads, T, head_dim) stand-in for attention
+        return normed[0].view(normed.shape[1], nh, hd).transpose(0, 1)
+
+    def via_output(normed, pe, i):
+        return runner.attention_output(heads(normed), i)
+
+    def direct(normed, pe, i):
+        return runner._layers[i].self_attn.o_proj(heads(normed).transpose(0, 1).reshape(1, -1, nh * hd))
+
+    with torch.no_grad():
+        ref_a = runner.decoder_hidden(ids, pos, via_output)
+        ref_b = runner.decoder_hidden(ids, pos, direct)
+        for layer in runner._layers:
+            layer.self_attn.o_proj = FakeLinear(layer.self_attn.o_proj)
+            layer.mlp = FakeMLP(layer.mlp)
+        engine_hook.bind_residual_epilogues(runner)
+        engine_hook.bind_residual_epilogues(runner)  # idempotent
+        calls.clear()
+        assert torch.equal(runner.decoder_hidden(ids, pos, via_output), ref_a)
+        n = len(runner._layers)
+        assert calls == [("o_proj", True), ("mlp", True)] * n
+        calls.clear()
+        assert torch.equal(runner.decoder_hidden(ids, pos, direct), ref_b)
+        assert calls == [("o_proj", False), ("mlp", True)] * n
+        assert runner._lse_residual is None
+        calls.clear()
+        runner.attention_output(heads(torch.randn(1, 6, nh * hd, generator=g)), 0)
+        assert calls == [("o_proj", False)]

@@ -16,7 +16,9 @@ These run the reference's own code paths, unmodified, from its install in baseli
   (`tests/test_piecewise_graph.py:47-58`), on the decode kernel and both token tiles of the
   tensor-core kernel;
 * `bytes_beyond_kv_pool` (`model_runner.py:131-159`), the engine's memory probe, including
-  its eager dummy iteration at 4160 tokens.
+  its eager dummy iteration at 4160 tokens;
+* `decoder_hidden` (`model_runner.py:213-224`) with the residual adds in the o_proj and down
+  epilogues, against the reference's own loop on the same int8 weights.
 
 A failed `_self_check` makes the reference drop its graphs silently and run eagerly; the
 assertions on the graph dicts and the refusal of `forward_fused` during replay make such a
@@ -133,6 +135,45 @@ def test_forward_fused_matches_dequantized_twin(tiny_dir, prompt_lens, dtype):
         advance(alloc_b, seqs_b, out_b)
         plan_a, plan_b = decode_plan(seqs_a), decode_plan(seqs_b)
     assert decisive >= 2 * len(prompt_lens), f"only {decisive} decisive rows"
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_residual_adds_run_in_the_projection_epilogues(tiny_dir, dtype):
+    """With the switch's defaults every layer's o_proj and MLP receive the layer's residual (the
+    adds run in their kernels' epilogues) in prefill and decode; the logits agree with the
+    reference's own layer loop on the same int8 weights (the bound methods removed) within the
+    one rounding per add that the fused form saves, and the greedy tokens are the same
+    wherever that loop's top-two margin exceeds four times the largest logit difference."""
+    runner = _int8_runner(tiny_dir, dtype)
+    plain = _int8_runner(tiny_dir, dtype)
+    del plain.decoder_hidden, plain.attention_output  # back to the class's methods
+    seen = []
+    for layer in runner._layers:
+        for mod in (layer.self_attn.o_proj, layer.mlp):
+            inner = mod.forward
+            mod.forward = (lambda f: lambda x, residual=None: seen.append(residual is not None) or f(x, residual))(inner)
+    alloc_a, alloc_b = BlockAllocator(NUM_BLOCKS, BLOCK_SIZE), BlockAllocator(NUM_BLOCKS, BLOCK_SIZE)
+    prompts = [[(5 * i + 2 * j) % 120 + 1 for j in range(n)] for i, n in enumerate((4, 21))]
+    seqs_a = [greedy_sequence(400 + i, p) for i, p in enumerate(prompts)]
+    seqs_b = [greedy_sequence(400 + i, p) for i, p in enumerate(prompts)]
+    for sa, sb in zip(seqs_a, seqs_b, strict=True):
+        assert alloc_a.allocate(sa, sa.num_tokens) and alloc_b.allocate(sb, sb.num_tokens)
+    plan_a = BatchPlan(entries=[prefill_entry(s, s.num_tokens) for s in seqs_a])
+    plan_b = BatchPlan(entries=[prefill_entry(s, s.num_tokens) for s in seqs_b])
+    for step in range(3):
+        seen.clear()
+        out_a, logits_a = forward_fused_with_logits(runner, plan_a, {s.seq_id: s for s in seqs_a})
+        out_b, logits_b = forward_fused_with_logits(plain, plan_b, {s.seq_id: s for s in seqs_b})
+        assert seen == [True] * (2 * len(runner._layers)), f"step {step}: residuals not handed over: {seen}"
+        diff = (logits_a - logits_b).abs()
+        assert diff.max().item() <= 1e-2 * logits_b.abs().max().item(), f"step {step}"
+        top2 = logits_b.topk(2, dim=-1).values
+        for row, ((_, tok_a, _), (_, tok_b, _)) in enumerate(zip(out_a, out_b, strict=True)):
+            if (top2[row, 0] - top2[row, 1]).item() > 4 * diff[row].max().item():
+                assert tok_a == tok_b
+        advance(alloc_a, seqs_a, out_b)
+        advance(alloc_b, seqs_b, out_b)
+        plan_a, plan_b = decode_plan(seqs_a), decode_plan(seqs_b)
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
