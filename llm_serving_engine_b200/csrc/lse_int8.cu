@@ -237,9 +237,17 @@ TcPlan plan_tc(int64_t M, int64_t K, int64_t N, int num_sms, int dev) {
     // Prefill-sized tiles (tensor-bound), more than half a wave but less than a whole one: every
     // tile whole on its own CTA, the remaining SMs idle.  Measured on B200 (Llama-3-8B shapes at
     // M = 512, 128 tiles): O 33.3 -> 27.0 us and down 72.9 -> 56.3 us against stream-K over all
-    // SMs, whose every tile then has two segments and a partial-sum reduction.  Decode-sized
-    // tiles (HBM-bound) keep every SM streaming.
-    if (t.tiles % G == 0 || (t.nt == 128 && t.tiles > G / 2 && t.tiles < G)) t.dp_tiles = t.tiles;
+    // SMs, whose every tile then has two segments and a partial-sum reduction.
+    // Decode-sized tiles (64 tokens) over more than one wave whose last wave is at least half
+    // full: whole tiles too, dealt round-robin (the first tiles % G CTAs take one more).
+    // Measured on B200 (us per launch, 32 or 16 weights per CUDA graph, stream-K -> whole):
+    // Llama-3-8B gate_up (224 tiles) at M = 64 35.2 -> 31.6, with SiLU * mul 38.7 -> 33.5, at
+    // M = 48 33.6 -> 31.1, at M = 33 32.2 -> 30.6; the Llama-3 lm_head shape (N = 128256, 1002
+    // tiles) at M = 64 118.8 -> 114.3.  With a nearly empty last wave stream-K stays ahead
+    // (Llama-3-70B gate_up, 448 tiles: 105.1 against 110.3 at M = 64), and so does a single
+    // partial wave (70B QKV, 80 tiles: 26.1 against 27.4 at M = 32).
+    const bool dp_decode = t.nt == 64 && t.tiles > G && 2 * (t.tiles % G) >= G;
+    if (dp_decode || t.tiles % G == 0 || (t.nt == 128 && t.tiles > G / 2 && t.tiles < G)) t.dp_tiles = t.tiles;
     else if (t.tiles < G) t.dp_tiles = 0;
     else {
         static const int sk_waves = tuning_knob("LSE_TC_SK_WAVES", 2);  // waves left to stream-K: 1 or 2

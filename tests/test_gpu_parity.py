@@ -321,6 +321,28 @@ def test_auto_choice_17_to_32_tokens(ws, M, K, N, expect):
     assert ws.counters_clear() and ws.guard_intact()
 
 
+@pytest.mark.parametrize("M,K,N", [(64, 4096, 28672), (40, 1040, 33240), (33, 2048, 30720)])
+def test_whole_tiles_over_one_and_a_half_waves(ws, M, K, N):
+    """64-token tiles over more than one wave with the last wave at least half full run whole
+    tiles round-robin (224, 260 and 240 tiles: some CTAs take two, ragged N and K included):
+    parity with the oracle on sampled rows and columns, deterministic, linear in x, and no
+    stream-K counter left set."""
+    x, w, s = make_inputs(M, K, N, seed=N + M)
+    packed = ops.pack_weight(w.cuda())
+    xd, sd = x.cuda(), s.cuda()
+    a = _packed_call(xd, packed, sd, N, K, ws, _lib.ALGO_TCGEN05)
+    b = _packed_call(xd, packed, sd, N, K, ws, _lib.ALGO_TCGEN05)
+    c = _packed_call(xd * 2, packed, sd, N, K, ws, _lib.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and torch.equal(c, a * 2)
+    rows = np.unique(np.linspace(0, M - 1, 5).astype(int))
+    cols = np.unique(np.concatenate([np.arange(0, N, 97), [N - 1]]))
+    ref = oracle_rows(x, w[cols], s[cols], rows)
+    got = a[torch.as_tensor(rows, device="cuda")][:, torch.as_tensor(cols, device="cuda")]
+    check_parity(got, ref, f"whole tiles M={M} K={K} N={N}")
+    assert ws.counters_clear() and ws.guard_intact()
+
+
 # ---- fused gate_up + SiLU * mul (decode) ------------------------------------------------
 def _silu_mul_ref(x, qg, sg, qu, su):
     g = ref_int8_linear(x, qg, sg)
