@@ -44,7 +44,8 @@ typedef enum lse_status {
 typedef enum lse_algo {
     LSE_ALGO_AUTO = 0,     /* pick by M and weight layout (see lse_int8_linear_packed) */
     LSE_ALGO_GEMV = 1,     /* row-major W only: CUDA-core GEMV, 128-bit int8 streams, warp-shuffle reduction */
-    LSE_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM tensor-core GEMM fed by TMA (whole tiles, stream-K or a cluster K split) */
+    LSE_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM tensor-core GEMM fed by TMA (whole tiles, stream-K
+                              or a cluster split of K, by shape) */
     LSE_ALGO_SKINNY = 3    /* packed W only, M <= 32: warp-MMA skinny GEMM for decode, weights
                               streamed straight into registers (fp16 MMA for M <= 8 with bf16->fp16
                               activations, bf16 MMA above), K split reduced across warps with the
