@@ -42,7 +42,7 @@ typedef enum lse_status {
 
 /* Kernel selection for lse_int8_linear_ex. */
 typedef enum lse_algo {
-    LSE_ALGO_AUTO = 0,     /* pick by M and weight layout (see lse_int8_linear_packed) */
+    LSE_ALGO_AUTO = 0,     /* pick by M, weight layout and weight size (see lse_int8_linear_packed) */
     LSE_ALGO_GEMV = 1,     /* row-major W only: CUDA-core GEMV, 128-bit int8 streams, warp-shuffle reduction */
     LSE_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM tensor-core GEMM fed by TMA (whole tiles, stream-K
                               or a cluster split of K, by shape) */
